@@ -1,0 +1,207 @@
+"""Host-side mirror of the reference's device seam, over the C ABI.
+
+The reference (Go) defines the seam in ann/backend.go:16-55:
+
+    type Backend interface { NewI8Index(bq []int8, scales []float32, n, dim int) (I8Index, error); Name() string }
+    type I8Index interface { Score(q, dst []float32) error; Close() error }
+    type I8BatchIndex interface { ScoreBatch(queries [][]float32, dst []float32) error }
+    type I8TopKIndex interface { TopKBatch(queries [][]float32, k int) ([][]Hit, error) }
+
+and gpu/anncuda/backend.go implements it with CUDA. ``B200Backend`` and
+``I8Index`` below keep those names, argument meanings and error behaviour (a
+Go ``error`` becomes a raised ``Fi8Error``; a decline is ``DeclinedError``) so
+the parity tests read like the reference's own. Every call goes to
+libfi8_b200.so; nothing here computes a score.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+
+from ._ffi import Fi8Error, check, lib
+
+
+@dataclass(frozen=True)
+class Hit:
+    """ann.Hit (ann/flat.go:51-54): corpus index and float64-widened score."""
+
+    Index: int
+    Score: float
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    check(lib().fi8_device_count(C.byref(n)))
+    return n.value
+
+
+class Context:
+    """One CUDA device (fi8_ctx)."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        check(lib().fi8_ctx_create(device, C.byref(h)))
+        self._h = h
+        self.device = device
+
+    @property
+    def handle(self):
+        return self._h
+
+    def sm_count(self) -> int:
+        n = C.c_int(0)
+        check(lib().fi8_ctx_sm_count(self._h, C.byref(n)))
+        return n.value
+
+    def merge_keys_async(self, d_in: int, nsrc: int, M: int, k: int, d_out: int, stream: int = 0) -> None:
+        """Top k per query of nsrc device key lists [nsrc][M][k] -> [M][k]."""
+        check(lib().fi8_merge_keys_async(self._h, C.c_void_p(d_in), nsrc, M, k, C.c_void_p(d_out),
+                                         C.c_void_p(stream or None)))
+
+    def close(self) -> None:
+        if self._h:
+            lib().fi8_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class B200Backend:
+    """ann.Backend on one B200 (the role of cudaBackend, gpu/anncuda/backend.go:38)."""
+
+    def __init__(self, device: int = 0):
+        self.ctx = Context(device)
+
+    def Name(self) -> str:
+        return "cuda-b200"
+
+    def NewI8Index(self, bq, scales, n: int, dim: int, id_base: int = 0) -> "I8Index":
+        """gpu/anncuda/backend.go:124-154: copies codes and scales to the device."""
+        bq = np.ascontiguousarray(bq, dtype=np.int8).reshape(-1)
+        scales = _f32(scales).reshape(-1)
+        if n <= 0 or dim <= 0:
+            raise Fi8Error(1, f"gpu: empty int8 index (n={n} dim={dim})")
+        if bq.shape[0] != n * dim or scales.shape[0] != n:
+            raise Fi8Error(1, f"gpu: int8 index shape mismatch (bq {bq.shape[0]}, scales "
+                              f"{scales.shape[0]}, n={n} dim={dim})")
+        return I8Index(self.ctx, bq, scales, n, dim, id_base)
+
+
+class I8Index:
+    """A device-resident FlatI8 shard: I8Index + I8BatchIndex + I8TopKIndex."""
+
+    def __init__(self, ctx: Context, bq: np.ndarray, scales: np.ndarray, n: int, dim: int, id_base: int = 0):
+        h = C.c_void_p()
+        check(lib().fi8_index_create(ctx.handle, _p(bq), _p(scales), n, dim, id_base, C.byref(h)))
+        self._h = h
+        self.ctx = ctx
+        self.n = n
+        self.dim = dim
+        self.id_base = id_base
+
+    # -- I8Index ---------------------------------------------------------
+    def Score(self, q: Sequence[float], dst: np.ndarray) -> None:
+        """Fills dst[j] with the W8A8 score of q against row j."""
+        q = _f32(q)
+        if q.shape[0] != self.dim:
+            raise Fi8Error(1, f"gpu: query dim {q.shape[0]} != index dim {self.dim}")
+        if dst.shape[0] != self.n or dst.dtype != np.float32 or not dst.flags.c_contiguous:
+            raise Fi8Error(1, f"gpu: dst len {dst.shape[0]} != index n {self.n}")
+        check(lib().fi8_score(self._h, _p(q), _p(dst)))
+
+    def Close(self) -> None:
+        if self._h:
+            check(lib().fi8_index_destroy(self._h))
+            self._h = None
+
+    # -- I8BatchIndex ----------------------------------------------------
+    def ScoreBatch(self, queries, dst: np.ndarray) -> None:
+        Q = self._queries(queries)
+        M = Q.shape[0]
+        if dst.shape[0] != M * self.n or dst.dtype != np.float32 or not dst.flags.c_contiguous:
+            raise Fi8Error(1, f"gpu: batch dst len {dst.shape[0]} != M*N {M * self.n}")
+        if M == 0:
+            return
+        check(lib().fi8_score_batch(self._h, _p(Q), M, _p(dst)))
+
+    # -- I8TopKIndex -----------------------------------------------------
+    def TopKBatch(self, queries, k: int) -> list[list[Hit]]:
+        idx, sc = self.topk_arrays(queries, k)
+        out = []
+        for m in range(idx.shape[0]):
+            row = []
+            for j in range(idx.shape[1]):
+                i = int(idx[m, j])
+                if i < 0:
+                    break
+                row.append(Hit(i, float(sc[m, j])))
+            out.append(row)
+        return out
+
+    def topk_arrays(self, queries, k: int):
+        """TopKBatch as arrays: (int32 [M,k], float32 [M,k]), index -1 = empty."""
+        Q = self._queries(queries)
+        M = Q.shape[0]
+        idx = np.empty((M, max(k, 0)), np.int32)
+        sc = np.empty((M, max(k, 0)), np.float32)
+        if M == 0:
+            return idx, sc
+        check(lib().fi8_topk_batch(self._h, _p(Q), M, k, _p(idx), _p(sc)))
+        return idx, sc
+
+    def max_k(self) -> int:
+        v = C.c_int32(0)
+        check(lib().fi8_topk_max_k(self._h, C.byref(v)))
+        return v.value
+
+    # -- device-resident forms ------------------------------------------
+    def topk_async(self, d_q: int, M: int, k: int, d_keys: int, stream: int = 0) -> None:
+        check(lib().fi8_topk_batch_async(self._h, C.c_void_p(d_q), M, k, C.c_void_p(d_keys),
+                                         C.c_void_p(stream or None)))
+
+    def sync(self) -> None:
+        check(lib().fi8_index_sync(self._h))
+
+    def _queries(self, queries) -> np.ndarray:
+        if isinstance(queries, np.ndarray) and queries.ndim == 2:
+            Q = _f32(queries)
+            if Q.shape[1] != self.dim:
+                raise Fi8Error(1, f"gpu: batch query dim {Q.shape[1]} != index dim {self.dim}")
+            return Q
+        rows = list(queries)
+        for m, q in enumerate(rows):
+            if len(q) != self.dim:
+                raise Fi8Error(1, f"gpu: batch query {m} dim {len(q)} != index dim {self.dim}")
+        if not rows:
+            return np.empty((0, self.dim), np.float32)
+        return _f32(np.stack([_f32(q) for q in rows]))
+
+    def __del__(self):
+        try:
+            self.Close()
+        except Exception:
+            pass
+
+
+def unpack_keys(keys: np.ndarray):
+    """Decode packed top-K keys (fi8_keys_unpack): (int32 idx, float32 score)."""
+    keys = np.ascontiguousarray(keys, dtype=np.uint64)
+    idx = np.empty(keys.shape, np.int32)
+    sc = np.empty(keys.shape, np.float32)
+    check(lib().fi8_keys_unpack(_p(keys), keys.size, _p(idx), _p(sc)))
+    return idx, sc

@@ -1,0 +1,490 @@
+// fi8_api.cu -- the C ABI (include/fi8.h): device contexts, device-resident
+// FlatI8 shards, and the Score / ScoreBatch / TopKBatch entry points that the
+// reference's ann.Backend seam calls (ann/backend.go:16-55).
+//
+// Error behaviour follows gpu/anncuda/backend.go: shape errors and device
+// failures are returned, never panicked; TopKBatch declines k <= 0 and k >= n
+// (backend.go:577). Unlike the reference it does not decline small n (its
+// topkMinN = 50_000, backend.go:305, is a launch-cost crossover of a two-kernel
+// design; here scoring and selection are one launch).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "../../include/fi8.h"
+#include "fi8_device.cuh"
+#include "fi8_scan.cuh"
+
+using namespace fi8;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  const int code = (e == cudaErrorMemoryAllocation) ? FI8_ERR_OOM : FI8_ERR_CUDA;
+  return fail(code, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define FI8_CUDA(call, what)                      \
+  do {                                            \
+    cudaError_t e_ = (call);                      \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <typename T>
+int ensure_device(T** p, size_t* cap, size_t need, const char* what) {
+  if (*cap >= need && *p) return FI8_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  const size_t n = std::max<size_t>(need, 1);
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T));
+  if (e != cudaSuccess) {
+    *p = nullptr;
+    return cuda_fail(e, what);
+  }
+  *cap = n;
+  return FI8_OK;
+}
+
+template <typename T>
+int ensure_host(T** p, size_t* cap, size_t need, const char* what) {
+  if (*cap >= need && *p) return FI8_OK;
+  if (*p) cudaFreeHost(*p);
+  *p = nullptr;
+  *cap = 0;
+  const size_t n = std::max<size_t>(need, 1);
+  cudaError_t e = cudaMallocHost(reinterpret_cast<void**>(p), n * sizeof(T));
+  if (e != cudaSuccess) {
+    *p = nullptr;
+    return cuda_fail(e, what);
+  }
+  *cap = n;
+  return FI8_OK;
+}
+
+// Queries handled per scan launch in the multi-query (one pass per query)
+// form; bounds the per-launch scratch.
+constexpr int32_t kScanMaxM = 64;
+constexpr int64_t kRowAlign = 256;  // n is padded to a multiple of this
+
+}  // namespace
+
+struct fi8_ctx {
+  int device = 0;
+  int sm_count = 0;
+};
+
+struct fi8_index {
+  fi8_ctx* ctx = nullptr;
+  int device = 0;
+  int sm_count = 0;
+  int64_t n = 0, n_alloc = 0;
+  int32_t dim = 0, dpad = 0;
+  uint32_t id_base = 0;
+  int8_t* d_codes = nullptr;
+  float* d_scales = nullptr;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+
+  // top-K scan scratch, sized for (scr_M queries, scr_k, scr_G CTAs)
+  unsigned long long* d_gthr = nullptr;
+  size_t gthr_cap = 0;
+  unsigned int* d_counter = nullptr;
+  size_t counter_cap = 0;
+  uint64_t* d_part = nullptr;
+  size_t part_cap = 0;
+  int32_t* d_part_counts = nullptr;
+  size_t part_counts_cap = 0;
+  unsigned int* d_err = nullptr;
+  unsigned int* h_err = nullptr;
+
+  // staging for the host-pointer entry points
+  float* d_q = nullptr;
+  size_t d_q_cap = 0;
+  uint64_t* d_keys = nullptr;
+  size_t d_keys_cap = 0;
+  float* d_scores = nullptr;
+  size_t d_scores_cap = 0;
+  uint64_t* h_keys = nullptr;
+  size_t h_keys_cap = 0;
+};
+
+extern "C" {
+
+const char* fi8_last_error(void) { return g_last_error.c_str(); }
+
+int fi8_device_count(int* out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_device_count: null out");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *out = 0;
+    return cuda_fail(e, "cudaGetDeviceCount");
+  }
+  *out = n;
+  return FI8_OK;
+}
+
+int fi8_ctx_create(int device, fi8_ctx** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_ctx_create: null out");
+  *out = nullptr;
+  int ndev = 0;
+  FI8_CUDA(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) return fail(FI8_ERR_ARG, "fi8_ctx_create: device %d of %d", device, ndev);
+  DeviceGuard g(device);
+  cudaDeviceProp prop;
+  FI8_CUDA(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10) return fail(FI8_ERR_DECLINED, "fi8: device %d is sm_%d%d, this build targets sm_100a", device, prop.major, prop.minor);
+  fi8_ctx* c = new (std::nothrow) fi8_ctx;
+  if (!c) return fail(FI8_ERR_OOM, "fi8_ctx_create: host allocation");
+  c->device = device;
+  c->sm_count = prop.multiProcessorCount;
+  *out = c;
+  return FI8_OK;
+}
+
+int fi8_ctx_destroy(fi8_ctx* ctx) {
+  delete ctx;
+  return FI8_OK;
+}
+
+int fi8_ctx_sm_count(fi8_ctx* ctx, int* out) {
+  if (!ctx || !out) return fail(FI8_ERR_ARG, "fi8_ctx_sm_count: null argument");
+  *out = ctx->sm_count;
+  return FI8_OK;
+}
+
+static void index_free(fi8_index* x) {
+  DeviceGuard g(x->device);
+  if (x->stream) cudaStreamSynchronize(x->stream);
+  cudaFree(x->d_codes);
+  cudaFree(x->d_scales);
+  cudaFree(x->d_gthr);
+  cudaFree(x->d_counter);
+  cudaFree(x->d_part);
+  cudaFree(x->d_part_counts);
+  cudaFree(x->d_err);
+  cudaFree(x->d_q);
+  cudaFree(x->d_keys);
+  cudaFree(x->d_scores);
+  if (x->h_keys) cudaFreeHost(x->h_keys);
+  if (x->h_err) cudaFreeHost(x->h_err);
+  if (x->stream) cudaStreamDestroy(x->stream);
+  delete x;
+}
+
+int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int64_t n, int32_t dim,
+                     int64_t id_base, fi8_index** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_index_create: null out");
+  *out = nullptr;
+  if (!ctx) return fail(FI8_ERR_ARG, "fi8_index_create: null ctx");
+  if (n <= 0 || dim <= 0)  // gpu/anncuda/backend.go:125-127
+    return fail(FI8_ERR_ARG, "gpu: empty int8 index (n=%lld dim=%d)", (long long)n, dim);
+  if (!codes || !scales) return fail(FI8_ERR_ARG, "fi8_index_create: null codes/scales");
+  if (id_base < 0 || id_base + n > 0x7FFFFFFFll)
+    return fail(FI8_ERR_ARG, "fi8_index_create: global indices must fit in 31 bits (id_base=%lld n=%lld)",
+                (long long)id_base, (long long)n);
+  const int32_t dpad = (dim + 15) / 16 * 16;
+  if (dpad > kScanMaxDpad)
+    return fail(FI8_ERR_DECLINED, "fi8_index_create: dim %d exceeds the supported %d", dim, kScanMaxDpad);
+  DeviceGuard g(ctx->device);
+  fi8_index* x = new (std::nothrow) fi8_index;
+  if (!x) return fail(FI8_ERR_OOM, "fi8_index_create: host allocation");
+  x->ctx = ctx;
+  x->device = ctx->device;
+  x->sm_count = ctx->sm_count;
+  x->n = n;
+  x->n_alloc = (n + kRowAlign - 1) / kRowAlign * kRowAlign;
+  x->dim = dim;
+  x->dpad = dpad;
+  x->id_base = (uint32_t)id_base;
+  cudaError_t e = cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&x->d_codes, (size_t)x->n_alloc * dpad);
+  if (e == cudaSuccess) e = cudaMalloc(&x->d_scales, (size_t)x->n_alloc * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&x->d_err, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMallocHost(&x->h_err, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemsetAsync(x->d_codes, 0, (size_t)x->n_alloc * dpad, x->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(x->d_scales, 0, (size_t)x->n_alloc * sizeof(float), x->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream);
+  if (e == cudaSuccess) {
+    if (dpad == dim)
+      e = cudaMemcpyAsync(x->d_codes, codes, (size_t)n * dim, cudaMemcpyHostToDevice, x->stream);
+    else
+      e = cudaMemcpy2DAsync(x->d_codes, dpad, codes, dim, dim, (size_t)n, cudaMemcpyHostToDevice, x->stream);
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(x->d_scales, scales, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, x->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
+  if (e != cudaSuccess) {
+    const int rc = cuda_fail(e, "gpu: device upload failed");
+    index_free(x);
+    return rc;
+  }
+  *out = x;
+  return FI8_OK;
+}
+
+int fi8_index_destroy(fi8_index* idx) {
+  if (!idx) return FI8_OK;
+  {
+    std::lock_guard<std::mutex> lk(idx->mu);
+  }
+  index_free(idx);
+  return FI8_OK;
+}
+
+int fi8_index_info(fi8_index* idx, int64_t* n, int32_t* dim) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_index_info: null index");
+  if (n) *n = idx->n;
+  if (dim) *dim = idx->dim;
+  return FI8_OK;
+}
+
+int fi8_topk_max_k(fi8_index* idx, int32_t* out) {
+  if (!idx || !out) return fail(FI8_ERR_ARG, "fi8_topk_max_k: null argument");
+  ScanGeometry g;
+  int32_t lo = 1, hi = kScanMaxCap;
+  while (lo < hi) {  // largest k with a valid geometry
+    const int32_t mid = (lo + hi + 1) / 2;
+    if (scan_geometry(idx->dpad, mid, true, &g)) lo = mid;
+    else hi = mid - 1;
+  }
+  *out = std::min<int32_t>(lo, kMergeMaxK);
+  return FI8_OK;
+}
+
+// ---------------------------------------------------------------------------
+// internal launch helpers (caller holds idx->mu and the device)
+// ---------------------------------------------------------------------------
+
+static int ensure_topk_scratch(fi8_index* x, int32_t M, int32_t k, int32_t G) {
+  int rc;
+  const size_t old_gthr = x->gthr_cap, old_ctr = x->counter_cap;
+  if ((rc = ensure_device(&x->d_gthr, &x->gthr_cap, (size_t)M, "scratch gthr")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_counter, &x->counter_cap, (size_t)M, "scratch counter")) != FI8_OK) return rc;
+  if (x->gthr_cap != old_gthr || x->counter_cap != old_ctr) {
+    // Fresh (or regrown) per-query state must start at zero; the kernel's last
+    // CTA returns it to zero after every launch.
+    FI8_CUDA(cudaMemsetAsync(x->d_gthr, 0, x->gthr_cap * sizeof(unsigned long long), x->stream), "memset gthr");
+    FI8_CUDA(cudaMemsetAsync(x->d_counter, 0, x->counter_cap * sizeof(unsigned int), x->stream), "memset counter");
+  }
+  if ((rc = ensure_device(&x->d_part, &x->part_cap, scan_part_keys(M, G, k), "scratch part")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_part_counts, &x->part_counts_cap, (size_t)M * G, "scratch counts")) != FI8_OK)
+    return rc;
+  return FI8_OK;
+}
+
+static ScanParams base_params(fi8_index* x, const ScanGeometry& geo) {
+  ScanParams p{};
+  p.codes = x->d_codes;
+  p.scales = x->d_scales;
+  p.n = x->n;
+  p.d = x->dim;
+  p.dpad = x->dpad;
+  p.rows_per_tile = geo.rows_per_tile;
+  p.stages = geo.stages;
+  p.ntiles = x->n_alloc / geo.rows_per_tile;
+  p.id_base = x->id_base;
+  p.err = x->d_err;
+  return p;
+}
+
+static int32_t grid_ctas(fi8_index* x, const ScanParams& p) {
+  int64_t G = std::min<int64_t>(x->sm_count > 0 ? x->sm_count : 1, p.ntiles);
+  return (int32_t)std::max<int64_t>(G, 1);
+}
+
+static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                       cudaStream_t st) {
+  ScanGeometry geo;
+  if (!scan_geometry(x->dpad, k, true, &geo))
+    return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d beyond the device top-K)", k);
+  ScanParams p = base_params(x, geo);
+  const int32_t G = grid_ctas(x, p);
+  const int32_t Mc = std::min(M, kScanMaxM);
+  int rc = ensure_topk_scratch(x, Mc, k, G);
+  if (rc != FI8_OK) return rc;
+  p.k = k;
+  p.cap = geo.cap;
+  p.gthr = x->d_gthr;
+  p.counter = x->d_counter;
+  p.part_keys = x->d_part;
+  p.part_counts = x->d_part_counts;
+  if (st != x->stream) {
+    // scratch was (re)initialised on the index stream; order the caller's stream after it
+    cudaEvent_t ev;
+    FI8_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
+    cudaEventRecord(ev, x->stream);
+    cudaStreamWaitEvent(st, ev, 0);
+    cudaEventDestroy(ev);
+  }
+  for (int32_t m0 = 0; m0 < M; m0 += Mc) {
+    const int32_t mm = std::min(Mc, M - m0);
+    p.q = d_q + (size_t)m0 * x->dim;
+    p.out_keys = d_keys + (size_t)m0 * k;
+    cudaError_t e = scan_launch(p, true, mm, G, geo.smem_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "scan_launch(topk)");
+  }
+  return FI8_OK;
+}
+
+static int launch_scores(fi8_index* x, const float* d_q, int32_t M, float* d_scores, cudaStream_t st) {
+  ScanGeometry geo;
+  if (!scan_geometry(x->dpad, 0, false, &geo)) return fail(FI8_ERR_ARG, "fi8: bad row pitch %d", x->dpad);
+  ScanParams p = base_params(x, geo);
+  const int32_t G = grid_ctas(x, p);
+  for (int32_t m0 = 0; m0 < M; m0 += kScanMaxM) {
+    const int32_t mm = std::min(kScanMaxM, M - m0);
+    p.q = d_q + (size_t)m0 * x->dim;
+    p.out_scores = d_scores + (size_t)m0 * x->n;
+    cudaError_t e = scan_launch(p, false, mm, G, geo.smem_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "scan_launch(score)");
+  }
+  return FI8_OK;
+}
+
+// After a synchronize: surface and clear the device error flag.
+static int check_device_error(fi8_index* x) {
+  if (*x->h_err != 0) {
+    const unsigned v = *x->h_err;
+    *x->h_err = 0;
+    cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream);
+    cudaStreamSynchronize(x->stream);
+    return fail(FI8_ERR_DEVICE, "fi8: kernel reported device error flags 0x%x (bounded wait expired)", v);
+  }
+  return FI8_OK;
+}
+
+int fi8_score_batch(fi8_index* idx, const float* q, int32_t M, float* dst) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_score_batch: null index");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || !q || !dst) return fail(FI8_ERR_ARG, "fi8_score_batch: bad arguments");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  fi8_index* x = idx;
+  int rc;
+  if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_scores, &x->d_scores_cap, (size_t)M * x->n, "staging scores")) != FI8_OK)
+    return rc;
+  FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
+           "H2D queries");
+  if ((rc = launch_scores(x, x->d_q, M, x->d_scores, x->stream)) != FI8_OK) return rc;
+  FI8_CUDA(cudaMemcpyAsync(dst, x->d_scores, (size_t)M * x->n * sizeof(float), cudaMemcpyDeviceToHost, x->stream),
+           "D2H scores");
+  FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
+           "D2H err");
+  FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+  return check_device_error(x);
+}
+
+int fi8_score(fi8_index* idx, const float* q, float* dst) { return fi8_score_batch(idx, q, 1, dst); }
+
+int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_topk_batch: null index");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || !q || !out_idx || !out_score) return fail(FI8_ERR_ARG, "fi8_topk_batch: bad arguments");
+  if (k <= 0 || (int64_t)k >= idx->n)  // gpu/anncuda/backend.go:577-579
+    return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d n=%lld batch=%d)", k, (long long)idx->n, M);
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  fi8_index* x = idx;
+  int rc;
+  const size_t nk = (size_t)M * k;
+  if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_keys, &x->d_keys_cap, nk, "staging keys")) != FI8_OK) return rc;
+  if ((rc = ensure_host(&x->h_keys, &x->h_keys_cap, nk, "pinned keys")) != FI8_OK) return rc;
+  FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
+           "H2D queries");
+  if ((rc = launch_topk(x, x->d_q, M, k, x->d_keys, x->stream)) != FI8_OK) return rc;
+  FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
+           "D2H keys");
+  FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
+           "D2H err");
+  FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+  if ((rc = check_device_error(x)) != FI8_OK) return rc;
+  return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
+}
+
+int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                         void* stream) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_topk_batch_async: null index");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || !d_q || !d_keys) return fail(FI8_ERR_ARG, "fi8_topk_batch_async: bad arguments");
+  // k >= n is allowed here: a row shard smaller than k contributes all of its
+  // rows (sorted, then empty slots) to the cross-shard merge.
+  if (k <= 0) return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d)", k);
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+  return launch_topk(idx, d_q, M, k, d_keys, st);
+}
+
+int fi8_index_sync(fi8_index* idx) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_index_sync: null index");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  FI8_CUDA(cudaDeviceSynchronize(), "sync");
+  FI8_CUDA(cudaMemcpy(idx->h_err, idx->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost), "D2H err");
+  return check_device_error(idx);
+}
+
+int fi8_keys_unpack(const uint64_t* keys, int64_t count, int32_t* out_idx, float* out_score) {
+  if (count < 0 || (count > 0 && (!keys || !out_idx || !out_score)))
+    return fail(FI8_ERR_ARG, "fi8_keys_unpack: bad arguments");
+  for (int64_t i = 0; i < count; i++) {
+    const uint64_t key = keys[i];
+    if (key == kEmptyKey) {
+      out_idx[i] = -1;
+      out_score[i] = 0.0f;
+    } else {
+      out_idx[i] = key_index(key);
+      out_score[i] = key_score(key);
+    }
+  }
+  return FI8_OK;
+}
+
+int fi8_merge_keys_async(fi8_ctx* ctx, const uint64_t* d_in, int32_t nsrc, int32_t M, int32_t k,
+                         uint64_t* d_out, void* stream) {
+  if (!ctx || !d_in || !d_out) return fail(FI8_ERR_ARG, "fi8_merge_keys_async: null argument");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || nsrc <= 0 || k <= 0) return fail(FI8_ERR_ARG, "fi8_merge_keys_async: bad shape");
+  if (k > kMergeMaxK) return fail(FI8_ERR_DECLINED, "fi8_merge_keys_async: k=%d beyond %d", k, kMergeMaxK);
+  DeviceGuard g(ctx->device);
+  cudaError_t e = merge_keys_launch(d_in, nsrc, M, k, d_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "merge_keys_launch");
+  return FI8_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,112 @@
+/*
+ * fi8.h -- C ABI of libfi8_b200.so, the B200 (sm_100a) backend for aikit's
+ * exact int8 nearest-neighbour scan (ann.FlatI8) and its FlatBinary -> FlatI8
+ * two-stage path.
+ *
+ * The ABI is what a Go adapter registered through ann.RegisterBackend
+ * (ann/backend.go:139) binds with cgo or a purego-style dlopen; INTEGRATION.md
+ * shows that adapter. Plain pointers and sizes only, no exceptions across the
+ * boundary, integer status codes, and no CPU fallback: a call either runs on
+ * the GPU or returns an error, which the Go seam already treats as "decline,
+ * use the next tier" (ann/flat_i8.go:191-198, ann/backend.go:86-122).
+ *
+ * Threading: every index serializes its own calls with an internal mutex, so an
+ * index may be shared by concurrent callers (FlatI8.Query is called
+ * concurrently, ann/flat_i8.go:29-30). Different indexes run concurrently.
+ */
+#ifndef FI8_H
+#define FI8_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define FI8_OK 0
+#define FI8_ERR_ARG 1      /* bad argument (shape mismatch, null pointer) */
+#define FI8_ERR_DECLINED 2 /* outside what the device path answers; caller falls back
+                              (the decline contract of gpu/anncuda/backend.go:577-579) */
+#define FI8_ERR_CUDA 3     /* a CUDA runtime call failed */
+#define FI8_ERR_OOM 4      /* device allocation failed (gpu/anncuda/backend.go:131-139) */
+#define FI8_ERR_DEVICE 5   /* a kernel reported an error (e.g. a bounded wait expired) */
+
+typedef struct fi8_ctx fi8_ctx;     /* one CUDA device */
+typedef struct fi8_index fi8_index; /* a device-resident FlatI8 shard */
+typedef struct fi8_bin fi8_bin;     /* a device-resident FlatBinaryI8 shard */
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* fi8_last_error(void);
+
+/* Number of visible CUDA devices. */
+int fi8_device_count(int* out);
+
+/* Open / close a device context. Replaces the device bring-up of
+ * gpu/anncuda/backend.go:67-116 (CreateSystemDefaultDevice + module loads). */
+int fi8_ctx_create(int device, fi8_ctx** out);
+int fi8_ctx_destroy(fi8_ctx* ctx);
+/* Streaming-multiprocessor count of the context's device. */
+int fi8_ctx_sm_count(fi8_ctx* ctx, int* out);
+
+/* ann.Backend.NewI8Index (ann/backend.go:20; gpu/anncuda/backend.go:124-154).
+ * Copies codes [n*dim] int8 row-major and scales [n] f32 to the device; the host
+ * arrays are not retained (they may alias an mmap, ann/flat_i8_mmap.go:157-180).
+ * id_base is the global index of row 0: a row shard of a larger corpus reports
+ * global indices (0 for a whole corpus). Rows are stored with a pitch of
+ * dim rounded up to 16 bytes, zero padded. */
+int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int64_t n,
+                     int32_t dim, int64_t id_base, fi8_index** out);
+
+/* I8Index.Close (ann/backend.go:31; gpu/anncuda/backend.go:238-246). */
+int fi8_index_destroy(fi8_index* idx);
+
+int fi8_index_info(fi8_index* idx, int64_t* n, int32_t* dim);
+
+/* I8Index.Score (ann/backend.go:30; gpu/anncuda/backend.go:181-205): q [dim] f32
+ * on the host, dst [n] f32 on the host. dst[j] is bit-identical to
+ * linalg.MatmulBTW8A8's value for row j (linalg/quant.go:290-296). */
+int fi8_score(fi8_index* idx, const float* q, float* dst);
+
+/* I8BatchIndex.ScoreBatch (ann/backend.go:43; gpu/anncuda/backend.go:212-236):
+ * q [M*dim], dst [M*n] row-major, every element assigned. */
+int fi8_score_batch(fi8_index* idx, const float* q, int32_t M, float* dst);
+
+/* I8TopKIndex.TopKBatch (ann/backend.go:54; gpu/anncuda/backend.go:568-667):
+ * q [M*dim] host f32; out_idx [M*k] int32 global indices, out_score [M*k] f32,
+ * each row sorted (score desc, index asc), padded with index -1 when fewer than
+ * k rows have a non-NaN score. Declines (FI8_ERR_DECLINED) when k <= 0 or
+ * k >= n, like the reference; also when k exceeds fi8_topk_max_k(). */
+int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx,
+                   float* out_score);
+
+/* Largest k the device top-K answers for this index. */
+int fi8_topk_max_k(fi8_index* idx, int32_t* out);
+
+/* Stream-ordered, device-resident form of fi8_topk_batch for callers that keep
+ * queries and results in HBM (multi-GPU merge, benchmarks): d_q [M*dim] f32 and
+ * d_keys [M*k] packed uint64 keys (decode with fi8_keys_unpack), both device
+ * pointers; stream is a cudaStream_t (NULL = the index's own stream). Does not
+ * synchronize; device-side errors surface at the next fi8_index_sync. Unlike
+ * fi8_topk_batch it accepts k >= n (a row shard smaller than k yields all of its
+ * rows, then empty keys). Calls on one index must not overlap on the GPU (they
+ * share the index's scratch); issue them on one stream. */
+int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                         void* stream);
+
+/* Wait for the index's stream and report any device-side error flag. */
+int fi8_index_sync(fi8_index* idx);
+
+/* Decode packed keys (host memory): index -1 / score 0 for empty slots. */
+int fi8_keys_unpack(const uint64_t* keys, int64_t count, int32_t* out_idx, float* out_score);
+
+/* Merge per-shard candidate keys: d_in [nsrc][M][k] (device, 0 = empty) ->
+ * d_out [M][k], the top k per query under (score desc, index asc). The
+ * N-way form of queryBatchSharded's merge (ann/backend.go:262-277). */
+int fi8_merge_keys_async(fi8_ctx* ctx, const uint64_t* d_in, int32_t nsrc, int32_t M, int32_t k,
+                         uint64_t* d_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

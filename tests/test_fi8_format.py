@@ -1,0 +1,92 @@
+"""FI8 v1 blob handling (ann/flat_i8_persist.go), CPU only. Re-expresses
+ann/flat_i8_persist_test.go and pins the real-data fixtures."""
+import hashlib
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import oracle
+from aikit_b200 import fi8_format, synth
+
+from conftest import GOLDEN
+
+
+def _good(n=100, d=32):
+    bq, bs = synth.Recipe(synth.UNIT, d, seed=3).codes(n)
+    return fi8_format.dumps(bq, bs), bq, bs
+
+
+def test_round_trip():
+    """TestFlatI8_roundTrip (ann/flat_i8_persist_test.go:24)."""
+    blob, bq, bs = _good(500, 64)
+    q2, s2 = fi8_format.load(blob)
+    assert q2.tobytes() == bq.tobytes() and s2.tobytes() == bs.tobytes()
+    assert fi8_format.dumps(q2, s2) == blob
+
+
+def test_empty_round_trip():
+    """TestFlatI8_emptyRoundTrip (ann/flat_i8_persist_test.go:53)."""
+    blob = fi8_format.dumps(np.zeros((0, 0), np.int8), np.zeros(0, np.float32))
+    q, s = fi8_format.load(blob)
+    assert q.shape[0] == 0 and s.shape[0] == 0
+
+
+def test_rejects_bad_blobs():
+    """TestLoadFlatI8_rejectsBadBlobs (ann/flat_i8_persist_test.go:71)."""
+    good, _, _ = _good()
+    flip = bytearray(good)
+    flip[0] = (flip[0] + 1) & 0xFF
+    for blob in [bytes([1, 2, 3]), b"", bytes(flip), good[:-4], good + b"\0"]:
+        with pytest.raises(fi8_format.FormatError):
+            fi8_format.load(blob)
+    fi8_format.load(good)
+
+
+def test_rejects_inconsistent_shape():
+    """TestLoadFlatI8_rejectsInconsistentShape (ann/flat_i8_persist_test.go:14)
+    and the committed fuzz-corpus seed (ann/testdata/fuzz/FuzzLoadFlatI8)."""
+    b = struct.pack("<IIIi", fi8_format.MAGIC, fi8_format.VERSION, 0x7FF90000, 0)
+    with pytest.raises(fi8_format.FormatError):
+        fi8_format.load(b)
+    seed = open(os.path.join(GOLDEN, "fuzz_seed_flati8.bin"), "rb").read()
+    assert len(seed) == 16
+    with pytest.raises(fi8_format.FormatError):
+        fi8_format.load(seed)
+
+
+def test_negative_shape_rejected():
+    b = struct.pack("<IIii", fi8_format.MAGIC, fi8_format.VERSION, -4, 2) + bytes(100)
+    with pytest.raises(fi8_format.FormatError):
+        fi8_format.load(b)
+
+
+def test_mmap_matches_copy(tmp_path):
+    """TestLoadFlatI8Mmap equals LoadFlatI8 (ann/flat_i8_mmap_test.go:26)."""
+    blob, bq, bs = _good(300, 48)
+    p = tmp_path / "x.fi8"
+    p.write_bytes(blob)
+    q, s = fi8_format.load_mmap(str(p))
+    assert np.array_equal(q, bq) and np.array_equal(s, bs)
+
+
+def test_embedded_corpus_fixture():
+    """The reference's shipped real-data blob: header (d=256, n=1747) recorded
+    at fixture generation; the committed 512-row head re-parses and serves a
+    FlatI8 query whose rank-0 hit is the row itself or, when the corpus holds an
+    exact duplicate (rows 432 and 511 here), the lower-index duplicate."""
+    meta = json.load(open(os.path.join(GOLDEN, "embedded_corpus_meta.json")))
+    assert (meta["dim"], meta["n"]) == (256, 1747)
+    assert meta["bytes"] == 16 + meta["n"] * meta["dim"] + 4 * meta["n"]
+    blob = open(os.path.join(GOLDEN, "embedded_corpus_head.fi8"), "rb").read()
+    q, s = fi8_format.load(blob)
+    assert q.shape == (512, 256)
+    # a dequantized row as the query: it must rank itself first
+    for row in (0, 17, 511):
+        qv = q[row].astype(np.float32) * s[row]
+        idx, sc = oracle.flat_i8_query(q, s, qv, 5)
+        assert idx[0] <= row and q[idx[0]].tobytes() == q[row].tobytes()
+        if idx[0] != row:
+            assert row in idx.tolist() and sc[idx.tolist().index(row)] == sc[0]
