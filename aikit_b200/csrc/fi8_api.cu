@@ -288,7 +288,7 @@ int fi8_topk_max_k(fi8_index* idx, int32_t* out) {
 // internal launch helpers (caller holds idx->mu and the device)
 // ---------------------------------------------------------------------------
 
-static int ensure_topk_scratch(fi8_index* x, int32_t M, int32_t k, int32_t G) {
+static int ensure_topk_scratch(fi8_index* x, int32_t M, int32_t k, int32_t G, cudaStream_t st) {
   int rc;
   const size_t old_gthr = x->gthr_cap, old_ctr = x->counter_cap;
   if ((rc = ensure_device(&x->d_gthr, &x->gthr_cap, (size_t)M, "scratch gthr")) != FI8_OK) return rc;
@@ -296,11 +296,13 @@ static int ensure_topk_scratch(fi8_index* x, int32_t M, int32_t k, int32_t G) {
   if (x->gthr_cap != old_gthr || x->counter_cap != old_ctr) {
     // Fresh (or regrown) per-query state must start at zero; the kernel's last
     // CTA returns it to zero after every launch.
-    FI8_CUDA(cudaMemsetAsync(x->d_gthr, 0, x->gthr_cap * sizeof(unsigned long long), x->stream), "memset gthr");
-    FI8_CUDA(cudaMemsetAsync(x->d_counter, 0, x->counter_cap * sizeof(unsigned int), x->stream), "memset counter");
+    // (on the launch stream, so the kernel that uses it is ordered after it).
+    FI8_CUDA(cudaMemsetAsync(x->d_gthr, 0, x->gthr_cap * sizeof(unsigned long long), st), "memset gthr");
+    FI8_CUDA(cudaMemsetAsync(x->d_counter, 0, x->counter_cap * sizeof(unsigned int), st), "memset counter");
   }
   if ((rc = ensure_device(&x->d_part, &x->part_cap, scan_part_keys(M, G, k), "scratch part")) != FI8_OK) return rc;
-  if ((rc = ensure_device(&x->d_part_counts, &x->part_counts_cap, (size_t)M * G, "scratch counts")) != FI8_OK)
+  if ((rc = ensure_device(&x->d_part_counts, &x->part_counts_cap, (size_t)M * scan_lists_per_query(G),
+                          "scratch counts")) != FI8_OK)
     return rc;
   return FI8_OK;
 }
@@ -333,7 +335,7 @@ static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uin
   ScanParams p = base_params(x, geo);
   const int32_t G = grid_ctas(x, p);
   const int32_t Mc = std::min(M, kScanMaxM);
-  int rc = ensure_topk_scratch(x, Mc, k, G);
+  int rc = ensure_topk_scratch(x, Mc, k, G, st);
   if (rc != FI8_OK) return rc;
   p.k = k;
   p.cap = geo.cap;
@@ -341,14 +343,6 @@ static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uin
   p.counter = x->d_counter;
   p.part_keys = x->d_part;
   p.part_counts = x->d_part_counts;
-  if (st != x->stream) {
-    // scratch was (re)initialised on the index stream; order the caller's stream after it
-    cudaEvent_t ev;
-    FI8_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
-    cudaEventRecord(ev, x->stream);
-    cudaStreamWaitEvent(st, ev, 0);
-    cudaEventDestroy(ev);
-  }
   for (int32_t m0 = 0; m0 < M; m0 += Mc) {
     const int32_t mm = std::min(Mc, M - m0);
     p.q = d_q + (size_t)m0 * x->dim;
@@ -446,8 +440,7 @@ int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k,
   if (k <= 0) return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d)", k);
   std::lock_guard<std::mutex> lk(idx->mu);
   DeviceGuard g(idx->device);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
-  return launch_topk(idx, d_q, M, k, d_keys, st);
+  return launch_topk(idx, d_q, M, k, d_keys, static_cast<cudaStream_t>(stream));
 }
 
 int fi8_index_sync(fi8_index* idx) {

@@ -87,11 +87,23 @@ __device__ __forceinline__ int8_t quant_code(float v, float inv) {
   return (int8_t)(int)x;
 }
 
+// An IEEE binary32 multiply with the NaN results of x86 SSE (MULSS), which is
+// what the reference's Go code runs on amd64: a NaN operand propagates quieted
+// (the first one if both are NaN), and an invalid operation (0 * Inf) yields the
+// "real indefinite" 0xFFC00000. Finite results are plain round-to-nearest.
+__device__ __forceinline__ float mul_x86(float a, float b) {
+  const float r = __fmul_rn(a, b);
+  if (r == r) return r;
+  if (a != a) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+  if (b != b) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+  return __uint_as_float(0xFFC00000u);
+}
+
 // float32(dot) * qscale * rowscale, left to right with two rounded multiplies;
 // an all-zero query (qscale == 0) scores exactly 0 (quant.go:291-294).
 __device__ __forceinline__ float w8a8_score(int32_t dot, float qscale, float rowscale) {
   if (qscale == 0.0f) return 0.0f;
-  return __fmul_rn(__fmul_rn(__int2float_rn(dot), qscale), rowscale);
+  return mul_x86(mul_x86(__int2float_rn(dot), qscale), rowscale);
 }
 
 // ---------------------------------------------------------------------------

@@ -6,20 +6,23 @@
 // replaces, gemv_w8a8 + topk_rows/topk_split/topk_merge
 // (gpu/anncuda/gemv_w8a8.cu:76-130, :480-669).
 //
-// Structure (one CTA per SM, persistent over row tiles):
-//   * thread 0 streams R-row tiles of the corpus (R*dpad contiguous bytes plus
-//     R scales) into a STAGES-deep shared-memory ring with cp.async.bulk,
-//     completion tracked by one mbarrier per stage;
-//   * every CTA quantizes its query in shared memory (bit-identical to
-//     quantizeRowInt8), then 8 lanes per row dot 16-byte chunks with dp4a and
-//     reduce with warp shuffles;
-//   * top-K: candidates above the CTA threshold go to a shared-memory buffer;
-//     when it fills, a bitonic sort keeps the best k and raises the threshold,
-//     which is also published to a per-query global threshold (atomicMax) that
-//     every CTA reads back each tile. The threshold is always the k-th best key
-//     of k real rows, so nothing that can reach the global top-k is dropped;
-//   * the last CTA to finish (ticket counter) merges the per-CTA survivors and
-//     writes the final sorted keys, then resets the per-query scratch.
+// One persistent CTA per SM, warp-specialized:
+//   * warp 16 (producer): streams R-row tiles of the corpus (R*dpad contiguous
+//     bytes plus R scales) into an S-deep shared-memory ring with
+//     cp.async.bulk; a "full" mbarrier per stage counts the bytes, an "empty"
+//     mbarrier per stage counts the consumer warps that are done with it;
+//   * warps 0-15 (two consumer groups of 8 warps): group g takes the CTA's
+//     tiles g, g+2, g+4, ... Each 8-lane quarter-warp owns RPG rows of a tile,
+//     holds its query chunks in registers (the query is quantized in shared
+//     memory first, bit-identical to quantizeRowInt8) and dots 16-byte row
+//     chunks with dp4a; a transpose-reduce leaves one full row sum per lane;
+//   * top-K per group: candidates above the group threshold are appended to a
+//     shared buffer; when it fills, a bitonic sort keeps the best k and raises
+//     the threshold, which is also published to a per-query global threshold
+//     (atomicMax) read back every tile. Every threshold is the k-th best key of
+//     k real rows, so nothing that can reach the global top-k is dropped;
+//   * the last CTA to finish (ticket counter) merges the per-group survivor
+//     lists, writes the final sorted keys and resets the per-query scratch.
 #include "fi8_device.cuh"
 #include "fi8_scan.cuh"
 
@@ -27,10 +30,22 @@ namespace fi8 {
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kRowsPerPass = kWarps * 4;  // 8 lanes per row, 4 rows per warp
+constexpr int kGroupThreads = 256;
+constexpr int kGroups = 2;
+constexpr int kConsumerThreads = kGroups * kGroupThreads;
+constexpr int kBlockThreads = kConsumerThreads + 32;  // + producer warp
+constexpr int kConsumerWarps = kConsumerThreads / 32;
+constexpr int kMaxStages = 4;
 constexpr size_t kSmemBudget = 220 * 1024;
+constexpr int kBarConsumers = 3;  // named barrier over the 512 consumer threads
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;
@@ -56,15 +71,35 @@ __device__ __forceinline__ void warp_append(bool take, uint64_t key, uint64_t* b
   if (take) buf[base + __popc(mask & lanemask_lt())] = key;
 }
 
-// Sort the first cnt entries of buf, keep the best k, raise the CTA threshold
-// and optionally publish it. Uniform: all threads call with the same cnt.
-__device__ void compact(uint64_t* buf, int cnt, int k, int* s_count, unsigned long long* s_local_thr,
-                        unsigned long long* gthr) {
+// Bitonic sort (descending) of n = 2^j keys by one 256-thread group.
+__device__ void group_sort_desc(uint64_t* buf, int n, int gtid, int bar) {
+  const int half = n >> 1;
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = gtid; i < half; i += kGroupThreads) {
+        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t a = buf[lo], b = buf[hi];
+        if ((a < b) == desc) {
+          buf[lo] = b;
+          buf[hi] = a;
+        }
+      }
+      named_sync(bar, kGroupThreads);
+    }
+  }
+}
+
+// Sort the first cnt keys, keep the best k, raise (and optionally publish) the
+// group threshold. All 256 threads of the group call it with the same cnt.
+__device__ void group_compact(uint64_t* buf, int cnt, int k, int* s_count, unsigned long long* s_local_thr,
+                              unsigned long long* gthr, int gtid, int bar) {
   const int n2 = next_pow2(cnt < 2 ? 2 : cnt);
-  for (int i = cnt + threadIdx.x; i < n2; i += blockDim.x) buf[i] = kEmptyKey;
-  __syncthreads();
-  bitonic_sort_desc(buf, n2);
-  if (threadIdx.x == 0) {
+  for (int i = cnt + gtid; i < n2; i += kGroupThreads) buf[i] = kEmptyKey;
+  named_sync(bar, kGroupThreads);
+  group_sort_desc(buf, n2, gtid, bar);
+  if (gtid == 0) {
     *s_count = cnt < k ? cnt : k;
     if (cnt >= k) {
       const unsigned long long t = buf[k - 1];
@@ -72,19 +107,42 @@ __device__ void compact(uint64_t* buf, int cnt, int k, int* s_count, unsigned lo
       if (gthr) atomicMax(gthr, t);
     }
   }
-  __syncthreads();
+  named_sync(bar, kGroupThreads);
 }
 
-template <bool TOPK>
-__global__ void __launch_bounds__(kThreads, 1) scan_kernel(ScanParams p) {
+// Number of leading keys >= T in a descending buffer of n keys.
+__device__ int prefix_at_least(const uint64_t* buf, int n, unsigned long long T) {
+  int lo = 0, hi = n;  // buf[0..lo) >= T, buf[hi..n) < T
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (buf[mid] >= T) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
+template <int RPG>
+struct RowsLog2 {
+  static constexpr int v = RPG == 1 ? 0 : RPG == 2 ? 1 : RPG == 4 ? 2 : 3;
+};
+
+// CPL: 16-byte chunks per lane per row (dpad = 128*CPL), 0 = generic pitch.
+// RPG: rows per 8-lane quarter-warp per tile (tile rows R = 32*RPG); the
+// generic kernel uses RPG=1 and R/32 passes.
+template <bool TOPK, int CPL, int RPG>
+__global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ float s_red[kWarps];
+  __shared__ uint64_t s_full[kMaxStages];
+  __shared__ uint64_t s_empty[kMaxStages];
+  __shared__ float s_red[kConsumerWarps];
   __shared__ float s_qscale;
-  __shared__ int s_count;
-  __shared__ int s_abort;
+  __shared__ int s_count[kGroups];
+  __shared__ unsigned long long s_thr[kGroups];
+  __shared__ unsigned long long s_local_thr[kGroups];
+  __shared__ unsigned long long s_T;
+  __shared__ volatile int s_abort;
+  __shared__ int s_gabort[kGroups];
   __shared__ int s_last;
-  __shared__ unsigned long long s_thr;
-  __shared__ unsigned long long s_local_thr;
   __shared__ int s_off[1025];
 
   const int G = gridDim.x;
@@ -101,159 +159,230 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(ScanParams p) {
 
   unsigned char* stages = smem;
   int8_t* q_s = reinterpret_cast<int8_t*>(smem + (size_t)S * stage_bytes);
-  uint64_t* buf = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes + (size_t)dpad);
-  uint64_t* bars = buf + (TOPK ? p.cap : 0);
+  uint64_t* bufs = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes + (size_t)dpad);
 
   const int64_t my_tiles = (p.ntiles > cta) ? (p.ntiles - cta + G - 1) / G : 0;
 
   if (tid == 0) {
-    for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
+    for (int s = 0; s < S; s++) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], kGroupThreads / 32);
+    }
     fence_mbar_init();
-    s_count = 0;
     s_abort = 0;
-    s_local_thr = 0;
-    s_thr = TOPK ? ld_relaxed_u64(p.gthr + y) : 0ull;
+    s_T = 0;
+    for (int g = 0; g < kGroups; g++) {
+      s_count[g] = 0;
+      s_local_thr[g] = 0;
+      s_thr[g] = TOPK ? ld_relaxed_u64(p.gthr + y) : 0ull;
+    }
   }
   __syncthreads();
 
-  auto issue = [&](int64_t it) {
-    const int s = (int)(it % S);
-    const int64_t tile = cta + it * G;
-    unsigned char* st = stages + (size_t)s * stage_bytes;
-    mbar_arrive_expect_tx(&bars[s], stage_bytes);
-    bulk_g2s(st, p.codes + (size_t)tile * code_bytes, code_bytes, &bars[s]);
-    bulk_g2s(st + code_bytes, p.scales + (size_t)tile * R, (uint32_t)R * 4u, &bars[s]);
-  };
-  if (tid == 0) {
-    const int64_t pre = my_tiles < S ? my_tiles : S;
-    for (int64_t it = 0; it < pre; it++) issue(it);
-  }
+  if (warp == kConsumerWarps) {
+    // ======================= producer warp =======================
+    if (lane == 0) {
+      int64_t it = 0;
+      for (; it < my_tiles; it++) {
+        const int s = (int)(it % S);
+        if (it >= S && !mbar_wait_bounded(&s_empty[s], (uint32_t)(((it / S) - 1) & 1))) {
+          s_abort = 1;
+          atomicOr(p.err, 1u);
+        }
+        if (s_abort) break;
+        const int64_t tile = cta + it * G;
+        unsigned char* st = stages + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(&s_full[s], stage_bytes);
+        bulk_g2s(st, p.codes + (size_t)tile * code_bytes, code_bytes, &s_full[s]);
+        bulk_g2s(st + code_bytes, p.scales + (size_t)tile * R, (uint32_t)R * 4u, &s_full[s]);
+      }
+      if (s_abort) {
+        // let the copies already issued land before the CTA can exit (bounded)
+        for (int64_t j = (it > S ? it - S : 0); j < it; j++)
+          mbar_wait_bounded(&s_full[j % S], (uint32_t)((j / S) & 1));
+      }
+    }
+    __syncwarp();
+  } else {
+    // ======================= consumer groups =======================
+    const int g = warp / (kGroupThreads / 32);
+    const int gtid = tid - g * kGroupThreads;
+    const int gwarp = gtid >> 5;
+    const int bar = 1 + g;
+    uint64_t* buf = bufs + (TOPK ? (size_t)g * p.cap : 0);
 
-  // ---- quantize this CTA's query into shared memory (quant.go:43-71) ----
-  const float* q = p.q + (size_t)y * p.d;
-  float m = 0.0f;
-  for (int i = tid; i < p.d; i += kThreads) m = absmax_step(m, q[i]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) m = absmax_combine(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if (lane == 0) s_red[warp] = m;
-  __syncthreads();
-  if (warp == 0) {
-    m = lane < kWarps ? s_red[lane] : 0.0f;
+    // quantize this CTA's query (quant.go:43-71) into shared memory
+    const float* q = p.q + (size_t)y * p.d;
+    float m = 0.0f;
+    for (int i = tid; i < p.d; i += kConsumerThreads) m = absmax_step(m, q[i]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = absmax_combine(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (lane == 0) s_red[0] = m;
-  }
-  __syncthreads();
-  const float maxabs = s_red[0];
-  if (maxabs == 0.0f) {
-    for (int i = tid; i < dpad; i += kThreads) q_s[i] = 0;
-    if (tid == 0) s_qscale = 0.0f;
-  } else {
-    const float sc = __fdiv_rn(maxabs, 127.0f);
-    const float inv = __fdiv_rn(1.0f, sc);
-    for (int i = tid; i < dpad; i += kThreads) q_s[i] = i < p.d ? quant_code(q[i], inv) : (int8_t)0;
-    if (tid == 0) s_qscale = sc;
-  }
-  __syncthreads();
-  const float qscale = s_qscale;
-
-  // ---- main loop over this CTA's tiles ----
-  const int chunks = dpad >> 4;
-  const int lane8 = lane & 7;
-  int64_t it = 0;
-  for (; it < my_tiles; it++) {
-    const int s = (int)(it % S);
-    const uint32_t par = (uint32_t)((it / S) & 1);
-    if (!mbar_wait_bounded(&bars[s], par)) {
-      s_abort = 1;
-      atomicOr(p.err, 1u);
-    }
-    const int64_t row0 = (cta + it * G) * (int64_t)R;
-    const unsigned char* st = stages + (size_t)s * stage_bytes;
-    const float* sc_s = reinterpret_cast<const float*>(st + code_bytes);
-    const unsigned long long thr = TOPK ? s_thr : 0ull;
-    for (int pass = 0; pass < R; pass += kRowsPerPass) {
-      const int r = pass + warp * 4 + (lane >> 3);
-      const int4* rowp = reinterpret_cast<const int4*>(st + (size_t)r * dpad);
-      const int4* qp = reinterpret_cast<const int4*>(q_s);
-      int acc = 0;
-#pragma unroll 4
-      for (int c = lane8; c < chunks; c += 8) {
-        const int4 a = rowp[c];
-        const int4 b = qp[c];
-        acc = __dp4a(a.x, b.x, acc);
-        acc = __dp4a(a.y, b.y, acc);
-        acc = __dp4a(a.z, b.z, acc);
-        acc = __dp4a(a.w, b.w, acc);
-      }
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-      const int64_t g = row0 + r;
-      const bool mine = (lane8 == 0) && (g < p.n);
-      float score = 0.0f;
-      if (mine) score = w8a8_score(acc, qscale, sc_s[r]);
-      if (TOPK) {
-        uint64_t key = kEmptyKey;
-        bool take = false;
-        if (mine && score == score) {
-          key = make_key(score, p.id_base + (uint32_t)g);
-          take = key > thr;
-        }
-        warp_append(take, key, buf, &s_count);
-      } else {
-        if (mine) p.out_scores[(size_t)y * p.n + g] = score;
-      }
-    }
-    __syncthreads();
-    if (s_abort) break;
-    if (tid == 0 && it + S < my_tiles) issue(it + S);
-    if (TOPK) {
-      const int cnt = s_count;
-      if (cnt > p.cap - R) compact(buf, cnt, p.k, &s_count, &s_local_thr, p.gthr + y);
-      if (tid == 0) {
-        const unsigned long long gt = ld_relaxed_u64(p.gthr + y);
-        s_thr = gt > s_local_thr ? gt : s_local_thr;
-      }
-      __syncthreads();
-    }
-  }
-
-  if (s_abort) {
-    // Let the copies this CTA started land before it exits (bounded).
+    if (lane == 0) s_red[warp] = m;
+    named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
-      const int64_t last = (it + S < my_tiles) ? it + S : my_tiles;
-      for (int64_t j = it; j < last; j++) mbar_wait_bounded(&bars[j % S], (uint32_t)((j / S) & 1));
+      float mm = 0.0f;
+      for (int w = 0; w < kConsumerWarps; w++) mm = absmax_combine(mm, s_red[w]);
+      s_red[0] = mm;
     }
-    __syncthreads();
+    named_sync(kBarConsumers, kConsumerThreads);
+    const float maxabs = s_red[0];
+    if (maxabs == 0.0f) {
+      for (int i = tid; i < dpad; i += kConsumerThreads) q_s[i] = 0;
+      if (tid == 0) s_qscale = 0.0f;
+    } else {
+      const float sc = __fdiv_rn(maxabs, 127.0f);
+      const float inv = __fdiv_rn(1.0f, sc);
+      for (int i = tid; i < dpad; i += kConsumerThreads) q_s[i] = i < p.d ? quant_code(q[i], inv) : (int8_t)0;
+      if (tid == 0) s_qscale = sc;
+    }
+    named_sync(kBarConsumers, kConsumerThreads);
+    const float qscale = s_qscale;
+
+    const int lane8 = lane & 7;
+    const int lg = lane >> 3;
+    constexpr int LOGR = RowsLog2<RPG>::v;
+    int4 qreg[CPL > 0 ? CPL : 1];
+#pragma unroll
+    for (int j = 0; j < (CPL > 0 ? CPL : 1); j++)
+      if (CPL > 0) qreg[j] = reinterpret_cast<const int4*>(q_s)[lane8 + 8 * j];
+
+    for (int64_t it = g; it < my_tiles; it += kGroups) {
+      const int s = (int)(it % S);
+      if (!mbar_wait_bounded(&s_full[s], (uint32_t)((it / S) & 1))) {
+        s_abort = 1;
+        atomicOr(p.err, 1u);
+      }
+      const int64_t row0 = (cta + it * G) * (int64_t)R;
+      const unsigned char* st = stages + (size_t)s * stage_bytes;
+      const float* sc_s = reinterpret_cast<const float*>(st + code_bytes);
+      const unsigned long long thr = TOPK ? s_thr[g] : 0ull;
+      unsigned long long gt_prefetch = 0ull;
+      if (TOPK && gtid == 0) gt_prefetch = ld_relaxed_u64(p.gthr + y);
+
+      const int passes = (CPL > 0) ? 1 : R / 32;
+      for (int pass = 0; pass < passes; pass++) {
+        // rows of this quarter-warp: base .. base + RPG - 1
+        const int base = pass * 32 + gwarp * (4 * RPG) + lg * RPG;
+        int vals[RPG];
+        if (CPL > 0) {
+          int acc[RPG][2];
+#pragma unroll
+          for (int i = 0; i < RPG; i++) acc[i][0] = acc[i][1] = 0;
+#pragma unroll
+          for (int j = 0; j < (CPL > 0 ? CPL : 1); j++) {
+#pragma unroll
+            for (int i = 0; i < RPG; i++) {
+              const int4 a = reinterpret_cast<const int4*>(st + (size_t)(base + i) * dpad)[lane8 + 8 * j];
+              int t = acc[i][j & 1];
+              t = __dp4a(a.x, qreg[j].x, t);
+              t = __dp4a(a.y, qreg[j].y, t);
+              t = __dp4a(a.z, qreg[j].z, t);
+              t = __dp4a(a.w, qreg[j].w, t);
+              acc[i][j & 1] = t;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < RPG; i++) vals[i] = acc[i][0] + acc[i][1];
+        } else {
+          const int chunks = dpad >> 4;
+          const int4* rowp = reinterpret_cast<const int4*>(st + (size_t)base * dpad);
+          const int4* qp = reinterpret_cast<const int4*>(q_s);
+          int a0 = 0, a1 = 0;
+          int c = lane8;
+          for (; c + 8 < chunks; c += 16) {
+            const int4 a = rowp[c], b = qp[c];
+            const int4 a2 = rowp[c + 8], b2 = qp[c + 8];
+            a0 = __dp4a(a.x, b.x, a0);
+            a0 = __dp4a(a.y, b.y, a0);
+            a0 = __dp4a(a.z, b.z, a0);
+            a0 = __dp4a(a.w, b.w, a0);
+            a1 = __dp4a(a2.x, b2.x, a1);
+            a1 = __dp4a(a2.y, b2.y, a1);
+            a1 = __dp4a(a2.z, b2.z, a1);
+            a1 = __dp4a(a2.w, b2.w, a1);
+          }
+          if (c < chunks) {
+            const int4 a = rowp[c], b = qp[c];
+            a0 = __dp4a(a.x, b.x, a0);
+            a0 = __dp4a(a.y, b.y, a0);
+            a0 = __dp4a(a.z, b.z, a0);
+            a0 = __dp4a(a.w, b.w, a0);
+          }
+          vals[0] = a0 + a1;
+        }
+        // transpose-reduce over the 8 lanes: lane8 >> (3-LOGR) ends up owning
+        // row (base + that index) with the complete sum.
+#pragma unroll
+        for (int h = RPG, off = 4; h > 1; h >>= 1, off >>= 1) {
+          const bool upper = (lane8 & off) != 0;
+#pragma unroll
+          for (int t = 0; t < h / 2; t++) {
+            const int keep = upper ? vals[t + h / 2] : vals[t];
+            const int send = upper ? vals[t] : vals[t + h / 2];
+            vals[t] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
+        }
+#pragma unroll
+        for (int off = 4 >> LOGR; off >= 1; off >>= 1) vals[0] += __shfl_xor_sync(0xffffffffu, vals[0], off);
+
+        const bool owner = (lane8 & ((8 >> LOGR) - 1)) == 0;
+        const int r = base + (lane8 >> (3 - LOGR));
+        const int64_t gr = row0 + r;
+        const bool mine = owner && (gr < p.n);
+        float score = 0.0f;
+        if (mine) score = w8a8_score(vals[0], qscale, sc_s[r]);
+        if (TOPK) {
+          uint64_t key = kEmptyKey;
+          bool take = false;
+          if (mine && score == score) {
+            key = make_key(score, p.id_base + (uint32_t)gr);
+            take = key > thr;
+          }
+          warp_append(take, key, buf, &s_count[g]);
+        } else if (mine) {
+          p.out_scores[(size_t)y * p.n + gr] = score;
+        }
+      }
+      // this warp is done reading the stage
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[s]);
+      if (TOPK) {
+        named_sync(bar, kGroupThreads);
+        const int cnt = s_count[g];
+        if (cnt > p.cap - R) group_compact(buf, cnt, p.k, &s_count[g], &s_local_thr[g], p.gthr + y, gtid, bar);
+        if (gtid == 0) {
+          s_thr[g] = gt_prefetch > s_local_thr[g] ? gt_prefetch : s_local_thr[g];
+          s_gabort[g] = s_abort;
+        }
+        named_sync(bar, kGroupThreads);
+        if (s_gabort[g]) break;  // group-uniform: read after the barrier
+      } else if (__any_sync(0xffffffffu, s_abort)) {
+        break;  // warp-uniform (score mode has no group barriers)
+      }
+    }
+    if (TOPK) {
+      named_sync(bar, kGroupThreads);
+      group_compact(buf, s_count[g], p.k, &s_count[g], &s_local_thr[g], p.gthr + y, gtid, bar);
+    }
   }
 
   if (!TOPK) return;
+  __syncthreads();  // both groups (and the producer) are done
 
-  // ---- per-CTA result: best k, filtered by the current shared threshold ----
-  {
-    const int cnt = s_abort ? 0 : s_count;
-    compact(buf, cnt, p.k, &s_count, &s_local_thr, p.gthr + y);
-  }
-  if (tid == 0) s_thr = ld_relaxed_u64(p.gthr + y);
+  // ---- per-group results: best k with key >= the shared threshold ----
+  if (tid == 0) s_T = ld_relaxed_u64(p.gthr + y);
   __syncthreads();
-  const int have = s_count;
-  const unsigned long long T = s_thr;
-  uint64_t* my_part = p.part_keys + ((size_t)y * G + cta) * p.k;
-  // buf[0..have) is sorted descending; keep the prefix with key >= T.
-  int keep = 0;
-  {
-    // count via ballot over the sorted prefix
-    for (int base = 0; base < have; base += kThreads) {
-      const int i = base + tid;
-      const int ok = (i < have && buf[i] >= T) ? 1 : 0;
-      const int c = __syncthreads_count(ok);
-      keep += c;
-      if (c < kThreads) break;
-    }
+  const int L = kGroups * G;  // survivor lists for this query
+  if (warp < kConsumerWarps) {
+    const int g = warp / (kGroupThreads / 32);
+    const int gtid = tid - g * kGroupThreads;
+    const uint64_t* buf = bufs + (size_t)g * p.cap;
+    const int have = s_count[g];
+    const int keep = prefix_at_least(buf, have, s_T);
+    uint64_t* mine = p.part_keys + ((size_t)y * L + (size_t)cta * kGroups + g) * p.k;
+    for (int i = gtid; i < keep; i += kGroupThreads) mine[i] = buf[i];
+    if (gtid == 0) p.part_counts[(size_t)y * L + cta * kGroups + g] = keep;
   }
-  for (int i = tid; i < keep; i += kThreads) my_part[i] = buf[i];
-  if (tid == 0) p.part_counts[(size_t)y * G + cta] = keep;
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -261,58 +390,61 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(ScanParams p) {
     s_last = (ticket == (unsigned int)(G - 1)) ? 1 : 0;
   }
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last || tid >= kGroupThreads) return;
 
-  // ---- last CTA: merge the G survivor lists for query y ----
+  // ---- last CTA, group 0: merge the L survivor lists for query y ----
   __threadfence();
-  if (tid == 0) {
-    s_thr = ld_relaxed_u64(p.gthr + y);
-    s_count = 0;
-    s_local_thr = 0;
+  const int gtid = tid;
+  const int bar = 1;
+  uint64_t* buf = bufs;
+  if (gtid == 0) {
+    s_T = ld_relaxed_u64(p.gthr + y);
+    s_count[0] = 0;
+    s_local_thr[0] = 0;
   }
-  // exclusive prefix of the G counts (warp 0, 32 at a time)
-  if (warp == 0) {
+  if (warp == 0) {  // exclusive prefix of the L counts
     int run = 0;
-    for (int b = 0; b < G; b += 32) {
+    for (int b = 0; b < L; b += 32) {
       const int i = b + lane;
-      int v = (i < G) ? __ldcg(p.part_counts + (size_t)y * G + i) : 0;
+      const int v = (i < L) ? __ldcg(p.part_counts + (size_t)y * L + i) : 0;
       int x = v;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const int t = __shfl_up_sync(0xffffffffu, x, off);
         if (lane >= off) x += t;
       }
-      if (i < G) s_off[i] = run + x - v;
+      if (i < L) s_off[i] = run + x - v;
       run += __shfl_sync(0xffffffffu, x, 31);
     }
-    if (lane == 0) s_off[G] = run;
+    if (lane == 0) s_off[L] = run;
   }
-  __syncthreads();
-  const int total = s_off[G];
-  const unsigned long long Tf = s_thr;
-  for (int base = 0; base < total; base += kThreads) {
-    const int e = base + tid;
+  named_sync(bar, kGroupThreads);
+  const int total = s_off[L];
+  const unsigned long long Tf = s_T;
+  for (int b0 = 0; b0 < total; b0 += kGroupThreads) {
+    const int e = b0 + gtid;
     bool take = false;
     uint64_t key = kEmptyKey;
     if (e < total) {
-      int lo = 0, hi = G;  // find l with s_off[l] <= e < s_off[l+1]
+      int lo = 0, hi = L;  // list l with s_off[l] <= e < s_off[l+1]
       while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
         if (s_off[mid] <= e) lo = mid;
         else hi = mid;
       }
-      key = __ldcg(p.part_keys + ((size_t)y * G + lo) * p.k + (e - s_off[lo]));
-      take = key >= Tf && key > s_local_thr;
+      key = __ldcg(p.part_keys + ((size_t)y * L + lo) * p.k + (e - s_off[lo]));
+      take = key >= Tf && key > s_local_thr[0];
     }
-    warp_append(take, key, buf, &s_count);
-    __syncthreads();
-    const int cnt = s_count;
-    if (cnt > p.cap - kThreads) compact(buf, cnt, p.k, &s_count, &s_local_thr, nullptr);
+    warp_append(take, key, buf, &s_count[0]);
+    named_sync(bar, kGroupThreads);
+    const int cnt = s_count[0];
+    if (cnt > p.cap - kGroupThreads) group_compact(buf, cnt, p.k, &s_count[0], &s_local_thr[0], nullptr, gtid, bar);
   }
-  compact(buf, s_count, p.k, &s_count, &s_local_thr, nullptr);
-  const int fin = s_count;
-  for (int i = tid; i < p.k; i += kThreads) p.out_keys[(size_t)y * p.k + i] = i < fin ? buf[i] : kEmptyKey;
-  if (tid == 0) {
+  named_sync(bar, kGroupThreads);
+  group_compact(buf, s_count[0], p.k, &s_count[0], &s_local_thr[0], nullptr, gtid, bar);
+  const int fin = s_count[0];
+  for (int i = gtid; i < p.k; i += kGroupThreads) p.out_keys[(size_t)y * p.k + i] = i < fin ? buf[i] : kEmptyKey;
+  if (gtid == 0) {
     p.counter[y] = 0u;
     p.gthr[y] = 0ull;
   }
@@ -320,24 +452,25 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(ScanParams p) {
 
 // ---------------------------------------------------------------------------
 // merge_keys_kernel: top-k of nsrc candidate lists per query, one CTA each.
-// Used for the cross-GPU merge after the all-gather (the 8-way analogue of
+// Used for the cross-GPU merge after the all-gather (the N-way analogue of
 // queryBatchSharded's merge, ann/backend.go:262-277).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kGroupThreads, 1)
     merge_keys_kernel(const uint64_t* in, int nsrc, int M, int k, int cap, uint64_t* out) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_count;
   __shared__ unsigned long long s_local_thr;
   uint64_t* buf = reinterpret_cast<uint64_t*>(smem);
   const int y = blockIdx.x;
-  if (threadIdx.x == 0) {
+  const int gtid = threadIdx.x;
+  if (gtid == 0) {
     s_count = 0;
     s_local_thr = 0;
   }
-  __syncthreads();
+  named_sync(1, kGroupThreads);
   const int total = nsrc * k;
-  for (int base = 0; base < total; base += kThreads) {
-    const int e = base + threadIdx.x;
+  for (int b0 = 0; b0 < total; b0 += kGroupThreads) {
+    const int e = b0 + gtid;
     bool take = false;
     uint64_t key = kEmptyKey;
     if (e < total) {
@@ -346,13 +479,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       take = key != kEmptyKey && key > s_local_thr;
     }
     warp_append(take, key, buf, &s_count);
-    __syncthreads();
+    named_sync(1, kGroupThreads);
     const int cnt = s_count;
-    if (cnt > cap - kThreads) compact(buf, cnt, k, &s_count, &s_local_thr, nullptr);
+    if (cnt > cap - kGroupThreads) group_compact(buf, cnt, k, &s_count, &s_local_thr, nullptr, gtid, 1);
   }
-  compact(buf, s_count, k, &s_count, &s_local_thr, nullptr);
+  named_sync(1, kGroupThreads);
+  group_compact(buf, s_count, k, &s_count, &s_local_thr, nullptr, gtid, 1);
   const int fin = s_count;
-  for (int i = threadIdx.x; i < k; i += kThreads) out[(size_t)y * k + i] = i < fin ? buf[i] : kEmptyKey;
+  for (int i = gtid; i < k; i += kGroupThreads) out[(size_t)y * k + i] = i < fin ? buf[i] : kEmptyKey;
 }
 
 int pow2_at_least(int x) {
@@ -361,26 +495,66 @@ int pow2_at_least(int x) {
   return p;
 }
 
+using ScanFn = void (*)(ScanParams);
+
+template <bool TOPK>
+ScanFn pick_kernel(int cpl) {
+  switch (cpl) {
+    case 1: return scan_kernel<TOPK, 1, 8>;
+    case 2: return scan_kernel<TOPK, 2, 4>;
+    case 3: return scan_kernel<TOPK, 3, 4>;
+    case 4: return scan_kernel<TOPK, 4, 2>;
+    case 6: return scan_kernel<TOPK, 6, 2>;
+    case 8: return scan_kernel<TOPK, 8, 1>;
+    case 12: return scan_kernel<TOPK, 12, 1>;
+    case 16: return scan_kernel<TOPK, 16, 1>;
+    default: return scan_kernel<TOPK, 0, 1>;
+  }
+}
+
+// Chunks per lane of the specialised kernels (0 = generic pitch).
+int specialised_cpl(int dpad) {
+  if (dpad % 128) return 0;
+  const int c = dpad / 128;
+  switch (c) {
+    case 1: case 2: case 3: case 4: case 6: case 8: case 12: case 16: return c;
+    default: return 0;
+  }
+}
+
+int rows_per_group(int cpl) { return cpl >= 8 ? 1 : cpl >= 4 ? 2 : cpl >= 2 ? 4 : 8; }
+
 }  // namespace
 
 bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g) {
   if (dpad <= 0 || dpad % 16 != 0 || dpad > kScanMaxDpad) return false;
-  // Rows per tile: a power-of-two multiple of 32 (so it divides the 256-row
-  // allocation padding) with a tile of at most 48 KB of codes.
-  int R = 32;
-  while (R < 256 && (size_t)(2 * R) * dpad <= 48 * 1024) R *= 2;
+  const int cpl = specialised_cpl(dpad);
+  int R;
+  if (cpl > 0) {
+    R = 32 * rows_per_group(cpl);
+  } else {
+    R = 32;  // generic pitch: R/32 passes of one row per quarter-warp
+    while (R < 256 && (size_t)(2 * R) * dpad <= 48 * 1024) R *= 2;
+  }
   const size_t stage = (size_t)R * (dpad + 4);
   int cap = 0;
   if (topk) {
     if (k <= 0) return false;
-    // Room for k survivors plus one full tile (scan) or one 256-key chunk
-    // (merge) of new candidates between compactions.
+    // room for k survivors plus one tile (scan) or one 256-key chunk (merge)
     cap = pow2_at_least(k + 256);
     if (cap > kScanMaxCap) return false;
   }
-  const size_t fixed = (size_t)dpad + (size_t)cap * 8 + 64;
-  int stages = 4;
-  while (stages > 2 && fixed + stages * stage > kSmemBudget) stages--;
+  const size_t fixed = (size_t)dpad + (size_t)kGroups * cap * 8;
+  // Depth: enough bytes in flight per SM without overfilling it (measured on
+  // B200: 3-4 stages of 32-48 KB sustain ~7.3 TB/s; 4 x 48 KB already drops).
+  // The stage count must be a multiple of the consumer-group count, so that
+  // stage s is only ever consumed by group s % 2, in tile order. With an odd
+  // count the two groups share a stage: bulk copies complete out of order, so a
+  // group could finish tile t+1 and then wait on tile t+3's stage while the
+  // other group's tile t (same stage) is still landing; the barrier is then one
+  // phase behind and its parity test reports "complete" for the wrong phase.
+  int stages = stage <= 36 * 1024 ? 4 : 2;
+  if (stages == 4 && fixed + stages * stage > kSmemBudget) stages = 2;
   if (fixed + stages * stage > kSmemBudget) return false;
   g->rows_per_tile = R;
   g->stages = stages;
@@ -391,45 +565,28 @@ bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g) {
 
 cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, size_t smem,
                         cudaStream_t stream) {
-  static thread_local int configured_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(scan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBudget);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(scan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBudget);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBudget);
-    if (e != cudaSuccess) return e;
-    configured_dev = dev;
-  }
-  if (G > 1024) return cudaErrorInvalidValue;
+  if (G > 512 || p.stages > kMaxStages || p.stages % kGroups != 0) return cudaErrorInvalidValue;
+  const int cpl = specialised_cpl(p.dpad);
+  if (cpl > 0 && p.rows_per_tile != 32 * rows_per_group(cpl)) return cudaErrorInvalidValue;
+  ScanFn fn = topk ? pick_kernel<true>(cpl) : pick_kernel<false>(cpl);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
+  if (e != cudaSuccess) return e;
   dim3 grid((unsigned)G, (unsigned)M);
-  if (topk)
-    scan_kernel<true><<<grid, kThreads, smem, stream>>>(p);
-  else
-    scan_kernel<false><<<grid, kThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  void* args[] = {const_cast<ScanParams*>(&p)};
+  return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, dim3(kBlockThreads), args, smem, stream);
 }
 
 cudaError_t merge_keys_launch(const uint64_t* in, int32_t nsrc, int32_t M, int32_t k, uint64_t* out,
                               cudaStream_t stream) {
   if (k <= 0 || k > kMergeMaxK || nsrc <= 0 || M <= 0) return cudaErrorInvalidValue;
-  const int cap = pow2_at_least(k + kThreads);
-  static thread_local int configured_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBudget);
-    if (e != cudaSuccess) return e;
-    configured_dev = dev;
-  }
-  merge_keys_kernel<<<M, kThreads, (size_t)cap * 8, stream>>>(in, nsrc, M, k, cap, out);
+  const int cap = pow2_at_least(k + kGroupThreads);
+  cudaError_t e = cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBudget);
+  if (e != cudaSuccess) return e;
+  merge_keys_kernel<<<M, kGroupThreads, (size_t)cap * 8, stream>>>(in, nsrc, M, k, cap, out);
   return cudaGetLastError();
 }
+
+int32_t scan_lists_per_query(int32_t G) { return kGroups * G; }
 
 }  // namespace fi8

@@ -25,8 +25,8 @@ struct ScanParams {
   int32_t cap;           // candidate buffer (power of two, >= k + R)
   unsigned long long* gthr;  // [M] shared per-query threshold key (zero at rest)
   unsigned int* counter;     // [M] CTA completion tickets (zero at rest)
-  uint64_t* part_keys;       // [M][G][k] per-CTA surviving keys
-  int32_t* part_counts;      // [M][G]
+  uint64_t* part_keys;       // [M][L][k] surviving keys per list (L = 2G)
+  int32_t* part_counts;      // [M][L]
   uint64_t* out_keys;        // [M][k] final keys, 0 = empty
   // score mode
   float* out_scores;         // [M][n]
@@ -48,8 +48,13 @@ bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g);
 cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, size_t smem,
                         cudaStream_t stream);
 
+// Survivor lists per query of a top-K scan launched with G CTAs (each CTA
+// runs two consumer groups, each with its own list).
+int32_t scan_lists_per_query(int32_t G);
 // Scratch sizes (elements) for a top-K scan over M queries with G CTAs each.
-inline size_t scan_part_keys(int32_t M, int32_t G, int32_t k) { return (size_t)M * G * k; }
+inline size_t scan_part_keys(int32_t M, int32_t G, int32_t k) {
+  return (size_t)M * scan_lists_per_query(G) * k;
+}
 
 // Merge nsrc sorted-or-unsorted key lists per query ([nsrc][M][k], 0 = empty)
 // into the top k per query ([M][k]). One CTA per query.

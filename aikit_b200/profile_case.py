@@ -1,0 +1,60 @@
+"""A small, self-contained FlatI8 workload for profilers (ncu) and timing.
+
+    python -m aikit_b200.profile_case --rows 2000000 --dim 768 --k 100 --batch 1 --reps 3
+
+Builds a synthetic mixture corpus (the bench's recipe) of --rows rows on cuda:0
+and runs --reps TopKBatch calls of --batch queries through the C ABI (device
+buffers, one stream), then prints the per-call device time. Sized so that a
+profiler capture of one launch ends in seconds while the corpus still exceeds L2.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--rows", type=int, default=2_000_000)
+    ap.add_argument("--dim", type=int, default=768)
+    ap.add_argument("--k", type=int, default=100)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--mode", choices=["topk", "score"], default="topk")
+    a = ap.parse_args()
+
+    import torch
+    from aikit_b200 import synth
+    from aikit_b200.ann import B200Backend
+
+    r = synth.Recipe(synth.MIXTURE, a.dim, seed=20260, ncl=1000, sigma=0.3)
+    bq, bs = r.codes(a.rows)
+    be = B200Backend(0)
+    ix = be.NewI8Index(bq, bs, a.rows, a.dim)
+    Q = torch.from_numpy(r.queries(a.batch)).cuda()
+    keys = torch.zeros((a.batch, a.k), dtype=torch.int64, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    times = []
+    for _ in range(a.reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if a.mode == "topk":
+            ix.topk_async(Q.data_ptr(), a.batch, a.k, keys.data_ptr(), stream.cuda_stream)
+        else:
+            dst = np.empty(a.batch * a.rows, np.float32)
+            ix.ScoreBatch(Q.cpu().numpy(), dst)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ix.sync()
+    gbs = [a.rows * (a.dim + 4) / (t * 1e-3) / 1e9 for t in times]
+    print(json.dumps({"rows": a.rows, "dim": a.dim, "k": a.k, "batch": a.batch, "ms": times,
+                      "gbs_per_pass": gbs}))
+
+
+if __name__ == "__main__":
+    main()

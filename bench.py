@@ -195,7 +195,9 @@ def main():
     nb = 8  # distinct query batches cycled through the steps
     Qh = recipe.queries(nb * BATCH).reshape(nb, BATCH, DIM)
     Qd = torch.from_numpy(Qh).cuda()
-    stream = torch.cuda.current_stream()
+    # a dedicated (non-default) stream: events, launches and NCCL all order on it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     st = stream.cuda_stream
     keys_local = torch.zeros((BATCH, K), dtype=torch.int64, device="cuda")
     gathered = torch.zeros((world, BATCH, K), dtype=torch.int64, device="cuda")

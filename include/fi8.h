@@ -86,8 +86,9 @@ int fi8_topk_max_k(fi8_index* idx, int32_t* out);
 /* Stream-ordered, device-resident form of fi8_topk_batch for callers that keep
  * queries and results in HBM (multi-GPU merge, benchmarks): d_q [M*dim] f32 and
  * d_keys [M*k] packed uint64 keys (decode with fi8_keys_unpack), both device
- * pointers; stream is a cudaStream_t (NULL = the index's own stream). Does not
- * synchronize; device-side errors surface at the next fi8_index_sync. Unlike
+ * pointers; stream is a cudaStream_t (NULL = the legacy default stream, as in
+ * CUDA). Does not synchronize; device-side errors surface at the next
+ * fi8_index_sync. Unlike
  * fi8_topk_batch it accepts k >= n (a row shard smaller than k yields all of its
  * rows, then empty keys). Calls on one index must not overlap on the GPU (they
  * share the index's scratch); issue them on one stream. */

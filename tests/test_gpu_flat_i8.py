@@ -159,10 +159,14 @@ def test_nan_and_negative_zero_scores(backend):
     gidx, gsc = ix.topk_arrays(Q, 2999)
     widx, wsc = oracle_topk(bq, bs, Q, 2999)
     assert_same(gidx.astype(np.int64), gsc, widx, wsc, "nan")
-    dst = np.empty(n, np.float32)
-    ix.Score(Q[1], dst)
-    aq, as_ = oracle.quantize_queries(Q[1:2])
-    assert dst.tobytes() == oracle.w8a8(aq, as_, bq, bs)[0].tobytes()
+    # Score output keeps amd64 NaN bits: a NaN scale propagates its payload, and
+    # an Inf query component (scale Inf, all codes 0) makes 0*Inf = 0xFFC00000.
+    Q[2, 0] = np.inf
+    for m in (1, 2):
+        dst = np.empty(n, np.float32)
+        ix.Score(Q[m], dst)
+        aq, as_ = oracle.quantize_queries(Q[m:m + 1])
+        assert dst.tobytes() == oracle.w8a8(aq, as_, bq, bs)[0].tobytes(), m
     ix.Close()
 
 
@@ -231,7 +235,9 @@ def test_row_shards_merge_equals_whole(backend):
               for lo, hi in zip(bounds[:-1], bounds[1:])]
     dq = torch.from_numpy(Q).cuda()
     keys = torch.zeros((len(shards), M, k), dtype=torch.int64, device="cuda")
-    st = torch.cuda.current_stream().cuda_stream
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    st = stream.cuda_stream
     for s, ix in enumerate(shards):  # shard 1 has a single row (< k): it yields that row
         ix.topk_async(dq.data_ptr(), M, k, keys[s].data_ptr(), st)
     out = torch.zeros((M, k), dtype=torch.int64, device="cuda")
@@ -240,6 +246,7 @@ def test_row_shards_merge_equals_whole(backend):
     for ix in shards:
         ix.sync()
     gidx, gsc = unpack_keys(out.cpu().numpy().view(np.uint64))
+    torch.cuda.set_stream(torch.cuda.default_stream())
     widx, wsc = oracle_topk(bq, bs, Q, k)
     assert_same(gidx.astype(np.int64), gsc, widx, wsc, "shards")
     for ix in shards:
