@@ -122,10 +122,12 @@ struct fi8_index {
   size_t gthr_cap = 0;
   unsigned int* d_counter = nullptr;
   size_t counter_cap = 0;
-  uint64_t* d_part = nullptr;
-  size_t part_cap = 0;
-  int32_t* d_part_counts = nullptr;
-  size_t part_counts_cap = 0;
+  unsigned int* d_counter2 = nullptr;
+  size_t counter2_cap = 0;
+  uint64_t* d_lvl1 = nullptr;
+  size_t lvl1_cap = 0;
+  uint64_t* d_lvl2 = nullptr;
+  size_t lvl2_cap = 0;
   unsigned int* d_err = nullptr;
   unsigned int* h_err = nullptr;
 
@@ -192,8 +194,9 @@ static void index_free(fi8_index* x) {
   cudaFree(x->d_scales);
   cudaFree(x->d_gthr);
   cudaFree(x->d_counter);
-  cudaFree(x->d_part);
-  cudaFree(x->d_part_counts);
+  cudaFree(x->d_counter2);
+  cudaFree(x->d_lvl1);
+  cudaFree(x->d_lvl2);
   cudaFree(x->d_err);
   cudaFree(x->d_q);
   cudaFree(x->d_keys);
@@ -288,22 +291,22 @@ int fi8_topk_max_k(fi8_index* idx, int32_t* out) {
 // internal launch helpers (caller holds idx->mu and the device)
 // ---------------------------------------------------------------------------
 
-static int ensure_topk_scratch(fi8_index* x, int32_t M, int32_t k, int32_t G, cudaStream_t st) {
+static int ensure_topk_scratch(fi8_index* x, int32_t M, int32_t kp, int32_t G, cudaStream_t st) {
   int rc;
-  const size_t old_gthr = x->gthr_cap, old_ctr = x->counter_cap;
+  const int32_t NB = scan_blocks(G);
+  const size_t old_gthr = x->gthr_cap, old_ctr = x->counter_cap, old_ctr2 = x->counter2_cap;
   if ((rc = ensure_device(&x->d_gthr, &x->gthr_cap, (size_t)M, "scratch gthr")) != FI8_OK) return rc;
-  if ((rc = ensure_device(&x->d_counter, &x->counter_cap, (size_t)M, "scratch counter")) != FI8_OK) return rc;
-  if (x->gthr_cap != old_gthr || x->counter_cap != old_ctr) {
-    // Fresh (or regrown) per-query state must start at zero; the kernel's last
-    // CTA returns it to zero after every launch.
-    // (on the launch stream, so the kernel that uses it is ordered after it).
+  if ((rc = ensure_device(&x->d_counter, &x->counter_cap, (size_t)M * NB, "scratch counter")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_counter2, &x->counter2_cap, (size_t)M, "scratch counter2")) != FI8_OK) return rc;
+  if (x->gthr_cap != old_gthr || x->counter_cap != old_ctr || x->counter2_cap != old_ctr2) {
+    // Fresh (or regrown) per-query state must start at zero, ordered before the
+    // kernel on its stream; the kernel returns it to zero after every launch.
     FI8_CUDA(cudaMemsetAsync(x->d_gthr, 0, x->gthr_cap * sizeof(unsigned long long), st), "memset gthr");
     FI8_CUDA(cudaMemsetAsync(x->d_counter, 0, x->counter_cap * sizeof(unsigned int), st), "memset counter");
+    FI8_CUDA(cudaMemsetAsync(x->d_counter2, 0, x->counter2_cap * sizeof(unsigned int), st), "memset counter2");
   }
-  if ((rc = ensure_device(&x->d_part, &x->part_cap, scan_part_keys(M, G, k), "scratch part")) != FI8_OK) return rc;
-  if ((rc = ensure_device(&x->d_part_counts, &x->part_counts_cap, (size_t)M * scan_lists_per_query(G),
-                          "scratch counts")) != FI8_OK)
-    return rc;
+  if ((rc = ensure_device(&x->d_lvl1, &x->lvl1_cap, (size_t)M * G * kp, "scratch lvl1")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_lvl2, &x->lvl2_cap, (size_t)M * NB * kp, "scratch lvl2")) != FI8_OK) return rc;
   return FI8_OK;
 }
 
@@ -318,6 +321,7 @@ static ScanParams base_params(fi8_index* x, const ScanGeometry& geo) {
   p.stages = geo.stages;
   p.ntiles = x->n_alloc / geo.rows_per_tile;
   p.id_base = x->id_base;
+  p.smem_bytes = (int32_t)geo.smem_bytes;
   p.err = x->d_err;
   return p;
 }
@@ -335,19 +339,21 @@ static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uin
   ScanParams p = base_params(x, geo);
   const int32_t G = grid_ctas(x, p);
   const int32_t Mc = std::min(M, kScanMaxM);
-  int rc = ensure_topk_scratch(x, Mc, k, G, st);
+  int rc = ensure_topk_scratch(x, Mc, geo.kp, G, st);
   if (rc != FI8_OK) return rc;
   p.k = k;
+  p.kp = geo.kp;
   p.cap = geo.cap;
   p.gthr = x->d_gthr;
   p.counter = x->d_counter;
-  p.part_keys = x->d_part;
-  p.part_counts = x->d_part_counts;
+  p.counter2 = x->d_counter2;
+  p.lvl1 = x->d_lvl1;
+  p.lvl2 = x->d_lvl2;
   for (int32_t m0 = 0; m0 < M; m0 += Mc) {
     const int32_t mm = std::min(Mc, M - m0);
     p.q = d_q + (size_t)m0 * x->dim;
     p.out_keys = d_keys + (size_t)m0 * k;
-    cudaError_t e = scan_launch(p, true, mm, G, geo.smem_bytes, st);
+    cudaError_t e = scan_launch(p, true, mm, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(topk)");
   }
   return FI8_OK;
@@ -362,7 +368,7 @@ static int launch_scores(fi8_index* x, const float* d_q, int32_t M, float* d_sco
     const int32_t mm = std::min(kScanMaxM, M - m0);
     p.q = d_q + (size_t)m0 * x->dim;
     p.out_scores = d_scores + (size_t)m0 * x->n;
-    cudaError_t e = scan_launch(p, false, mm, G, geo.smem_bytes, st);
+    cudaError_t e = scan_launch(p, false, mm, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(score)");
   }
   return FI8_OK;

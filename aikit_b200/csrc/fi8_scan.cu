@@ -12,17 +12,20 @@
 //     cp.async.bulk; a "full" mbarrier per stage counts the bytes, an "empty"
 //     mbarrier per stage counts the consumer warps that are done with it;
 //   * warps 0-15 (two consumer groups of 8 warps): group g takes the CTA's
-//     tiles g, g+2, g+4, ... Each 8-lane quarter-warp owns RPG rows of a tile,
-//     holds its query chunks in registers (the query is quantized in shared
-//     memory first, bit-identical to quantizeRowInt8) and dots 16-byte row
-//     chunks with dp4a; a transpose-reduce leaves one full row sum per lane;
+//     tiles g, g+2, g+4, ... (stage s always belongs to group s % 2). Each
+//     8-lane quarter-warp owns RPG rows of a tile, holds its query chunks in
+//     registers (the query is quantized in shared memory first, bit-identical
+//     to quantizeRowInt8) and dots 16-byte row chunks with dp4a; a
+//     transpose-reduce leaves one complete row sum per owner lane;
 //   * top-K per group: candidates above the group threshold are appended to a
 //     shared buffer; when it fills, a bitonic sort keeps the best k and raises
 //     the threshold, which is also published to a per-query global threshold
 //     (atomicMax) read back every tile. Every threshold is the k-th best key of
 //     k real rows, so nothing that can reach the global top-k is dropped;
-//   * the last CTA to finish (ticket counter) merges the per-group survivor
-//     lists, writes the final sorted keys and resets the per-query scratch.
+//   * merge: each CTA merges its two groups' sorted top-k lists; the last CTA
+//     of every block of 8 CTAs (ticket counter) merges the block's lists; the
+//     last block merges the block lists and writes the final sorted keys. All
+//     merges are "top-k of two sorted lists" bitonic networks in shared memory.
 #include "fi8_device.cuh"
 #include "fi8_scan.cuh"
 
@@ -35,7 +38,7 @@ constexpr int kGroups = 2;
 constexpr int kConsumerThreads = kGroups * kGroupThreads;
 constexpr int kBlockThreads = kConsumerThreads + 32;  // + producer warp
 constexpr int kConsumerWarps = kConsumerThreads / 32;
-constexpr int kMaxStages = 4;
+constexpr int kMaxStages = 8;
 constexpr size_t kSmemBudget = 220 * 1024;
 constexpr int kBarConsumers = 3;  // named barrier over the 512 consumer threads
 
@@ -110,25 +113,65 @@ __device__ void group_compact(uint64_t* buf, int cnt, int k, int* s_count, unsig
   named_sync(bar, kGroupThreads);
 }
 
-// Number of leading keys >= T in a descending buffer of n keys.
-__device__ int prefix_at_least(const uint64_t* buf, int n, unsigned long long T) {
-  int lo = 0, hi = n;  // buf[0..lo) >= T, buf[hi..n) < T
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (buf[mid] >= T) lo = mid + 1;
-    else hi = mid;
+// Tree-merge `total` sorted (descending) lists of kp keys held in slots
+// [0, total) into slot 0. Each pairwise step keeps the top kp of two sorted
+// lists: c[i] = max(a[i], b[kp-1-i]) is bitonic and holds exactly that top kp,
+// and a bitonic merge sorts it. All pairs of a level advance together.
+__device__ void tree_merge_slots(uint64_t* slots, int total, int kp, int gtid, int bar) {
+  for (int step = 1; step < total; step <<= 1) {
+    const int npairs = (total - step + 2 * step - 1) / (2 * step);
+    for (int w = gtid; w < npairs * kp; w += kGroupThreads) {
+      const int j = (w / kp) * 2 * step, i = w % kp;
+      const uint64_t a = slots[(size_t)j * kp + i];
+      const uint64_t b = slots[(size_t)(j + step) * kp + (kp - 1 - i)];
+      slots[(size_t)j * kp + i] = a > b ? a : b;
+    }
+    named_sync(bar, kGroupThreads);
+    for (int stride = kp >> 1; stride > 0; stride >>= 1) {
+      for (int w = gtid; w < npairs * (kp >> 1); w += kGroupThreads) {
+        const int j = (w / (kp >> 1)) * 2 * step, i = w % (kp >> 1);
+        uint64_t* s = slots + (size_t)j * kp;
+        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int hi = lo + stride;
+        const uint64_t a = s[lo], b = s[hi];
+        if (a < b) {
+          s[lo] = b;
+          s[hi] = a;
+        }
+      }
+      named_sync(bar, kGroupThreads);
+    }
   }
-  return lo;
 }
 
-template <int RPG>
-struct RowsLog2 {
-  static constexpr int v = RPG == 1 ? 0 : RPG == 2 ? 1 : RPG == 4 ? 2 : 3;
-};
+// Top kp of m global lists (each `len` <= kp keys, stride `stride` keys apart,
+// sorted descending, 0 = empty) into slots[0..kp). Uses as many shared slots
+// as fit; slot 0 carries the running result between rounds.
+__device__ void merge_global_lists(const uint64_t* lists, int m, int len, size_t stride, int kp,
+                                   uint64_t* slots, int nslots, int gtid, int bar) {
+  int done = 0;
+  bool have = false;
+  if (m == 0) {
+    for (int i = gtid; i < kp; i += kGroupThreads) slots[i] = kEmptyKey;
+    named_sync(bar, kGroupThreads);
+    return;
+  }
+  while (done < m) {
+    const int base = have ? 1 : 0;
+    const int c = min(nslots - base, m - done);
+    for (int w = gtid; w < c * kp; w += kGroupThreads) {
+      const int l = w / kp, i = w % kp;
+      slots[(size_t)(base + l) * kp + i] = i < len ? __ldcg(lists + (size_t)(done + l) * stride + i) : kEmptyKey;
+    }
+    named_sync(bar, kGroupThreads);
+    tree_merge_slots(slots, base + c, kp, gtid, bar);
+    done += c;
+    have = true;
+  }
+}
 
 // CPL: 16-byte chunks per lane per row (dpad = 128*CPL), 0 = generic pitch.
-// RPG: rows per 8-lane quarter-warp per tile (tile rows R = 32*RPG); the
-// generic kernel uses RPG=1 and R/32 passes.
+// RPG: rows per 8-lane quarter-warp per pass; a tile is R = 32*RPG*passes rows.
 template <bool TOPK, int CPL, int RPG>
 __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -139,12 +182,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
   __shared__ int s_count[kGroups];
   __shared__ unsigned long long s_thr[kGroups];
   __shared__ unsigned long long s_local_thr[kGroups];
-  __shared__ unsigned long long s_T;
   __shared__ volatile int s_abort;
   __shared__ int s_gabort[kGroups];
   __shared__ int s_last;
-  __shared__ int s_off[1025];
 
+  constexpr int LOGR = RPG == 1 ? 0 : RPG == 2 ? 1 : RPG == 4 ? 2 : 3;
   const int G = gridDim.x;
   const int cta = blockIdx.x;
   const int y = blockIdx.y;
@@ -170,7 +212,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
     }
     fence_mbar_init();
     s_abort = 0;
-    s_T = 0;
     for (int g = 0; g < kGroups; g++) {
       s_count[g] = 0;
       s_local_thr[g] = 0;
@@ -240,12 +281,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
 
     const int lane8 = lane & 7;
     const int lg = lane >> 3;
-    constexpr int LOGR = RowsLog2<RPG>::v;
     int4 qreg[CPL > 0 ? CPL : 1];
 #pragma unroll
     for (int j = 0; j < (CPL > 0 ? CPL : 1); j++)
       if (CPL > 0) qreg[j] = reinterpret_cast<const int4*>(q_s)[lane8 + 8 * j];
 
+    const int rows_per_pass = 32 * RPG;
+    const int passes = R / rows_per_pass;
     for (int64_t it = g; it < my_tiles; it += kGroups) {
       const int s = (int)(it % S);
       if (!mbar_wait_bounded(&s_full[s], (uint32_t)((it / S) & 1))) {
@@ -259,10 +301,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
       unsigned long long gt_prefetch = 0ull;
       if (TOPK && gtid == 0) gt_prefetch = ld_relaxed_u64(p.gthr + y);
 
-      const int passes = (CPL > 0) ? 1 : R / 32;
       for (int pass = 0; pass < passes; pass++) {
         // rows of this quarter-warp: base .. base + RPG - 1
-        const int base = pass * 32 + gwarp * (4 * RPG) + lg * RPG;
+        const int base = pass * rows_per_pass + gwarp * (4 * RPG) + lg * RPG;
         int vals[RPG];
         if (CPL > 0) {
           int acc[RPG][2];
@@ -363,148 +404,100 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
     if (TOPK) {
       named_sync(bar, kGroupThreads);
       group_compact(buf, s_count[g], p.k, &s_count[g], &s_local_thr[g], p.gthr + y, gtid, bar);
+      // the group's list: its best keys, sorted, empty-padded to kp
+      for (int i = s_count[g] + gtid; i < p.kp; i += kGroupThreads) buf[i] = kEmptyKey;
     }
   }
 
   if (!TOPK) return;
   __syncthreads();  // both groups (and the producer) are done
-
-  // ---- per-group results: best k with key >= the shared threshold ----
-  if (tid == 0) s_T = ld_relaxed_u64(p.gthr + y);
-  __syncthreads();
-  const int L = kGroups * G;  // survivor lists for this query
-  if (warp < kConsumerWarps) {
-    const int g = warp / (kGroupThreads / 32);
-    const int gtid = tid - g * kGroupThreads;
-    const uint64_t* buf = bufs + (size_t)g * p.cap;
-    const int have = s_count[g];
-    const int keep = prefix_at_least(buf, have, s_T);
-    uint64_t* mine = p.part_keys + ((size_t)y * L + (size_t)cta * kGroups + g) * p.k;
-    for (int i = gtid; i < keep; i += kGroupThreads) mine[i] = buf[i];
-    if (gtid == 0) p.part_counts[(size_t)y * L + cta * kGroups + g] = keep;
+  const int kp = p.kp;
+  const int NB = (G + kMergeBlock - 1) / kMergeBlock;
+  if (warp < kGroupThreads / 32) {
+    // group 0 merges the two group lists of this CTA. They sit cap keys apart;
+    // group 1's list moves next to group 0's (kp <= cap/2 unless kp == cap, in
+    // which case the copy is in place, so source and target never overlap).
+    for (int i = tid; i < kp; i += kGroupThreads) bufs[kp + i] = bufs[(size_t)p.cap + i];
+    named_sync(1, kGroupThreads);
+    tree_merge_slots(bufs, 2, kp, tid, 1);
+    uint64_t* mine = p.lvl1 + ((size_t)y * G + cta) * kp;
+    for (int i = tid; i < kp; i += kGroupThreads) mine[i] = bufs[i];
+    __threadfence();
   }
-  __threadfence();
   __syncthreads();
+  const int blk = cta / kMergeBlock;
+  const int members = min(kMergeBlock, G - blk * kMergeBlock);
   if (tid == 0) {
-    const unsigned int ticket = atomicAdd(p.counter + y, 1u);
-    s_last = (ticket == (unsigned int)(G - 1)) ? 1 : 0;
+    const unsigned int ticket = atomicAdd(p.counter + (size_t)y * NB + blk, 1u);
+    s_last = (ticket == (unsigned int)(members - 1)) ? 1 : 0;
   }
   __syncthreads();
-  if (!s_last || tid >= kGroupThreads) return;
+  if (!s_last || warp >= kGroupThreads / 32) return;
 
-  // ---- last CTA, group 0: merge the L survivor lists for query y ----
+  // ---- last CTA of the block: merge the block's CTA lists ----
   __threadfence();
-  const int gtid = tid;
-  const int bar = 1;
-  uint64_t* buf = bufs;
-  if (gtid == 0) {
-    s_T = ld_relaxed_u64(p.gthr + y);
-    s_count[0] = 0;
-    s_local_thr[0] = 0;
+  const int nslots = p.smem_bytes / (kp * 8);
+  uint64_t* slots = reinterpret_cast<uint64_t*>(smem);
+  merge_global_lists(p.lvl1 + ((size_t)y * G + (size_t)blk * kMergeBlock) * kp, members, kp, kp, kp, slots,
+                     nslots, tid, 1);
+  uint64_t* blist = p.lvl2 + ((size_t)y * NB + blk) * kp;
+  for (int i = tid; i < kp; i += kGroupThreads) blist[i] = slots[i];
+  if (tid == 0) p.counter[(size_t)y * NB + blk] = 0u;  // every member has taken its ticket
+  __threadfence();
+  named_sync(1, kGroupThreads);
+  if (tid == 0) {
+    const unsigned int ticket = atomicAdd(p.counter2 + y, 1u);
+    s_last = (ticket == (unsigned int)(NB - 1)) ? 1 : 0;
   }
-  if (warp == 0) {  // exclusive prefix of the L counts
-    int run = 0;
-    for (int b = 0; b < L; b += 32) {
-      const int i = b + lane;
-      const int v = (i < L) ? __ldcg(p.part_counts + (size_t)y * L + i) : 0;
-      int x = v;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, x, off);
-        if (lane >= off) x += t;
-      }
-      if (i < L) s_off[i] = run + x - v;
-      run += __shfl_sync(0xffffffffu, x, 31);
-    }
-    if (lane == 0) s_off[L] = run;
-  }
-  named_sync(bar, kGroupThreads);
-  const int total = s_off[L];
-  const unsigned long long Tf = s_T;
-  for (int b0 = 0; b0 < total; b0 += kGroupThreads) {
-    const int e = b0 + gtid;
-    bool take = false;
-    uint64_t key = kEmptyKey;
-    if (e < total) {
-      int lo = 0, hi = L;  // list l with s_off[l] <= e < s_off[l+1]
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (s_off[mid] <= e) lo = mid;
-        else hi = mid;
-      }
-      key = __ldcg(p.part_keys + ((size_t)y * L + lo) * p.k + (e - s_off[lo]));
-      take = key >= Tf && key > s_local_thr[0];
-    }
-    warp_append(take, key, buf, &s_count[0]);
-    named_sync(bar, kGroupThreads);
-    const int cnt = s_count[0];
-    if (cnt > p.cap - kGroupThreads) group_compact(buf, cnt, p.k, &s_count[0], &s_local_thr[0], nullptr, gtid, bar);
-  }
-  named_sync(bar, kGroupThreads);
-  group_compact(buf, s_count[0], p.k, &s_count[0], &s_local_thr[0], nullptr, gtid, bar);
-  const int fin = s_count[0];
-  for (int i = gtid; i < p.k; i += kGroupThreads) p.out_keys[(size_t)y * p.k + i] = i < fin ? buf[i] : kEmptyKey;
-  if (gtid == 0) {
-    p.counter[y] = 0u;
+  named_sync(1, kGroupThreads);
+  if (!s_last) return;
+
+  // ---- last block: merge the block lists, write the final keys ----
+  __threadfence();
+  merge_global_lists(p.lvl2 + (size_t)y * NB * kp, NB, kp, kp, kp, slots, nslots, tid, 1);
+  for (int i = tid; i < p.k; i += kGroupThreads) p.out_keys[(size_t)y * p.k + i] = slots[i];
+  if (tid == 0) {
+    p.counter2[y] = 0u;
     p.gthr[y] = 0ull;
   }
 }
 
 // ---------------------------------------------------------------------------
-// merge_keys_kernel: top-k of nsrc candidate lists per query, one CTA each.
-// Used for the cross-GPU merge after the all-gather (the N-way analogue of
+// merge_keys_kernel: top-k of nsrc sorted candidate lists per query, one CTA
+// each. The cross-GPU merge after the all-gather (the N-way analogue of
 // queryBatchSharded's merge, ann/backend.go:262-277).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kGroupThreads, 1)
-    merge_keys_kernel(const uint64_t* in, int nsrc, int M, int k, int cap, uint64_t* out) {
+    merge_keys_kernel(const uint64_t* in, int nsrc, int M, int k, int kp, int nslots, uint64_t* out) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ int s_count;
-  __shared__ unsigned long long s_local_thr;
-  uint64_t* buf = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* slots = reinterpret_cast<uint64_t*>(smem);
   const int y = blockIdx.x;
-  const int gtid = threadIdx.x;
-  if (gtid == 0) {
-    s_count = 0;
-    s_local_thr = 0;
-  }
-  named_sync(1, kGroupThreads);
-  const int total = nsrc * k;
-  for (int b0 = 0; b0 < total; b0 += kGroupThreads) {
-    const int e = b0 + gtid;
-    bool take = false;
-    uint64_t key = kEmptyKey;
-    if (e < total) {
-      const int src = e / k, j = e - src * k;
-      key = in[((size_t)src * M + y) * k + j];
-      take = key != kEmptyKey && key > s_local_thr;
-    }
-    warp_append(take, key, buf, &s_count);
-    named_sync(1, kGroupThreads);
-    const int cnt = s_count;
-    if (cnt > cap - kGroupThreads) group_compact(buf, cnt, k, &s_count, &s_local_thr, nullptr, gtid, 1);
-  }
-  named_sync(1, kGroupThreads);
-  group_compact(buf, s_count, k, &s_count, &s_local_thr, nullptr, gtid, 1);
-  const int fin = s_count;
-  for (int i = gtid; i < k; i += kGroupThreads) out[(size_t)y * k + i] = i < fin ? buf[i] : kEmptyKey;
+  merge_global_lists(in + (size_t)y * k, nsrc, k, (size_t)M * k, kp, slots, nslots, threadIdx.x, 1);
+  for (int i = threadIdx.x; i < k; i += kGroupThreads) out[(size_t)y * k + i] = slots[i];
 }
 
 int pow2_at_least(int x) {
-  int p = 2;
+  int p = 1;
   while (p < x) p <<= 1;
   return p;
 }
 
 using ScanFn = void (*)(ScanParams);
 
+// (CPL, RPG) pairs with a specialised kernel; RPG keeps a pass near 24-32 KB.
+struct Shape {
+  int cpl, rpg;
+};
+constexpr Shape kShapes[] = {{1, 8}, {2, 4}, {3, 2}, {4, 2}, {6, 1}, {8, 1}, {12, 1}, {16, 1}};
+
 template <bool TOPK>
 ScanFn pick_kernel(int cpl) {
   switch (cpl) {
     case 1: return scan_kernel<TOPK, 1, 8>;
     case 2: return scan_kernel<TOPK, 2, 4>;
-    case 3: return scan_kernel<TOPK, 3, 4>;
+    case 3: return scan_kernel<TOPK, 3, 2>;
     case 4: return scan_kernel<TOPK, 4, 2>;
-    case 6: return scan_kernel<TOPK, 6, 2>;
+    case 6: return scan_kernel<TOPK, 6, 1>;
     case 8: return scan_kernel<TOPK, 8, 1>;
     case 12: return scan_kernel<TOPK, 12, 1>;
     case 16: return scan_kernel<TOPK, 16, 1>;
@@ -512,81 +505,84 @@ ScanFn pick_kernel(int cpl) {
   }
 }
 
-// Chunks per lane of the specialised kernels (0 = generic pitch).
-int specialised_cpl(int dpad) {
-  if (dpad % 128) return 0;
-  const int c = dpad / 128;
-  switch (c) {
-    case 1: case 2: case 3: case 4: case 6: case 8: case 12: case 16: return c;
-    default: return 0;
-  }
+int rows_per_group(int dpad, int* cpl_out) {
+  *cpl_out = 0;
+  if (dpad % 128 == 0)
+    for (const Shape& s : kShapes)
+      if (s.cpl * 128 == dpad) {
+        *cpl_out = s.cpl;
+        return s.rpg;
+      }
+  return 1;
 }
-
-int rows_per_group(int cpl) { return cpl >= 8 ? 1 : cpl >= 4 ? 2 : cpl >= 2 ? 4 : 8; }
 
 }  // namespace
 
 bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g) {
   if (dpad <= 0 || dpad % 16 != 0 || dpad > kScanMaxDpad) return false;
-  const int cpl = specialised_cpl(dpad);
-  int R;
-  if (cpl > 0) {
-    R = 32 * rows_per_group(cpl);
-  } else {
-    R = 32;  // generic pitch: R/32 passes of one row per quarter-warp
-    while (R < 256 && (size_t)(2 * R) * dpad <= 48 * 1024) R *= 2;
-  }
+  int cpl = 0;
+  const int rpg = rows_per_group(dpad, &cpl);
+  // Tile: one pass of 32*RPG rows, doubled (more passes) while it stays at or
+  // under 32 KB; at most 256 rows so it divides the allocation padding.
+  int R = 32 * rpg;
+  while (R < 256 && (size_t)(2 * R) * dpad <= 32 * 1024) R *= 2;
   const size_t stage = (size_t)R * (dpad + 4);
-  int cap = 0;
+  int cap = 0, kp = 0;
   if (topk) {
     if (k <= 0) return false;
-    // room for k survivors plus one tile (scan) or one 256-key chunk (merge)
+    // room for k survivors plus one tile of new candidates between compactions
     cap = pow2_at_least(k + 256);
+    kp = pow2_at_least(k);
     if (cap > kScanMaxCap) return false;
   }
   const size_t fixed = (size_t)dpad + (size_t)kGroups * cap * 8;
-  // Depth: enough bytes in flight per SM without overfilling it (measured on
-  // B200: 3-4 stages of 32-48 KB sustain ~7.3 TB/s; 4 x 48 KB already drops).
-  // The stage count must be a multiple of the consumer-group count, so that
-  // stage s is only ever consumed by group s % 2, in tile order. With an odd
-  // count the two groups share a stage: bulk copies complete out of order, so a
-  // group could finish tile t+1 and then wait on tile t+3's stage while the
-  // other group's tile t (same stage) is still landing; the barrier is then one
-  // phase behind and its parity test reports "complete" for the wrong phase.
-  int stages = stage <= 36 * 1024 ? 4 : 2;
-  if (stages == 4 && fixed + stages * stage > kSmemBudget) stages = 2;
+  // Ring depth: an even count (stage s always belongs to consumer group s % 2;
+  // with an odd count the groups would share stages, and because bulk copies
+  // complete out of order a parity wait could then observe the wrong phase),
+  // at least two stages per group when they fit, and about 100-160 KB in
+  // flight per SM (B200 measurement: 3-4 x 32-48 KB sustain ~7.3 TB/s with one
+  // CTA per SM; 4 x 48 KB already drops).
+  int stages = 2;
+  while (stages + 2 <= kMaxStages && (stages + 2) * stage <= 160 * 1024 && fixed + (stages + 2) * stage <= kSmemBudget)
+    stages += 2;
   if (fixed + stages * stage > kSmemBudget) return false;
   g->rows_per_tile = R;
   g->stages = stages;
   g->cap = cap;
+  g->kp = kp;
   g->smem_bytes = fixed + stages * stage;
+  // the merges reuse the dynamic shared memory for lists of kp keys: at least
+  // two must fit
+  if (topk && g->smem_bytes < (size_t)2 * kp * 8) g->smem_bytes = (size_t)2 * kp * 8;
   return true;
 }
 
-cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, size_t smem,
-                        cudaStream_t stream) {
-  if (G > 512 || p.stages > kMaxStages || p.stages % kGroups != 0) return cudaErrorInvalidValue;
-  const int cpl = specialised_cpl(p.dpad);
-  if (cpl > 0 && p.rows_per_tile != 32 * rows_per_group(cpl)) return cudaErrorInvalidValue;
+cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cudaStream_t stream) {
+  if (p.stages > kMaxStages || p.stages % kGroups != 0 || p.stages < 2) return cudaErrorInvalidValue;
+  int cpl = 0;
+  const int rpg = rows_per_group(p.dpad, &cpl);
+  if (p.rows_per_tile % (32 * rpg) != 0) return cudaErrorInvalidValue;
   ScanFn fn = topk ? pick_kernel<true>(cpl) : pick_kernel<false>(cpl);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)G, (unsigned)M);
   void* args[] = {const_cast<ScanParams*>(&p)};
-  return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, dim3(kBlockThreads), args, smem, stream);
+  return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, dim3(kBlockThreads), args,
+                          (size_t)p.smem_bytes, stream);
 }
 
 cudaError_t merge_keys_launch(const uint64_t* in, int32_t nsrc, int32_t M, int32_t k, uint64_t* out,
                               cudaStream_t stream) {
   if (k <= 0 || k > kMergeMaxK || nsrc <= 0 || M <= 0) return cudaErrorInvalidValue;
-  const int cap = pow2_at_least(k + kGroupThreads);
+  const int kp = pow2_at_least(k);
+  int nslots = (int)(kSmemBudget / ((size_t)kp * 8));
+  if (nslots > nsrc + 1) nslots = nsrc + 1;
+  if (nslots < 2) nslots = 2;
   cudaError_t e = cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBudget);
   if (e != cudaSuccess) return e;
-  merge_keys_kernel<<<M, kGroupThreads, (size_t)cap * 8, stream>>>(in, nsrc, M, k, cap, out);
+  merge_keys_kernel<<<M, kGroupThreads, (size_t)nslots * kp * 8, stream>>>(in, nsrc, M, k, kp, nslots, out);
   return cudaGetLastError();
 }
-
-int32_t scan_lists_per_query(int32_t G) { return kGroups * G; }
 
 }  // namespace fi8

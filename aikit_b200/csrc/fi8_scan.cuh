@@ -15,18 +15,21 @@ struct ScanParams {
   int64_t n;             // real rows
   int32_t d;             // query length (reference dim)
   int32_t dpad;          // row pitch in bytes, multiple of 16
-  int32_t rows_per_tile; // R, multiple of 32, divides 256
-  int32_t stages;        // bulk-copy pipeline depth
+  int32_t rows_per_tile; // R, power of two in [32, 256]
+  int32_t stages;        // bulk-copy ring depth (even)
   int64_t ntiles;        // n_alloc / R
   const float* q;        // [M][d] f32 queries
   uint32_t id_base;      // global id of row 0 (row sharding)
+  int32_t smem_bytes;    // dynamic shared memory of the launch
   // top-K mode
   int32_t k;
-  int32_t cap;           // candidate buffer (power of two, >= k + R)
+  int32_t kp;            // k rounded up to a power of two: length of every list
+  int32_t cap;           // per-group candidate buffer (power of two, >= k + 256)
   unsigned long long* gthr;  // [M] shared per-query threshold key (zero at rest)
-  unsigned int* counter;     // [M] CTA completion tickets (zero at rest)
-  uint64_t* part_keys;       // [M][L][k] surviving keys per list (L = 2G)
-  int32_t* part_counts;      // [M][L]
+  unsigned int* counter;     // [M][NB] per-block CTA tickets (zero at rest)
+  unsigned int* counter2;    // [M] block tickets (zero at rest)
+  uint64_t* lvl1;            // [M][G][kp] per-CTA top-kp lists
+  uint64_t* lvl2;            // [M][NB][kp] per-block top-kp lists
   uint64_t* out_keys;        // [M][k] final keys, 0 = empty
   // score mode
   float* out_scores;         // [M][n]
@@ -37,27 +40,23 @@ struct ScanGeometry {
   int32_t rows_per_tile;
   int32_t stages;
   int32_t cap;
+  int32_t kp;
   size_t smem_bytes;
 };
 
-// Largest supported row pitch and top-K for the scan kernels.
+// Largest supported row pitch and candidate buffer for the scan kernels.
 constexpr int32_t kScanMaxDpad = 2048;
 constexpr int32_t kScanMaxCap = 4096;
+// CTAs whose lists one first-level merge combines.
+constexpr int32_t kMergeBlock = 8;
 
 bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g);
-cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, size_t smem,
-                        cudaStream_t stream);
+cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cudaStream_t stream);
 
-// Survivor lists per query of a top-K scan launched with G CTAs (each CTA
-// runs two consumer groups, each with its own list).
-int32_t scan_lists_per_query(int32_t G);
-// Scratch sizes (elements) for a top-K scan over M queries with G CTAs each.
-inline size_t scan_part_keys(int32_t M, int32_t G, int32_t k) {
-  return (size_t)M * scan_lists_per_query(G) * k;
-}
+inline int32_t scan_blocks(int32_t G) { return (G + kMergeBlock - 1) / kMergeBlock; }
 
-// Merge nsrc sorted-or-unsorted key lists per query ([nsrc][M][k], 0 = empty)
-// into the top k per query ([M][k]). One CTA per query.
+// Merge nsrc key lists per query ([nsrc][M][k], each sorted descending, 0 =
+// empty) into the top k per query ([M][k]). One CTA per query.
 cudaError_t merge_keys_launch(const uint64_t* in, int32_t nsrc, int32_t M, int32_t k,
                               uint64_t* out, cudaStream_t stream);
 constexpr int32_t kMergeMaxK = 2048;
