@@ -14,6 +14,8 @@ FI8_ERR_CUDA = 3
 FI8_ERR_OOM = 4
 FI8_ERR_DEVICE = 5
 
+FI8_OPT_GEMM_MIN_BATCH = 1
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _I64 = C.c_int64
@@ -33,6 +35,8 @@ SIGNATURES = {
     "fi8_topk_batch": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
     "fi8_topk_max_k": (C.c_int, [_P, _P]),
     "fi8_topk_batch_async": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
+    "fi8_index_set_option": (C.c_int, [_P, C.c_int, _I64]),
+    "fi8_index_last_launch_count": (C.c_int, [_P, _P]),
     "fi8_index_sync": (C.c_int, [_P]),
     "fi8_keys_unpack": (C.c_int, [_P, _I64, _P, _P]),
     "fi8_merge_keys_async": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P]),

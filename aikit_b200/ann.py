@@ -177,6 +177,16 @@ class I8Index:
     def sync(self) -> None:
         check(lib().fi8_index_sync(self._h))
 
+    def last_launch_count(self) -> int:
+        v = C.c_int32(0)
+        check(lib().fi8_index_last_launch_count(self._h, C.byref(v)))
+        return v.value
+
+    def set_gemm_min_batch(self, m: int) -> None:
+        """Batches of at least m queries use the tensor-core GEMM path."""
+        from ._ffi import FI8_OPT_GEMM_MIN_BATCH
+        check(lib().fi8_index_set_option(self._h, FI8_OPT_GEMM_MIN_BATCH, m))
+
     def _queries(self, queries) -> np.ndarray:
         if isinstance(queries, np.ndarray) and queries.ndim == 2:
             Q = _f32(queries)

@@ -16,9 +16,11 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/fi8.h"
 #include "fi8_device.cuh"
+#include "fi8_gemm.cuh"
 #include "fi8_scan.cuh"
 
 using namespace fi8;
@@ -140,6 +142,27 @@ struct fi8_index {
   size_t d_scores_cap = 0;
   uint64_t* h_keys = nullptr;
   size_t h_keys_cap = 0;
+
+  // batched (tcgen05 GEMM) path
+  CUtensorMap tmB;       // corpus codes [n_alloc][dpad], 256-row boxes
+  bool has_tmB = false;
+  int8_t* d_A = nullptr;  // quantized queries [Mpad][dpad]
+  size_t A_cap = 0;
+  CUtensorMap tmA;       // over d_A, rebuilt when d_A moves
+  const int8_t* tmA_base = nullptr;
+  int64_t tmA_rows = 0;
+  float* d_qscale = nullptr;
+  size_t qscale_cap = 0;
+  unsigned long long* d_thr = nullptr;
+  size_t thr_cap = 0;
+  unsigned int* d_cnt = nullptr;
+  size_t cnt_cap = 0;
+  uint64_t* d_cand = nullptr;
+  size_t cand_cap = 0;
+  uint64_t* d_topk = nullptr;
+  size_t topk_cap = 0;
+  int32_t gemm_min_batch = 2;  // batches of at least this many queries use the GEMM path
+  int32_t last_launches = 0;   // kernels launched by the last query call
 };
 
 extern "C" {
@@ -201,6 +224,12 @@ static void index_free(fi8_index* x) {
   cudaFree(x->d_q);
   cudaFree(x->d_keys);
   cudaFree(x->d_scores);
+  cudaFree(x->d_A);
+  cudaFree(x->d_qscale);
+  cudaFree(x->d_thr);
+  cudaFree(x->d_cnt);
+  cudaFree(x->d_cand);
+  cudaFree(x->d_topk);
   if (x->h_keys) cudaFreeHost(x->h_keys);
   if (x->h_err) cudaFreeHost(x->h_err);
   if (x->stream) cudaStreamDestroy(x->stream);
@@ -254,6 +283,7 @@ int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int
     index_free(x);
     return rc;
   }
+  x->has_tmB = make_tmap_i8(&x->tmB, x->d_codes, (uint64_t)x->n_alloc, (uint64_t)dpad, (uint32_t)kGemmBN);
   *out = x;
   return FI8_OK;
 }
@@ -331,8 +361,8 @@ static int32_t grid_ctas(fi8_index* x, const ScanParams& p) {
   return (int32_t)std::max<int64_t>(G, 1);
 }
 
-static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
-                       cudaStream_t st) {
+static int launch_topk_scan(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                            cudaStream_t st) {
   ScanGeometry geo;
   if (!scan_geometry(x->dpad, k, true, &geo))
     return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d beyond the device top-K)", k);
@@ -355,8 +385,98 @@ static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uin
     p.out_keys = d_keys + (size_t)m0 * k;
     cudaError_t e = scan_launch(p, true, mm, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(topk)");
+    x->last_launches++;
   }
   return FI8_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Batched path: quantize the batch, then for each row range one tcgen05 GEMM
+// (threshold-filter epilogue) and one per-query select.
+// ---------------------------------------------------------------------------
+static int32_t pow2_ge_host(int64_t x) {
+  int32_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles.
+static void plan_ranges(int64_t n, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
+  const int64_t F = std::max<int64_t>(4, cap / (4 * (int64_t)k));
+  int64_t hi = std::max<int64_t>(k, 1024);
+  hi = (hi + kGemmBN - 1) / kGemmBN * kGemmBN;
+  int64_t lo = 0;
+  while (lo < n) {
+    const int64_t h = std::min<int64_t>(n, hi);
+    out->push_back(GemmLevel{lo, h});
+    lo = h;
+    hi = (lo * F + kGemmBN - 1) / kGemmBN * kGemmBN;
+  }
+}
+
+static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                            cudaStream_t st) {
+  if (k > select_max_k())
+    return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d beyond the device top-K)", k);
+  const int32_t kp = pow2_ge_host(k);
+  const int32_t Mpad = (M + kGemmBM - 1) / kGemmBM * kGemmBM;
+  // per-query candidate capacity: ~256 MB of keys at most across the batch
+  int32_t cap = pow2_ge_host(std::max<int64_t>(8192, std::min<int64_t>(65536, (1ll << 25) / M)));
+  if (cap > 65536) cap = 65536;
+  int rc;
+  if ((rc = ensure_device(&x->d_A, &x->A_cap, (size_t)Mpad * x->dpad, "gemm A")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_qscale, &x->qscale_cap, (size_t)Mpad, "gemm qscale")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_thr, &x->thr_cap, (size_t)M, "gemm thr")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_cnt, &x->cnt_cap, (size_t)M, "gemm cnt")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_cand, &x->cand_cap, (size_t)M * cap, "gemm cand")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_topk, &x->topk_cap, (size_t)M * kp, "gemm topk")) != FI8_OK) return rc;
+  const int64_t A_rows = (int64_t)(x->A_cap / x->dpad);
+  if (x->tmA_base != x->d_A || x->tmA_rows != A_rows) {
+    if (!make_tmap_i8(&x->tmA, x->d_A, (uint64_t)A_rows, (uint64_t)x->dpad, (uint32_t)kGemmBM))
+      return fail(FI8_ERR_CUDA, "fi8: cuTensorMapEncodeTiled failed for the query tile map");
+    x->tmA_base = x->d_A;
+    x->tmA_rows = A_rows;
+  }
+  cudaError_t e = quantize_launch(d_q, M, Mpad, x->dim, x->dpad, x->d_A, x->d_qscale, x->d_thr, x->d_cnt,
+                                  x->d_topk, kp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_launch");
+  x->last_launches++;
+  std::vector<GemmLevel> ranges;
+  plan_ranges(x->n, k, cap, &ranges);
+  GemmParams p{};
+  p.kchunks = (x->dpad + kGemmBK - 1) / kGemmBK;
+  p.M = M;
+  p.qtiles = Mpad / kGemmBM;
+  p.id_base = x->id_base;
+  p.scales = x->d_scales;
+  p.qscale = x->d_qscale;
+  p.thr = x->d_thr;
+  p.cnt = x->d_cnt;
+  p.cand = x->d_cand;
+  p.cap = cap;
+  p.err = x->d_err;
+  for (size_t i = 0; i < ranges.size(); i++) {
+    p.row_lo = ranges[i].row_lo;
+    p.row_hi = ranges[i].row_hi;
+    p.rtiles = (p.row_hi - p.row_lo + kGemmBN - 1) / kGemmBN;
+    const int64_t units = (int64_t)p.qtiles * p.rtiles;
+    const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(x->sm_count, units));
+    e = gemm_launch(x->tmA, x->tmB, p, G, st);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_launch");
+    const bool last = (i + 1 == ranges.size());
+    e = select_launch(M, k, kp, x->d_topk, x->d_thr, x->d_cnt, x->d_cand, cap, last ? d_keys : nullptr,
+                      x->d_err, st);
+    if (e != cudaSuccess) return cuda_fail(e, "select_launch");
+    x->last_launches += 2;
+  }
+  return FI8_OK;
+}
+
+static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                       cudaStream_t st) {
+  x->last_launches = 0;
+  if (M >= x->gemm_min_batch && x->has_tmB) return launch_topk_gemm(x, d_q, M, k, d_keys, st);
+  return launch_topk_scan(x, d_q, M, k, d_keys, st);
 }
 
 static int launch_scores(fi8_index* x, const float* d_q, int32_t M, float* d_scores, cudaStream_t st) {
@@ -370,6 +490,7 @@ static int launch_scores(fi8_index* x, const float* d_q, int32_t M, float* d_sco
     p.out_scores = d_scores + (size_t)m0 * x->n;
     cudaError_t e = scan_launch(p, false, mm, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(score)");
+    x->last_launches++;
   }
   return FI8_OK;
 }
@@ -381,7 +502,8 @@ static int check_device_error(fi8_index* x) {
     *x->h_err = 0;
     cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream);
     cudaStreamSynchronize(x->stream);
-    return fail(FI8_ERR_DEVICE, "fi8: kernel reported device error flags 0x%x (bounded wait expired)", v);
+    return fail(FI8_ERR_DEVICE, "fi8: kernel reported device error flags 0x%x (%s)", v,
+                (v & 1u) ? "a bounded wait expired" : "a candidate buffer overflowed");
   }
   return FI8_OK;
 }
@@ -397,6 +519,7 @@ int fi8_score_batch(fi8_index* idx, const float* q, int32_t M, float* dst) {
   if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
   if ((rc = ensure_device(&x->d_scores, &x->d_scores_cap, (size_t)M * x->n, "staging scores")) != FI8_OK)
     return rc;
+  x->last_launches = 0;
   FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
            "H2D queries");
   if ((rc = launch_scores(x, x->d_q, M, x->d_scores, x->stream)) != FI8_OK) return rc;
@@ -432,6 +555,20 @@ int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t
   FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
            "D2H err");
   FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+  if (*x->h_err == 2u) {
+    // The batched path dropped candidates (a row range admitted more than its
+    // per-query buffer holds, e.g. on a corpus ordered against the queries).
+    // Its answer is incomplete; recompute the batch with the per-query scan,
+    // which has no such limit.
+    *x->h_err = 0;
+    FI8_CUDA(cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream), "memset err");
+    if ((rc = launch_topk_scan(x, x->d_q, M, k, x->d_keys, x->stream)) != FI8_OK) return rc;
+    FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
+             "D2H keys");
+    FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
+             "D2H err");
+    FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+  }
   if ((rc = check_device_error(x)) != FI8_OK) return rc;
   return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
 }
@@ -447,6 +584,26 @@ int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k,
   std::lock_guard<std::mutex> lk(idx->mu);
   DeviceGuard g(idx->device);
   return launch_topk(idx, d_q, M, k, d_keys, static_cast<cudaStream_t>(stream));
+}
+
+int fi8_index_set_option(fi8_index* idx, int option, int64_t value) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_index_set_option: null index");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  switch (option) {
+    case FI8_OPT_GEMM_MIN_BATCH:
+      if (value < 1) return fail(FI8_ERR_ARG, "fi8_index_set_option: GEMM_MIN_BATCH must be >= 1");
+      idx->gemm_min_batch = (int32_t)std::min<int64_t>(value, 1 << 30);
+      return FI8_OK;
+    default:
+      return fail(FI8_ERR_ARG, "fi8_index_set_option: unknown option %d", option);
+  }
+}
+
+int fi8_index_last_launch_count(fi8_index* idx, int32_t* out) {
+  if (!idx || !out) return fail(FI8_ERR_ARG, "fi8_index_last_launch_count: null argument");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  *out = idx->last_launches;
+  return FI8_OK;
 }
 
 int fi8_index_sync(fi8_index* idx) {

@@ -1,0 +1,480 @@
+// fi8_gemm.cu -- the batched FlatI8 path on sm_100a: the W8A8 scores of a
+// query batch against a corpus row range as a tcgen05 kind::i8 tensor-core
+// GEMM (int32 accumulators in TMEM), with the scale epilogue and an exact
+// threshold filter fused, so the Q x N score matrix never reaches HBM.
+//
+// Reference semantics: the batch scores of ScoreBatch / MatmulBTW8A8 with M
+// queries (ann/backend.go:43, linalg/quant.go:192-298) and the per-query top-K
+// of TopKBatch (gpu/anncuda/backend.go:568-667, ann/flat_i8.go:214-246).
+//
+// Selection runs over row ranges [0,s1), [s1,s2), ... of growing size. For
+// each range the GEMM keeps, per query, every row whose packed key exceeds the
+// query's threshold; then select_kernel folds those candidates into the
+// query's running exact top-k and sets the next threshold to its k-th best key
+// -- the k-th best of k real rows already seen, so no row that can reach the
+// final top-k is ever discarded. Ranges grow by a factor F, so a range admits
+// about k*F candidates per query on exchangeable data, whatever N is.
+//
+// gemm_kernel, one persistent CTA per SM, warp-specialized (576 threads):
+//   warp 0   TMA producer: per pipeline stage, a 128x128 query tile and a
+//            256x128 corpus tile (both SWIZZLE_128B, K-major) -> shared memory
+//   warp 1   MMA issuer: 4 x tcgen05.mma.kind::i8 (128x256x32) per stage into
+//            one of two 256-column TMEM accumulators; tcgen05.commit frees the
+//            stage and, after the last K stage, hands the accumulator on
+//   warps 2-17 epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
+//            lanes 32*(w%4).. = its queries, and one quarter of the 256
+//            columns), a branch-free float pre-filter against the query's
+//            threshold, then the exact key test and append for survivors.
+// No TMA multicast is used anywhere.
+#include <cuda.h>
+
+#include "fi8_device.cuh"
+#include "fi8_gemm.cuh"
+#include "fi8_select.cuh"
+
+namespace fi8 {
+
+namespace {
+
+constexpr int kStageA = kGemmBM * kGemmBK;  // 16 KB
+constexpr int kStageB = kGemmBN * kGemmBK;  // 32 KB
+constexpr int kStageBytes = kStageA + kStageB;
+constexpr int kStages = 4;
+constexpr int kEpiWarps = 16;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kGemmThreads = 64 + kEpiThreads;
+constexpr int kBarEpi = 1;  // named barrier over the epilogue warps
+constexpr int kTmemCols = 512;  // two 256-column accumulators
+constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024;  // + alignment slack
+
+// tcgen05 instruction descriptor, kind::i8: D = s32 (c_format 2), A and B
+// signed 8-bit (format 1), both K-major, N = 256 (n_dim = N>>3), M = 128
+// (m_dim = M>>4).
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGemmBN >> 3) << 17) |
+                            ((uint32_t)(kGemmBM >> 4) << 24);
+
+// Shared-memory matrix descriptor for a K-major SWIZZLE_128B tile whose rows
+// are 128 bytes: start address >> 4, leading byte offset 1 (unused for
+// swizzled K-major), stride byte offset 1024 >> 4 (8-row swizzle atoms),
+// version 1, layout type 2 (128B swizzle). The tile base is 1024-aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Placement of a tile's queries in the A operand (= TMEM lanes). A tile with
+// at most 64 real queries spreads them 16 per 32-lane quarter, so all four
+// epilogue sub-partitions get work; a fuller tile is dense.
+__host__ __device__ __forceinline__ int tile_row_of(int j, int m_t) {
+  return m_t <= 64 ? ((j >> 4) << 5) + (j & 15) : j;
+}
+__device__ __forceinline__ int tile_query_of(int r, int m_t) {
+  if (m_t <= 64) {
+    const int l = r & 31;
+    return l < 16 ? ((r >> 5) << 4) + l : -1;
+  }
+  return r;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t s_full[kStages], s_empty[kStages], s_tfull[2], s_tempty[2], s_done;
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_abort;
+  __shared__ __align__(16) float s_scale[2][kGemmBN];
+  __shared__ int s_eabort[2];
+
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int64_t units = (int64_t)p.qtiles * p.rtiles;
+  const int64_t my_units = units > blockIdx.x ? (units - blockIdx.x + G - 1) / G : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&s_tfull[b], 1);
+      mbar_init(&s_tempty[b], kEpiWarps);
+    }
+    mbar_init(&s_done, 1);
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int64_t step = 0;
+      for (int64_t u = 0; u < my_units && !s_abort; u++) {
+        const int64_t unit = blockIdx.x + u * G;
+        const int qt = (int)(unit % p.qtiles);
+        const int64_t rt = unit / p.qtiles;
+        const int32_t row0 = (int32_t)(p.row_lo + rt * kGemmBN);
+        for (int kc = 0; kc < p.kchunks; kc++, step++) {
+          const int s = (int)(step % kStages);
+          if (step >= kStages && !mbar_wait_bounded(&s_empty[s], (uint32_t)(((step / kStages) - 1) & 1))) {
+            s_abort = 1;
+            atomicOr(p.err, 1u);
+            break;
+          }
+          unsigned char* st = smem + (size_t)s * kStageBytes;
+          mbar_arrive_expect_tx(&s_full[s], kStageBytes);
+          tma_load_2d(st, &tmA, kc * kGemmBK, qt * kGemmBM, &s_full[s]);
+          tma_load_2d(st + kStageA, &tmB, kc * kGemmBK, row0, &s_full[s]);
+        }
+      }
+      // let issued copies land before teardown (bounded; a no-op when drained)
+      for (int64_t j = (step > kStages ? step - kStages : 0); j < step; j++)
+        mbar_wait_bounded(&s_full[j % kStages], (uint32_t)((j / kStages) & 1));
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      int64_t step = 0;
+      for (int64_t u = 0; u < my_units && !s_abort; u++) {
+        const int b = (int)(u & 1);
+        if (u >= 2 && !mbar_wait_bounded(&s_tempty[b], (uint32_t)(((u / 2) - 1) & 1))) {
+          s_abort = 1;
+          atomicOr(p.err, 1u);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(b * kGemmBN);
+        for (int kc = 0; kc < p.kchunks; kc++, step++) {
+          const int s = (int)(step % kStages);
+          if (!mbar_wait_bounded(&s_full[s], (uint32_t)((step / kStages) & 1))) {
+            s_abort = 1;
+            atomicOr(p.err, 1u);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + (size_t)s * kStageBytes);
+          const uint32_t b_base = a_base + kStageA;
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 32; k++) {
+            // advance K by 32 bytes inside the swizzled 128-byte rows
+            umma_i8(d_tmem, sw128_desc(a_base) + (uint64_t)(2 * k), sw128_desc(b_base) + (uint64_t)(2 * k),
+                    (kc > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&s_empty[s]);
+        }
+        if (s_abort) break;
+        umma_commit(&s_tfull[b]);
+      }
+      // every MMA this thread issued has completed before TMEM is released
+      umma_commit(&s_done);
+      mbar_wait_bounded(&s_done, 0);
+    }
+  } else {
+    // ------------------------------ epilogue ------------------------------
+    // Warp w reads TMEM lanes 32*(w%4).. (its queries) and columns
+    // 64*((w-2)/4).. of each 256-column accumulator.
+    const int etid = threadIdx.x - 64;
+    const int quarter = warp & 3;
+    const int cq = (warp - 2) >> 2;
+    for (int64_t u = 0; u < my_units; u++) {
+      const int64_t unit = blockIdx.x + u * G;
+      const int qt = (int)(unit % p.qtiles);
+      const int64_t rt = unit / p.qtiles;
+      const int64_t row0 = p.row_lo + rt * kGemmBN;
+      const int b = (int)(u & 1);
+      const int m_t = min(kGemmBM, p.M - qt * kGemmBM);
+      const int r = quarter * 32 + lane;  // A row / TMEM lane of this thread
+      const int j = tile_query_of(r, m_t);
+      const bool valid_q = j >= 0 && j < m_t;
+      const int q = qt * kGemmBM + j;
+      const float qs = valid_q ? p.qscale[qt * kGemmBM + r] : 0.0f;
+      const bool qzero = qs == 0.0f;  // an all-zero query scores exactly 0
+      const unsigned long long T = valid_q ? p.thr[q] : ~0ull;
+      const float Tscore = (T == 0ull) ? -INFINITY : key_score(T);
+      // this unit's 256 row scales, once, for every epilogue warp
+      if (etid < kGemmBN) s_scale[b][etid] = p.scales[row0 + etid];
+      // abort decision, uniform over the epilogue warps: sampled by one thread
+      // before the barrier, read by all after it (parity-buffered, so a fast
+      // thread cannot overwrite it while a slow one still reads)
+      if (etid == 0) s_eabort[b] = s_abort;
+      named_sync(kBarEpi, kEpiThreads);
+      if (s_eabort[b]) break;
+      if (!mbar_wait_bounded(&s_tfull[b], (uint32_t)((u / 2) & 1))) {
+        s_abort = 1;
+        atomicOr(p.err, 1u);
+      }
+      tc_fence_after();
+      const int64_t lim = p.row_hi - row0;  // valid columns of this tile
+#pragma unroll 1
+      for (int c = 0; c < 2; c++) {
+        const int col0 = cq * 64 + c * 32;
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kGemmBN + col0), v);
+        // branch-free pass: the plain product equals the exact (x86 NaN
+        // semantics) score whenever it is not NaN, and NaN never passes
+        uint32_t mask = 0;
+        const float4* s4 = reinterpret_cast<const float4*>(&s_scale[b][col0]);
+#pragma unroll
+        for (int i4 = 0; i4 < 8; i4++) {
+          const float4 rs = s4[i4];
+          const float rsv[4] = {rs.x, rs.y, rs.z, rs.w};
+#pragma unroll
+          for (int t = 0; t < 4; t++) {
+            const int i = i4 * 4 + t;
+            float sc = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), rsv[t]);
+            sc = qzero ? 0.0f : sc;
+            mask |= (sc >= Tscore ? 1u : 0u) << i;
+          }
+        }
+        if (!valid_q) mask = 0u;
+        if (col0 + 32 > lim) mask &= (col0 >= lim) ? 0u : ((1u << (uint32_t)(lim - col0)) - 1u);
+        if (mask) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            if ((mask >> i) & 1u) {
+              const float score = w8a8_score((int32_t)v[i], qs, s_scale[b][col0 + i]);
+              const uint64_t key = make_key(score, p.id_base + (uint32_t)(row0 + col0 + i));
+              if (key > T) {
+                const unsigned int pos = atomicAdd(p.cnt + q, 1u);
+                if (pos < (unsigned int)p.cap) p.cand[(size_t)q * p.cap + pos] = key;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive1(&s_tempty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// One CTA per A row (Mpad rows): quantize the query placed there
+// (quant.go:43-71, zero scale 0; see tile_row_of) or zero-fill an unused row,
+// and reset that query's select state.
+__global__ void __launch_bounds__(256) quantize_kernel(const float* q, int M, int d, int dpad, int8_t* A,
+                                                       float* qscale, unsigned long long* thr, unsigned int* cnt,
+                                                       uint64_t* topk, int kp) {
+  __shared__ float s_red[8];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int qt = row / kGemmBM;
+  const int m_t = min(kGemmBM, M - qt * kGemmBM);
+  const int j = tile_query_of(row % kGemmBM, m_t);
+  int8_t* dst = A + (size_t)row * dpad;
+  if (j < 0 || j >= m_t) {  // no query at this row
+    for (int i = tid; i < dpad; i += blockDim.x) dst[i] = 0;
+    if (tid == 0) qscale[row] = 0.0f;
+    return;
+  }
+  const int qi = qt * kGemmBM + j;
+  const float* src = q + (size_t)qi * d;
+  float m = 0.0f;
+  for (int i = tid; i < d; i += blockDim.x) m = absmax_step(m, src[i]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = absmax_combine(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((tid & 31) == 0) s_red[tid >> 5] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float mm = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) mm = absmax_combine(mm, s_red[w]);
+    s_red[0] = mm;
+  }
+  __syncthreads();
+  const float maxabs = s_red[0];
+  if (maxabs == 0.0f) {
+    for (int i = tid; i < dpad; i += blockDim.x) dst[i] = 0;
+    if (tid == 0) qscale[row] = 0.0f;
+  } else {
+    const float sc = __fdiv_rn(maxabs, 127.0f);
+    const float inv = __fdiv_rn(1.0f, sc);
+    for (int i = tid; i < dpad; i += blockDim.x) dst[i] = i < d ? quant_code(src[i], inv) : (int8_t)0;
+    if (tid == 0) qscale[row] = sc;
+  }
+  if (tid == 0) {
+    thr[qi] = 0ull;
+    cnt[qi] = 0u;
+  }
+  for (int i = tid; i < kp; i += blockDim.x) topk[(size_t)qi * kp + i] = kEmptyKey;
+}
+
+// One CTA (one 256-thread group) per query: fold this range's candidates into
+// the running top-k. The carried list holds keys of earlier ranges (all >= the
+// threshold the candidates passed), so top-k of the union is exact.
+__global__ void __launch_bounds__(kGroupThreads, 1)
+    select_kernel(int k, int kp, int cap_s, uint64_t* topk, unsigned long long* thr, unsigned int* cnt,
+                  const uint64_t* cand, int cap, uint64_t* out, unsigned int* err) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_count;
+  __shared__ unsigned long long s_local_thr;
+  uint64_t* buf = reinterpret_cast<uint64_t*>(smem);
+  const int qi = blockIdx.x;
+  const int gtid = threadIdx.x;
+  const int bar = 1;
+  if (gtid == 0) {
+    s_count = 0;
+    s_local_thr = 0;
+  }
+  named_sync(bar, kGroupThreads);
+  uint64_t* mine = topk + (size_t)qi * kp;
+  for (int i0 = 0; i0 < kp; i0 += kGroupThreads) {
+    const int i = i0 + gtid;
+    const uint64_t key = i < kp ? mine[i] : kEmptyKey;
+    warp_append(key != kEmptyKey, key, buf, &s_count);
+  }
+  named_sync(bar, kGroupThreads);
+  const unsigned int c_all = cnt[qi];
+  if (c_all > (unsigned int)cap && gtid == 0) atomicOr(err, 2u);  // candidates were dropped
+  const int n_c = (int)(c_all < (unsigned int)cap ? c_all : (unsigned int)cap);
+  const uint64_t* src = cand + (size_t)qi * cap;
+  if (s_count > cap_s - kGroupThreads) group_compact(buf, s_count, k, &s_count, &s_local_thr, nullptr, gtid, bar);
+  for (int b0 = 0; b0 < n_c; b0 += kGroupThreads) {
+    const int e = b0 + gtid;
+    uint64_t key = kEmptyKey;
+    bool take = false;
+    if (e < n_c) {
+      key = src[e];
+      take = key > s_local_thr;
+    }
+    warp_append(take, key, buf, &s_count);
+    named_sync(bar, kGroupThreads);
+    const int cnow = s_count;
+    if (cnow > cap_s - kGroupThreads) group_compact(buf, cnow, k, &s_count, &s_local_thr, nullptr, gtid, bar);
+  }
+  named_sync(bar, kGroupThreads);
+  group_compact(buf, s_count, k, &s_count, &s_local_thr, nullptr, gtid, bar);
+  const int fin = s_count;
+  for (int i = gtid; i < kp; i += kGroupThreads) mine[i] = i < fin ? buf[i] : kEmptyKey;
+  if (out)
+    for (int i = gtid; i < k; i += kGroupThreads) out[(size_t)qi * k + i] = i < fin ? buf[i] : kEmptyKey;
+  if (gtid == 0) {
+    thr[qi] = fin >= k ? buf[k - 1] : 0ull;
+    cnt[qi] = 0u;
+  }
+}
+
+int pow2_ge(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+}  // namespace
+
+int32_t select_max_k() { return 4096 - kGroupThreads; }
+
+bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pitch, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || pitch % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  const cuuint64_t dims[2] = {pitch, rows};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G,
+                        cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
+  if (e != cudaSuccess) return e;
+  gemm_kernel<<<G, kGemmThreads, kGemmSmem, stream>>>(tmA, tmB, p);
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,
+                            float* qscale, unsigned long long* thr, unsigned int* cnt, uint64_t* topk, int32_t kp,
+                            cudaStream_t stream) {
+  quantize_kernel<<<Mpad, 256, 0, stream>>>(q, M, d, dpad, A, qscale, thr, cnt, topk, kp);
+  return cudaGetLastError();
+}
+
+cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsigned long long* thr,
+                          unsigned int* cnt, const uint64_t* cand, int32_t cap, uint64_t* out, unsigned int* err,
+                          cudaStream_t stream) {
+  const int cap_s = pow2_ge(k + kGroupThreads) > pow2_ge(kp + kGroupThreads) ? pow2_ge(k + kGroupThreads)
+                                                                            : pow2_ge(kp + kGroupThreads);
+  if (cap_s > 8192) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 * 8);
+  if (e != cudaSuccess) return e;
+  select_kernel<<<M, kGroupThreads, (size_t)cap_s * 8, stream>>>(k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
+  return cudaGetLastError();
+}
+
+}  // namespace fi8

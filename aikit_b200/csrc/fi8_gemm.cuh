@@ -1,0 +1,58 @@
+// fi8_gemm.cuh -- host-visible declarations for the batched FlatI8 path:
+// query quantization, the tcgen05 kind::i8 GEMM with a threshold-filter
+// epilogue, and the per-query exact select between row ranges.
+#pragma once
+
+#include <cuda.h>
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fi8 {
+
+constexpr int32_t kGemmBM = 128;  // queries per tile (TMEM lanes)
+constexpr int32_t kGemmBN = 256;  // corpus rows per tile (MMA N)
+constexpr int32_t kGemmBK = 128;  // K bytes per pipeline stage (one 128B-swizzle row)
+
+struct GemmLevel {
+  int64_t row_lo, row_hi;  // corpus rows [lo, hi) of this range; lo % 256 == 0
+};
+
+struct GemmParams {
+  int64_t row_lo, row_hi;
+  int32_t kchunks;       // ceil(dpad / 128)
+  int32_t M;             // real queries
+  int32_t qtiles;        // ceil(M / 128)
+  int64_t rtiles;        // 256-row tiles in [row_lo, row_hi)
+  uint32_t id_base;      // global id of corpus row 0
+  const float* scales;   // [n_alloc] row scales
+  const float* qscale;   // [Mpad] query scales
+  const unsigned long long* thr;  // [M] per-query threshold key (0 = none)
+  unsigned int* cnt;     // [M] candidates appended this range
+  uint64_t* cand;        // [M][cap] candidate keys
+  int32_t cap;
+  unsigned int* err;
+};
+
+// Build a 2-D SWIZZLE_128B tensor map over an int8 matrix [rows][pitch]
+// (pitch a multiple of 16 bytes) with a {128 bytes, box_rows} box.
+bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pitch, uint32_t box_rows);
+
+cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G,
+                        cudaStream_t stream);
+
+// Quantize M queries ([M][d] f32) into A ([Mpad][dpad] int8, zero padded) and
+// qscale ([Mpad]); also resets the per-query select state (thr, cnt, topk).
+cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,
+                            float* qscale, unsigned long long* thr, unsigned int* cnt, uint64_t* topk, int32_t kp,
+                            cudaStream_t stream);
+
+// Per query: top-k of (carried topk list [kp] U this range's candidates) ->
+// topk, thr = k-th best key (0 if fewer), cnt = 0; optionally out[q][k].
+cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsigned long long* thr,
+                          unsigned int* cnt, const uint64_t* cand, int32_t cap, uint64_t* out, unsigned int* err,
+                          cudaStream_t stream);
+
+int32_t select_max_k();
+
+}  // namespace fi8

@@ -205,7 +205,7 @@ def main():
 
     def step(i, m=BATCH):
         ix.topk_async(Qd[i % nb].data_ptr(), m, K, keys_local.data_ptr(), st)
-        launches = 1
+        launches = ix.last_launch_count()
         if world > 1:  # multi-GPU runs the batch-64 form only
             dist.all_gather_into_tensor(gathered.view(-1), keys_local.view(-1))
             be.ctx.merge_keys_async(gathered.data_ptr(), world, m, K, merged.data_ptr(), st)

@@ -95,6 +95,16 @@ int fi8_topk_max_k(fi8_index* idx, int32_t* out);
 int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
                          void* stream);
 
+/* Tuning knobs of an index. FI8_OPT_GEMM_MIN_BATCH: batches of at least this
+ * many queries take the tcgen05 GEMM path, smaller ones the per-query scan
+ * (default 2). Both return identical results. */
+#define FI8_OPT_GEMM_MIN_BATCH 1
+int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
+
+/* Number of kernels the index's last query call launched (scan: one per 64
+ * queries; batched: quantize + a GEMM and a select per row range). */
+int fi8_index_last_launch_count(fi8_index* idx, int32_t* out);
+
 /* Wait for the index's stream and report any device-side error flag. */
 int fi8_index_sync(fi8_index* idx);
 

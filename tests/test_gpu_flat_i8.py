@@ -15,27 +15,9 @@ from aikit_b200 import DeclinedError, fi8_format, synth
 from aikit_b200.ann import unpack_keys
 
 from conftest import GOLDEN
+from parity_util import assert_same, oracle_topk
 
 pytestmark = pytest.mark.gpu
-
-
-def oracle_topk(bq, bs, Q, k):
-    idx = np.full((len(Q), k), -1, np.int64)
-    sc = np.zeros((len(Q), k), np.float32)
-    for m, q in enumerate(Q):
-        i, s = oracle.flat_i8_query(bq, bs, q, k)
-        idx[m, :len(i)] = i
-        sc[m, :len(s)] = np.asarray(s, np.float32)
-    return idx, sc
-
-
-def assert_same(gidx, gsc, widx, wsc, what=""):
-    assert gidx.shape == widx.shape, what
-    bad = np.nonzero(gidx != widx)
-    assert bad[0].size == 0, f"{what}: first index mismatch at {bad[0][0]},{bad[1][0]}: " \
-        f"gpu {gidx[bad[0][0]]} vs oracle {widx[bad[0][0]]}"
-    valid = widx >= 0
-    assert gsc[valid].tobytes() == wsc[valid].tobytes(), f"{what}: scores differ"
 
 
 def test_committed_goldens(backend):
