@@ -402,7 +402,9 @@ static int32_t pow2_ge_host(int64_t x) {
 
 // Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles.
 static void plan_ranges(int64_t n, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
-  const int64_t F = std::max<int64_t>(4, cap / (4 * (int64_t)k));
+  // Growth factor: a range admits ~k*F candidates per query; 16 keeps each
+  // select small while the number of ranges stays logarithmic.
+  const int64_t F = std::min<int64_t>(16, std::max<int64_t>(4, cap / (4 * (int64_t)k)));
   int64_t hi = std::max<int64_t>(k, 1024);
   hi = (hi + kGemmBN - 1) / kGemmBN * kGemmBN;
   int64_t lo = 0;

@@ -357,10 +357,12 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* q, int M, in
   for (int i = tid; i < kp; i += blockDim.x) topk[(size_t)qi * kp + i] = kEmptyKey;
 }
 
-// One CTA (one 256-thread group) per query: fold this range's candidates into
-// the running top-k. The carried list holds keys of earlier ranges (all >= the
+// One CTA of 1024 threads per query: fold this range's candidates into the
+// running top-k. The carried list holds keys of earlier ranges (all >= the
 // threshold the candidates passed), so top-k of the union is exact.
-__global__ void __launch_bounds__(kGroupThreads, 1)
+constexpr int kSelThreads = 1024;
+
+__global__ void __launch_bounds__(kSelThreads, 1)
     select_kernel(int k, int kp, int cap_s, uint64_t* topk, unsigned long long* thr, unsigned int* cnt,
                   const uint64_t* cand, int cap, uint64_t* out, unsigned int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -368,27 +370,28 @@ __global__ void __launch_bounds__(kGroupThreads, 1)
   __shared__ unsigned long long s_local_thr;
   uint64_t* buf = reinterpret_cast<uint64_t*>(smem);
   const int qi = blockIdx.x;
-  const int gtid = threadIdx.x;
-  const int bar = 1;
-  if (gtid == 0) {
+  const int tid = threadIdx.x;
+  constexpr int bar = 1;
+  if (tid == 0) {
     s_count = 0;
     s_local_thr = 0;
   }
-  named_sync(bar, kGroupThreads);
+  named_sync(bar, kSelThreads);
   uint64_t* mine = topk + (size_t)qi * kp;
-  for (int i0 = 0; i0 < kp; i0 += kGroupThreads) {
-    const int i = i0 + gtid;
+  for (int i0 = 0; i0 < kp; i0 += kSelThreads) {
+    const int i = i0 + tid;
     const uint64_t key = i < kp ? mine[i] : kEmptyKey;
     warp_append(key != kEmptyKey, key, buf, &s_count);
   }
-  named_sync(bar, kGroupThreads);
+  named_sync(bar, kSelThreads);
   const unsigned int c_all = cnt[qi];
-  if (c_all > (unsigned int)cap && gtid == 0) atomicOr(err, 2u);  // candidates were dropped
+  if (c_all > (unsigned int)cap && tid == 0) atomicOr(err, 2u);  // candidates were dropped
   const int n_c = (int)(c_all < (unsigned int)cap ? c_all : (unsigned int)cap);
   const uint64_t* src = cand + (size_t)qi * cap;
-  if (s_count > cap_s - kGroupThreads) group_compact(buf, s_count, k, &s_count, &s_local_thr, nullptr, gtid, bar);
-  for (int b0 = 0; b0 < n_c; b0 += kGroupThreads) {
-    const int e = b0 + gtid;
+  if (s_count > cap_s - kSelThreads)
+    group_compact<kSelThreads>(buf, s_count, k, &s_count, &s_local_thr, nullptr, tid, bar);
+  for (int b0 = 0; b0 < n_c; b0 += kSelThreads) {
+    const int e = b0 + tid;
     uint64_t key = kEmptyKey;
     bool take = false;
     if (e < n_c) {
@@ -396,17 +399,18 @@ __global__ void __launch_bounds__(kGroupThreads, 1)
       take = key > s_local_thr;
     }
     warp_append(take, key, buf, &s_count);
-    named_sync(bar, kGroupThreads);
+    named_sync(bar, kSelThreads);
     const int cnow = s_count;
-    if (cnow > cap_s - kGroupThreads) group_compact(buf, cnow, k, &s_count, &s_local_thr, nullptr, gtid, bar);
+    if (cnow > cap_s - kSelThreads)
+      group_compact<kSelThreads>(buf, cnow, k, &s_count, &s_local_thr, nullptr, tid, bar);
   }
-  named_sync(bar, kGroupThreads);
-  group_compact(buf, s_count, k, &s_count, &s_local_thr, nullptr, gtid, bar);
+  named_sync(bar, kSelThreads);
+  group_compact<kSelThreads>(buf, s_count, k, &s_count, &s_local_thr, nullptr, tid, bar);
   const int fin = s_count;
-  for (int i = gtid; i < kp; i += kGroupThreads) mine[i] = i < fin ? buf[i] : kEmptyKey;
+  for (int i = tid; i < kp; i += kSelThreads) mine[i] = i < fin ? buf[i] : kEmptyKey;
   if (out)
-    for (int i = gtid; i < k; i += kGroupThreads) out[(size_t)qi * k + i] = i < fin ? buf[i] : kEmptyKey;
-  if (gtid == 0) {
+    for (int i = tid; i < k; i += kSelThreads) out[(size_t)qi * k + i] = i < fin ? buf[i] : kEmptyKey;
+  if (tid == 0) {
     thr[qi] = fin >= k ? buf[k - 1] : 0ull;
     cnt[qi] = 0u;
   }
@@ -436,7 +440,7 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
-int32_t select_max_k() { return 4096 - kGroupThreads; }
+int32_t select_max_k() { return 4096; }  // kp <= 4096 keeps the select buffer at 64 KB
 
 bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pitch, uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -468,12 +472,14 @@ cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, 
 cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsigned long long* thr,
                           unsigned int* cnt, const uint64_t* cand, int32_t cap, uint64_t* out, unsigned int* err,
                           cudaStream_t stream) {
-  const int cap_s = pow2_ge(k + kGroupThreads) > pow2_ge(kp + kGroupThreads) ? pow2_ge(k + kGroupThreads)
-                                                                            : pow2_ge(kp + kGroupThreads);
+  // buffer: the carried list plus room for a few thousand candidates between
+  // compactions (a compaction is a bitonic sort of the buffer)
+  int cap_s = pow2_ge(kp + kSelThreads);
+  if (cap_s < 4096) cap_s = 4096;
   if (cap_s > 8192) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 * 8);
   if (e != cudaSuccess) return e;
-  select_kernel<<<M, kGroupThreads, (size_t)cap_s * 8, stream>>>(k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
+  select_kernel<<<M, kSelThreads, (size_t)cap_s * 8, stream>>>(k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
   return cudaGetLastError();
 }
 

@@ -41,12 +41,14 @@ __device__ __forceinline__ void warp_append(bool take, uint64_t key, uint64_t* b
   if (take) buf[base + __popc(mask & lanemask_lt())] = key;
 }
 
-// Bitonic sort (descending) of n = 2^j keys by one 256-thread group.
+// Bitonic sort (descending) of n = 2^j keys by a group of NT threads that
+// synchronize on named barrier `bar`.
+template <int NT = kGroupThreads>
 __device__ inline void group_sort_desc(uint64_t* buf, int n, int gtid, int bar) {
   const int half = n >> 1;
   for (int size = 2; size <= n; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = gtid; i < half; i += kGroupThreads) {
+      for (int i = gtid; i < half; i += NT) {
         const int lo = 2 * stride * (i / stride) + (i % stride);
         const int hi = lo + stride;
         const bool desc = (lo & size) == 0;
@@ -56,19 +58,20 @@ __device__ inline void group_sort_desc(uint64_t* buf, int n, int gtid, int bar) 
           buf[hi] = a;
         }
       }
-      named_sync(bar, kGroupThreads);
+      named_sync(bar, NT);
     }
   }
 }
 
 // Sort the first cnt keys, keep the best k, raise (and optionally publish) the
-// group threshold. All 256 threads of the group call it with the same cnt.
+// group threshold. All NT threads of the group call it with the same cnt.
+template <int NT = kGroupThreads>
 __device__ inline void group_compact(uint64_t* buf, int cnt, int k, int* s_count, unsigned long long* s_local_thr,
                                      unsigned long long* gthr, int gtid, int bar) {
   const int n2 = next_pow2_dev(cnt < 2 ? 2 : cnt);
-  for (int i = cnt + gtid; i < n2; i += kGroupThreads) buf[i] = kEmptyKey;
-  named_sync(bar, kGroupThreads);
-  group_sort_desc(buf, n2, gtid, bar);
+  for (int i = cnt + gtid; i < n2; i += NT) buf[i] = kEmptyKey;
+  named_sync(bar, NT);
+  group_sort_desc<NT>(buf, n2, gtid, bar);
   if (gtid == 0) {
     *s_count = cnt < k ? cnt : k;
     if (cnt >= k) {
@@ -77,7 +80,7 @@ __device__ inline void group_compact(uint64_t* buf, int cnt, int k, int* s_count
       if (gthr) atomicMax(gthr, t);
     }
   }
-  named_sync(bar, kGroupThreads);
+  named_sync(bar, NT);
 }
 
 // Tree-merge `total` sorted (descending) lists of kp keys held in slots

@@ -23,6 +23,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--mode", choices=["topk", "score"], default="topk")
+    ap.add_argument("--trace", action="store_true",
+                    help="also report per-kernel device time (torch.profiler / CUPTI) over the reps")
     a = ap.parse_args()
 
     import torch
@@ -38,6 +40,11 @@ def main() -> None:
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     times = []
+    prof = None
+    if a.trace:
+        from torch.profiler import ProfilerActivity, profile
+        prof = profile(activities=[ProfilerActivity.CUDA])
+        prof.__enter__()
     for _ in range(a.reps):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -51,9 +58,24 @@ def main() -> None:
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
     ix.sync()
+    kernels = None
+    if prof is not None:
+        prof.__exit__(None, None, None)
+        agg = {}
+        for ev in prof.events():
+            if ev.device_type.name != "CUDA":
+                continue
+            name = next((k for k in ("scan_kernel", "gemm_kernel", "select_kernel", "quantize_kernel",
+                                     "merge_keys_kernel", "Memcpy", "Memset") if k in ev.name), ev.name[:40])
+            t = agg.setdefault(name, [0, 0.0])
+            t[0] += 1
+            t[1] += ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
+        kernels = {k: {"calls_per_rep": v[0] / a.reps, "us_per_rep": v[1] / a.reps} for k, v in agg.items()}
     gbs = [a.rows * (a.dim + 4) / (t * 1e-3) / 1e9 for t in times]
-    print(json.dumps({"rows": a.rows, "dim": a.dim, "k": a.k, "batch": a.batch, "ms": times,
-                      "gbs_per_pass": gbs}))
+    out = {"rows": a.rows, "dim": a.dim, "k": a.k, "batch": a.batch, "ms": times, "gbs_per_pass": gbs}
+    if kernels is not None:
+        out["kernels"] = kernels
+    print(json.dumps(out))
 
 
 if __name__ == "__main__":
