@@ -40,6 +40,7 @@ SIGNATURES = {
     "fi8_index_sync": (C.c_int, [_P]),
     "fi8_keys_unpack": (C.c_int, [_P, _I64, _P, _P]),
     "fi8_merge_keys_async": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P]),
+    "fi8_topk1_noalloc": (C.c_int, [_P, _P, _I32, _P, _P]),
 }
 
 

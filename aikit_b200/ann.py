@@ -174,6 +174,12 @@ class I8Index:
         check(lib().fi8_topk_batch_async(self._h, C.c_void_p(d_q), M, k, C.c_void_p(d_keys),
                                          C.c_void_p(stream or None)))
 
+    def topk1_noalloc(self, d_q: int, k: int, d_keys: int, stream: int = 0) -> None:
+        """fi8_topk1_noalloc: one query's top-k with the library's fixed scratch
+        (no device allocation on this call); device pointers, k <= 256."""
+        check(lib().fi8_topk1_noalloc(self._h, C.c_void_p(d_q), k, C.c_void_p(d_keys),
+                                      C.c_void_p(stream or None)))
+
     def sync(self) -> None:
         check(lib().fi8_index_sync(self._h))
 

@@ -646,3 +646,82 @@ int fi8_merge_keys_async(fi8_ctx* ctx, const uint64_t* d_in, int32_t nsrc, int32
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free single-query top-K (fi8_topk1_noalloc).
+//
+// For callers that must not allocate device memory while serving: a process
+// whose HBM is pre-reserved at start-up (the corpus plus a caching allocator's
+// pool) can see cudaMalloc fail on the query path, and cudaMalloc may
+// synchronize the device, stalling every other stream. fi8_topk_batch_async
+// grows its scratch with cudaMalloc on first use; this variant runs the same
+// scan kernel with its scratch in the fixed array below instead, and calls no
+// cudaMalloc, cudaFree or allocating library routine.
+//
+// The array exists once per device that loads this library and lives until
+// the process exits. It holds, for one query: the shared threshold and the
+// ticket counters (cleared before every call), kNoAllocMaxCtas per-CTA lists
+// and their per-block lists of up to kNoAllocMaxK keys. Every call on a device
+// shares it and it keeps the last call's contents, so two calls that overlap
+// on the GPU (on different streams, or on different indexes of the same
+// device) race; serialize them, e.g. on one stream.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int32_t kNoAllocMaxK = 256;      // keys per list (k rounded up to a power of two)
+constexpr int32_t kNoAllocMaxCtas = 160;   // >= the 148 SMs of a B200
+constexpr int32_t kNoAllocMaxBlocks = (kNoAllocMaxCtas + kMergeBlock - 1) / kMergeBlock;
+constexpr size_t kNoAllocHeader = 256;     // gthr @0, counter2 @8, counter[] @16
+constexpr size_t kNoAllocLvl1 = (size_t)kNoAllocMaxCtas * kNoAllocMaxK * sizeof(uint64_t);
+constexpr size_t kNoAllocLvl2 = (size_t)kNoAllocMaxBlocks * kNoAllocMaxK * sizeof(uint64_t);
+constexpr size_t kNoAllocBytes = kNoAllocHeader + kNoAllocLvl1 + kNoAllocLvl2;  // 368,896 bytes
+static_assert(16 + kNoAllocMaxBlocks * sizeof(unsigned int) <= kNoAllocHeader, "header overflow");
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[64] = {};  // device address of the array, per device ordinal
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+extern "C" int fi8_topk1_noalloc(fi8_index* idx, const float* d_q, int32_t k, uint64_t* d_keys, void* stream) {
+  if (!idx || !d_q || !d_keys) return fail(FI8_ERR_ARG, "fi8_topk1_noalloc: null argument");
+  if (k <= 0) return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d)", k);
+  if (k > kNoAllocMaxK)
+    return fail(FI8_ERR_ARG, "fi8_topk1_noalloc: k=%d exceeds the allocation-free limit of %d", k, kNoAllocMaxK);
+  ScanGeometry geo;
+  if (!scan_geometry(idx->dpad, k, true, &geo) || geo.kp > kNoAllocMaxK)
+    return fail(FI8_ERR_ARG, "fi8_topk1_noalloc: k=%d not supported for dim %d", k, idx->dim);
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  if (idx->device < 0 || idx->device >= 64) return fail(FI8_ERR_ARG, "fi8_topk1_noalloc: device ordinal");
+  unsigned char* base;
+  {
+    // Set-up, once per device and with that device current: in host code the
+    // array's name is only a stand-in, so ask the runtime for its address.
+    std::lock_guard<std::mutex> lk2(g_noalloc_mu);
+    if (!g_noalloc_ptr[idx->device]) {
+      void* ptr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "fi8_topk1_noalloc: cudaGetSymbolAddress");
+      g_noalloc_ptr[idx->device] = static_cast<unsigned char*>(ptr);
+    }
+    base = g_noalloc_ptr[idx->device];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  FI8_CUDA(cudaMemsetAsync(base, 0, kNoAllocHeader, st), "fi8_topk1_noalloc: clear counters");
+  ScanParams p = base_params(idx, geo);
+  const int32_t G = std::min<int32_t>(grid_ctas(idx, p), kNoAllocMaxCtas);
+  p.k = k;
+  p.kp = geo.kp;
+  p.cap = geo.cap;
+  p.gthr = reinterpret_cast<unsigned long long*>(base);
+  p.counter2 = reinterpret_cast<unsigned int*>(base + 8);
+  p.counter = reinterpret_cast<unsigned int*>(base + 16);
+  p.lvl1 = reinterpret_cast<uint64_t*>(base + kNoAllocHeader);
+  p.lvl2 = reinterpret_cast<uint64_t*>(base + kNoAllocHeader + kNoAllocLvl1);
+  p.q = d_q;
+  p.out_keys = d_keys;
+  cudaError_t e = scan_launch(p, true, 1, G, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fi8_topk1_noalloc: scan_launch");
+  idx->last_launches = 1;
+  return FI8_OK;
+}

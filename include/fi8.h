@@ -117,6 +117,20 @@ int fi8_keys_unpack(const uint64_t* keys, int64_t count, int32_t* out_idx, float
 int fi8_merge_keys_async(fi8_ctx* ctx, const uint64_t* d_in, int32_t nsrc, int32_t M, int32_t k,
                          uint64_t* d_out, void* stream);
 
+/* Allocation-free single-query top-K. No counterpart in the reference: it is
+ * for callers that must not allocate device memory while serving (HBM fully
+ * reserved at start-up, so a cudaMalloc on the query path could fail or
+ * stall the device). Same result as fi8_topk_batch_async with M = 1: d_q [dim]
+ * f32 and d_keys [k] packed keys, both device pointers supplied by the caller;
+ * stream is a cudaStream_t (NULL = the legacy default stream). It allocates
+ * nothing: its scratch is a fixed 368,896-byte array in the library (one per
+ * device, held until the process exits), so k is limited to 256 (a clear
+ * FI8_ERR_ARG above that). The first call on each device resolves that array's
+ * address (set-up; make that first call before any stream capture). Calls
+ * share the array, so two calls that overlap on the GPU race: serialize them.
+ * Does not synchronize; device errors surface at fi8_index_sync. */
+int fi8_topk1_noalloc(fi8_index* idx, const float* d_q, int32_t k, uint64_t* d_keys, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
