@@ -15,6 +15,9 @@ FI8_ERR_OOM = 4
 FI8_ERR_DEVICE = 5
 
 FI8_OPT_GEMM_MIN_BATCH = 1
+FI8_OPT_KERNEL_TIMING = 2
+# kernel classes of fi8_index_kernel_times, in index order
+KERNEL_KINDS = ("scan_kernel", "gemm_kernel", "select_kernel", "quantize_kernel")
 
 _P = C.c_void_p
 _I32 = C.c_int32
@@ -37,6 +40,7 @@ SIGNATURES = {
     "fi8_topk_batch_async": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
     "fi8_index_set_option": (C.c_int, [_P, C.c_int, _I64]),
     "fi8_index_last_launch_count": (C.c_int, [_P, _P]),
+    "fi8_index_kernel_times": (C.c_int, [_P, _P, _P, _P, C.c_int]),
     "fi8_index_sync": (C.c_int, [_P]),
     "fi8_keys_unpack": (C.c_int, [_P, _I64, _P, _P]),
     "fi8_merge_keys_async": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P]),

@@ -188,6 +188,23 @@ class I8Index:
         check(lib().fi8_index_last_launch_count(self._h, C.byref(v)))
         return v.value
 
+    def set_kernel_timing(self, on: bool) -> None:
+        """Record a CUDA event pair around every kernel this index launches."""
+        from ._ffi import FI8_OPT_KERNEL_TIMING
+        check(lib().fi8_index_set_option(self._h, FI8_OPT_KERNEL_TIMING, 1 if on else 0))
+
+    def kernel_times(self, reset: bool = True) -> dict:
+        """Per kernel class: launches, summed device ms and algorithmic bytes of
+        the launches timed since the last reset (waits for them to finish)."""
+        from ._ffi import KERNEL_KINDS
+        nk = len(KERNEL_KINDS)
+        launches = (C.c_int64 * nk)()
+        ms = (C.c_double * nk)()
+        nbytes = (C.c_double * nk)()
+        check(lib().fi8_index_kernel_times(self._h, launches, ms, nbytes, 1 if reset else 0))
+        return {name: {"launches": int(launches[i]), "ms": float(ms[i]), "bytes": float(nbytes[i])}
+                for i, name in enumerate(KERNEL_KINDS) if launches[i]}
+
     def set_gemm_min_batch(self, m: int) -> None:
         """Batches of at least m queries use the tensor-core GEMM path."""
         from ._ffi import FI8_OPT_GEMM_MIN_BATCH

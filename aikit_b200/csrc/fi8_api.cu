@@ -163,7 +163,52 @@ struct fi8_index {
   size_t topk_cap = 0;
   int32_t gemm_min_batch = 2;  // batches of at least this many queries use the GEMM path
   int32_t last_launches = 0;   // kernels launched by the last query call
+
+  // optional per-launch timing (FI8_OPT_KERNEL_TIMING)
+  struct TimedLaunch {
+    int kind;
+    cudaEvent_t e0, e1;
+    double bytes;
+  };
+  bool timing = false;
+  std::vector<TimedLaunch> timed;
+  std::vector<cudaEvent_t> event_pool;
 };
+
+namespace {
+
+cudaEvent_t take_event(fi8_index* x) {
+  cudaEvent_t e = nullptr;
+  if (!x->event_pool.empty()) {
+    e = x->event_pool.back();
+    x->event_pool.pop_back();
+  } else if (cudaEventCreate(&e) != cudaSuccess) {
+    e = nullptr;
+  }
+  return e;
+}
+
+// Bracket one kernel launch with events when timing is on. begin() returns the
+// start event (or null); end() records the stop event and files the launch.
+cudaEvent_t timer_begin(fi8_index* x, cudaStream_t st) {
+  if (!x->timing) return nullptr;
+  cudaEvent_t e = take_event(x);
+  if (e) cudaEventRecord(e, st);
+  return e;
+}
+
+void timer_end(fi8_index* x, cudaStream_t st, cudaEvent_t e0, int kind, double bytes) {
+  if (!e0) return;
+  cudaEvent_t e1 = take_event(x);
+  if (!e1) {
+    x->event_pool.push_back(e0);
+    return;
+  }
+  cudaEventRecord(e1, st);
+  x->timed.push_back(fi8_index::TimedLaunch{kind, e0, e1, bytes});
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -232,6 +277,11 @@ static void index_free(fi8_index* x) {
   cudaFree(x->d_topk);
   if (x->h_keys) cudaFreeHost(x->h_keys);
   if (x->h_err) cudaFreeHost(x->h_err);
+  for (auto& t : x->timed) {
+    cudaEventDestroy(t.e0);
+    cudaEventDestroy(t.e1);
+  }
+  for (cudaEvent_t e : x->event_pool) cudaEventDestroy(e);
   if (x->stream) cudaStreamDestroy(x->stream);
   delete x;
 }
@@ -356,6 +406,12 @@ static ScanParams base_params(fi8_index* x, const ScanGeometry& geo) {
   return p;
 }
 
+// Algorithmic bytes of a scan launch over mm queries: one pass over every
+// row's codes and scale per query, plus the float queries.
+static double scan_bytes(const fi8_index* x, int32_t mm) {
+  return (double)mm * ((double)x->n * (x->dim + 4) + (double)x->dim * 4);
+}
+
 static int32_t grid_ctas(fi8_index* x, const ScanParams& p) {
   int64_t G = std::min<int64_t>(x->sm_count > 0 ? x->sm_count : 1, p.ntiles);
   return (int32_t)std::max<int64_t>(G, 1);
@@ -383,8 +439,10 @@ static int launch_topk_scan(fi8_index* x, const float* d_q, int32_t M, int32_t k
     const int32_t mm = std::min(Mc, M - m0);
     p.q = d_q + (size_t)m0 * x->dim;
     p.out_keys = d_keys + (size_t)m0 * k;
+    cudaEvent_t t0 = timer_begin(x, st);
     cudaError_t e = scan_launch(p, true, mm, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(topk)");
+    timer_end(x, st, t0, FI8_KERNEL_SCAN, scan_bytes(x, mm));
     x->last_launches++;
   }
   return FI8_OK;
@@ -439,9 +497,11 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
     x->tmA_base = x->d_A;
     x->tmA_rows = A_rows;
   }
+  cudaEvent_t t0 = timer_begin(x, st);
   cudaError_t e = quantize_launch(d_q, M, Mpad, x->dim, x->dpad, x->d_A, x->d_qscale, x->d_thr, x->d_cnt,
                                   x->d_topk, kp, st);
   if (e != cudaSuccess) return cuda_fail(e, "quantize_launch");
+  timer_end(x, st, t0, FI8_KERNEL_QUANTIZE, (double)M * x->dim * 4 + (double)Mpad * x->dpad);
   x->last_launches++;
   std::vector<GemmLevel> ranges;
   plan_ranges(x->n, k, cap, &ranges);
@@ -463,12 +523,18 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
     p.rtiles = (p.row_hi - p.row_lo + kGemmBN - 1) / kGemmBN;
     const int64_t units = (int64_t)p.qtiles * p.rtiles;
     const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(x->sm_count, units));
+    t0 = timer_begin(x, st);
     e = gemm_launch(x->tmA, x->tmB, p, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_launch");
+    // the range's codes and scales, plus the int8 query tile
+    timer_end(x, st, t0, FI8_KERNEL_GEMM,
+              (double)(p.row_hi - p.row_lo) * (x->dim + 4) + (double)M * x->dim);
     const bool last = (i + 1 == ranges.size());
+    t0 = timer_begin(x, st);
     e = select_launch(M, k, kp, x->d_topk, x->d_thr, x->d_cnt, x->d_cand, cap, last ? d_keys : nullptr,
                       x->d_err, st);
     if (e != cudaSuccess) return cuda_fail(e, "select_launch");
+    timer_end(x, st, t0, FI8_KERNEL_SELECT, 0.0);
     x->last_launches += 2;
   }
   return FI8_OK;
@@ -490,8 +556,10 @@ static int launch_scores(fi8_index* x, const float* d_q, int32_t M, float* d_sco
     const int32_t mm = std::min(kScanMaxM, M - m0);
     p.q = d_q + (size_t)m0 * x->dim;
     p.out_scores = d_scores + (size_t)m0 * x->n;
+    cudaEvent_t t0 = timer_begin(x, st);
     cudaError_t e = scan_launch(p, false, mm, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(score)");
+    timer_end(x, st, t0, FI8_KERNEL_SCAN, scan_bytes(x, mm) + (double)mm * x->n * 4);
     x->last_launches++;
   }
   return FI8_OK;
@@ -596,6 +664,10 @@ int fi8_index_set_option(fi8_index* idx, int option, int64_t value) {
       if (value < 1) return fail(FI8_ERR_ARG, "fi8_index_set_option: GEMM_MIN_BATCH must be >= 1");
       idx->gemm_min_batch = (int32_t)std::min<int64_t>(value, 1 << 30);
       return FI8_OK;
+    case FI8_OPT_KERNEL_TIMING:
+      if (value != 0 && value != 1) return fail(FI8_ERR_ARG, "fi8_index_set_option: KERNEL_TIMING is 0 or 1");
+      idx->timing = value != 0;
+      return FI8_OK;
     default:
       return fail(FI8_ERR_ARG, "fi8_index_set_option: unknown option %d", option);
   }
@@ -605,6 +677,33 @@ int fi8_index_last_launch_count(fi8_index* idx, int32_t* out) {
   if (!idx || !out) return fail(FI8_ERR_ARG, "fi8_index_last_launch_count: null argument");
   std::lock_guard<std::mutex> lk(idx->mu);
   *out = idx->last_launches;
+  return FI8_OK;
+}
+
+int fi8_index_kernel_times(fi8_index* idx, int64_t* launches, double* ms, double* bytes, int reset) {
+  if (!idx || !launches || !ms || !bytes) return fail(FI8_ERR_ARG, "fi8_index_kernel_times: null argument");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  for (int i = 0; i < FI8_KERNEL_KINDS; i++) {
+    launches[i] = 0;
+    ms[i] = 0.0;
+    bytes[i] = 0.0;
+  }
+  for (const auto& t : idx->timed) {
+    FI8_CUDA(cudaEventSynchronize(t.e1), "fi8_index_kernel_times: event sync");
+    float dt = 0.0f;
+    FI8_CUDA(cudaEventElapsedTime(&dt, t.e0, t.e1), "fi8_index_kernel_times: elapsed time");
+    launches[t.kind] += 1;
+    ms[t.kind] += dt;
+    bytes[t.kind] += t.bytes;
+  }
+  if (reset) {
+    for (const auto& t : idx->timed) {
+      idx->event_pool.push_back(t.e0);
+      idx->event_pool.push_back(t.e1);
+    }
+    idx->timed.clear();
+  }
   return FI8_OK;
 }
 

@@ -43,8 +43,8 @@ constexpr int kStages = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kGemmThreads = 64 + kEpiThreads;
-constexpr int kBarEpi = 1;  // named barrier over the epilogue warps
 constexpr int kTmemCols = 512;  // two 256-column accumulators
+constexpr int kStageKeys = 4;   // staged candidate keys per epilogue thread
 constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024;  // + alignment slack
 
 // tcgen05 instruction descriptor, kind::i8: D = s32 (c_format 2), A and B
@@ -69,6 +69,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+
+// 8-byte asynchronous global -> shared copy (no registers held while in
+// flight); completion by cp_async_wait_all in the issuing thread.
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -117,14 +125,23 @@ __device__ __forceinline__ int tile_query_of(int r, int m_t) {
   return r;
 }
 
+// Move a thread's staged candidate keys into its query's global list.
+__device__ __forceinline__ void flush_staged(const GemmParams& p, int q, const uint64_t* stage, int staged) {
+  if (staged == 0) return;
+  unsigned int pos = atomicAdd(p.cnt + q, (unsigned int)staged);
+  uint64_t* dst = p.cand + (size_t)q * p.cap;
+  for (int j = 0; j < staged; j++, pos++)
+    if (pos < (unsigned int)p.cap) dst[pos] = stage[j];
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ uint64_t s_full[kStages], s_empty[kStages], s_tfull[2], s_tempty[2], s_done;
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
-  __shared__ __align__(16) float s_scale[2][kGemmBN];
-  __shared__ int s_eabort[2];
+  __shared__ __align__(16) float s_scale[kEpiWarps][2][64];  // per epilogue warp: its columns' row scales
+  __shared__ uint64_t s_stage[kEpiThreads][kStageKeys];       // per epilogue thread: staged candidates
 
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -225,48 +242,72 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------ epilogue ------------------------------
     // Warp w reads TMEM lanes 32*(w%4).. (its queries) and columns
-    // 64*((w-2)/4).. of each 256-column accumulator.
-    const int etid = threadIdx.x - 64;
+    // 64*((w-2)/4).. of each 256-column accumulator. Each warp stages the 64
+    // row scales of its own columns in a private shared slice and loads the
+    // next unit's while it filters this one, so the epilogue warps never wait
+    // for one another or for a scale load.
+    const int ew = warp - 2;
     const int quarter = warp & 3;
-    const int cq = (warp - 2) >> 2;
+    const int cq = ew >> 2;
+    const int r = quarter * 32 + lane;  // A row / TMEM lane of this thread
+    float* const my_scale = &s_scale[ew][0][0];
+    if (my_units > 0) {
+      const int64_t row0 = p.row_lo + ((int64_t)blockIdx.x / p.qtiles) * kGemmBN;
+      cp_async8(my_scale + 2 * lane, p.scales + row0 + cq * 64 + 2 * lane);
+    }
+    cp_async_commit();
+    // per-query state of the current query tile (constant within a launch)
+    // (a lane without a query gets qs = 0 and Tscore = +inf: it never passes)
+    int cur_qt = -1, q = 0;
+    uint64_t* const my_stage = s_stage[ew * 32 + lane];
+    int staged = 0;  // candidates held in my_stage, not yet in the global list
+    float qs = 0.0f, Tscore = INFINITY;
+    unsigned long long T = ~0ull;
     for (int64_t u = 0; u < my_units; u++) {
       const int64_t unit = blockIdx.x + u * G;
       const int qt = (int)(unit % p.qtiles);
       const int64_t rt = unit / p.qtiles;
       const int64_t row0 = p.row_lo + rt * kGemmBN;
       const int b = (int)(u & 1);
-      const int m_t = min(kGemmBM, p.M - qt * kGemmBM);
-      const int r = quarter * 32 + lane;  // A row / TMEM lane of this thread
-      const int j = tile_query_of(r, m_t);
-      const bool valid_q = j >= 0 && j < m_t;
-      const int q = qt * kGemmBM + j;
-      const float qs = valid_q ? p.qscale[qt * kGemmBM + r] : 0.0f;
-      const bool qzero = qs == 0.0f;  // an all-zero query scores exactly 0
-      const unsigned long long T = valid_q ? p.thr[q] : ~0ull;
-      const float Tscore = (T == 0ull) ? -INFINITY : key_score(T);
-      // this unit's 256 row scales, once, for every epilogue warp
-      if (etid < kGemmBN) s_scale[b][etid] = p.scales[row0 + etid];
-      // abort decision, uniform over the epilogue warps: sampled by one thread
-      // before the barrier, read by all after it (parity-buffered, so a fast
-      // thread cannot overwrite it while a slow one still reads)
-      if (etid == 0) s_eabort[b] = s_abort;
-      named_sync(kBarEpi, kEpiThreads);
-      if (s_eabort[b]) break;
+      if (qt != cur_qt) {
+        flush_staged(p, q, my_stage, staged);  // staged keys belong to the previous tile's query
+        staged = 0;
+        cur_qt = qt;
+        const int m_t = min(kGemmBM, p.M - qt * kGemmBM);
+        const int j = tile_query_of(r, m_t);
+        const bool valid_q = j >= 0 && j < m_t;
+        q = qt * kGemmBM + j;
+        qs = valid_q ? p.qscale[qt * kGemmBM + r] : 0.0f;
+        T = valid_q ? p.thr[q] : ~0ull;
+        Tscore = !valid_q ? INFINITY : (T == 0ull) ? -INFINITY : key_score(T);
+      }
+      if (s_abort) break;
+      // this unit's scales (copied during the previous unit) have landed;
+      // start the copy of the next unit's into the other slot
+      cp_async_wait_all();
+      __syncwarp();
+      if (u + 1 < my_units) {
+        const int64_t nrow0 = p.row_lo + ((unit + G) / p.qtiles) * kGemmBN;
+        cp_async8(my_scale + (b ^ 1) * 64 + 2 * lane, p.scales + nrow0 + cq * 64 + 2 * lane);
+      }
+      cp_async_commit();
       if (!mbar_wait_bounded(&s_tfull[b], (uint32_t)((u / 2) & 1))) {
         s_abort = 1;
         atomicOr(p.err, 1u);
+        break;
       }
       tc_fence_after();
       const int64_t lim = p.row_hi - row0;  // valid columns of this tile
 #pragma unroll 1
       for (int c = 0; c < 2; c++) {
         const int col0 = cq * 64 + c * 32;
+        const float* scl = my_scale + b * 64 + c * 32;
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kGemmBN + col0), v);
         // branch-free pass: the plain product equals the exact (x86 NaN
         // semantics) score whenever it is not NaN, and NaN never passes
         uint32_t mask = 0;
-        const float4* s4 = reinterpret_cast<const float4*>(&s_scale[b][col0]);
+        const float4* s4 = reinterpret_cast<const float4*>(scl);
 #pragma unroll
         for (int i4 = 0; i4 < 8; i4++) {
           const float4 rs = s4[i4];
@@ -274,23 +315,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int t = 0; t < 4; t++) {
             const int i = i4 * 4 + t;
-            float sc = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), rsv[t]);
-            sc = qzero ? 0.0f : sc;
+            const float sc = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), rsv[t]);
             mask |= (sc >= Tscore ? 1u : 0u) << i;
           }
         }
-        if (!valid_q) mask = 0u;
+        if (qs == 0.0f) mask = (0.0f >= Tscore) ? 0xFFFFFFFFu : 0u;  // an all-zero query scores exactly 0
         if (col0 + 32 > lim) mask &= (col0 >= lim) ? 0u : ((1u << (uint32_t)(lim - col0)) - 1u);
         if (mask) {
+          // Survivors go to this thread's few shared staging slots while they
+          // fit; otherwise one reservation in the query's global list takes
+          // the staged keys and this chunk's. A survivor's score is the plain
+          // product (it is not NaN) or exactly 0 for an all-zero query. A
+          // survivor whose key does not beat the threshold (a score tie at
+          // Tscore with a higher index) leaves an empty key, which the select
+          // skips.
+          const int nm = __popc(mask);
+          uint64_t* dst;
+          unsigned int pos, lim;
+          if (staged + nm <= kStageKeys) {
+            dst = my_stage;
+            pos = (unsigned int)staged;
+            lim = kStageKeys;
+            staged += nm;
+          } else {
+            pos = atomicAdd(p.cnt + q, (unsigned int)(staged + nm));
+            dst = p.cand + (size_t)q * p.cap;
+            lim = (unsigned int)p.cap;
+            for (int j = 0; j < staged; j++, pos++)
+              if (pos < lim) dst[pos] = my_stage[j];
+            staged = 0;
+          }
+          const uint32_t id0 = p.id_base + (uint32_t)(row0 + col0);
 #pragma unroll
           for (int i = 0; i < 32; i++) {
             if ((mask >> i) & 1u) {
-              const float score = w8a8_score((int32_t)v[i], qs, s_scale[b][col0 + i]);
-              const uint64_t key = make_key(score, p.id_base + (uint32_t)(row0 + col0 + i));
-              if (key > T) {
-                const unsigned int pos = atomicAdd(p.cnt + q, 1u);
-                if (pos < (unsigned int)p.cap) p.cand[(size_t)q * p.cap + pos] = key;
-              }
+              const float sc =
+                  qs == 0.0f ? 0.0f : __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), scl[i]);
+              const uint64_t key = make_key(sc, id0 + (uint32_t)i);
+              if (pos < lim) dst[pos] = key > T ? key : kEmptyKey;
+              pos++;
             }
           }
         }
@@ -299,6 +362,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive1(&s_tempty[b]);
     }
+    cp_async_wait_all();  // no copy into shared memory outlives the loop
+    flush_staged(p, q, my_stage, staged);
   }
   tc_fence_before();
   __syncthreads();
@@ -361,16 +426,57 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* q, int M, in
 // running top-k. The carried list holds keys of earlier ranges (all >= the
 // threshold the candidates passed), so top-k of the union is exact.
 constexpr int kSelThreads = 1024;
+constexpr int kRadixBins = 256;
 
+// Streaming form, for a union larger than the shared buffer: append, and sort
+// and cut the buffer to the best k whenever it nears full. Leaves the kept
+// keys sorted in buf[0..*s_count).
+__device__ void select_stream(int k, int cap_s, const uint64_t* mine, int kp, const uint64_t* src, int n_c,
+                              uint64_t* buf, int* s_count, unsigned long long* s_local_thr, int tid, int bar) {
+  for (int i0 = 0; i0 < kp; i0 += kSelThreads) {
+    const int i = i0 + tid;
+    const uint64_t key = i < kp ? mine[i] : kEmptyKey;
+    warp_append(key != kEmptyKey, key, buf, s_count);
+  }
+  named_sync(bar, kSelThreads);
+  if (*s_count > cap_s - kSelThreads)
+    group_compact<kSelThreads>(buf, *s_count, k, s_count, s_local_thr, nullptr, tid, bar);
+  for (int b0 = 0; b0 < n_c; b0 += kSelThreads) {
+    const int e = b0 + tid;
+    uint64_t key = kEmptyKey;
+    bool take = false;
+    if (e < n_c) {
+      key = src[e];
+      take = key > *s_local_thr;
+    }
+    warp_append(take, key, buf, s_count);
+    named_sync(bar, kSelThreads);
+    const int cnow = *s_count;
+    if (cnow > cap_s - kSelThreads)
+      group_compact<kSelThreads>(buf, cnow, k, s_count, s_local_thr, nullptr, tid, bar);
+  }
+  named_sync(bar, kSelThreads);
+  group_compact<kSelThreads>(buf, *s_count, k, s_count, s_local_thr, nullptr, tid, bar);
+}
+
+// Usual form: the union fits in shared memory. An MSD radix select (8-bit
+// digits, most significant first) finds the digit prefix that exactly the k
+// best keys match or exceed -- keys are distinct, so the walk ends at a digit
+// bucket whose whole count is still needed -- and one pass keeps those keys.
+// Only the last range's select sorts (its output is the answer).
 __global__ void __launch_bounds__(kSelThreads, 1)
     select_kernel(int k, int kp, int cap_s, uint64_t* topk, unsigned long long* thr, unsigned int* cnt,
                   const uint64_t* cand, int cap, uint64_t* out, unsigned int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_count;
-  __shared__ unsigned long long s_local_thr;
-  uint64_t* buf = reinterpret_cast<uint64_t*>(smem);
+  __shared__ unsigned long long s_local_thr, s_prefix, s_mask, s_min;
+  __shared__ unsigned int s_hist[kRadixBins];
+  __shared__ int s_rank, s_done;
+  uint64_t* buf = reinterpret_cast<uint64_t*>(smem);  // [cap_s] the union
+  uint64_t* sel = buf + cap_s;                         // [kp] the kept keys
   const int qi = blockIdx.x;
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
   constexpr int bar = 1;
   if (tid == 0) {
     s_count = 0;
@@ -378,40 +484,118 @@ __global__ void __launch_bounds__(kSelThreads, 1)
   }
   named_sync(bar, kSelThreads);
   uint64_t* mine = topk + (size_t)qi * kp;
-  for (int i0 = 0; i0 < kp; i0 += kSelThreads) {
-    const int i = i0 + tid;
-    const uint64_t key = i < kp ? mine[i] : kEmptyKey;
-    warp_append(key != kEmptyKey, key, buf, &s_count);
-  }
-  named_sync(bar, kSelThreads);
   const unsigned int c_all = cnt[qi];
   if (c_all > (unsigned int)cap && tid == 0) atomicOr(err, 2u);  // candidates were dropped
   const int n_c = (int)(c_all < (unsigned int)cap ? c_all : (unsigned int)cap);
   const uint64_t* src = cand + (size_t)qi * cap;
-  if (s_count > cap_s - kSelThreads)
-    group_compact<kSelThreads>(buf, s_count, k, &s_count, &s_local_thr, nullptr, tid, bar);
-  for (int b0 = 0; b0 < n_c; b0 += kSelThreads) {
-    const int e = b0 + tid;
-    uint64_t key = kEmptyKey;
-    bool take = false;
-    if (e < n_c) {
-      key = src[e];
-      take = key > s_local_thr;
+
+  const uint64_t* kept;  // the kept keys (<= kp of them) and how many
+  int nkept;
+  bool sorted;
+  if (kp + n_c > cap_s) {
+    select_stream(k, cap_s, mine, kp, src, n_c, buf, &s_count, &s_local_thr, tid, bar);
+    kept = buf;
+    nkept = s_count;
+    sorted = true;
+  } else {
+    for (int i0 = 0; i0 < kp; i0 += kSelThreads) {
+      const int i = i0 + tid;
+      const uint64_t key = i < kp ? mine[i] : kEmptyKey;
+      warp_append(key != kEmptyKey, key, buf, &s_count);
     }
-    warp_append(take, key, buf, &s_count);
+    for (int b0 = 0; b0 < n_c; b0 += kSelThreads) {
+      const int e = b0 + tid;
+      const uint64_t key = e < n_c ? src[e] : kEmptyKey;
+      warp_append(key != kEmptyKey, key, buf, &s_count);
+    }
+    if (tid == 0) {
+      s_prefix = 0ull;
+      s_mask = 0ull;
+      s_min = ~0ull;
+      s_rank = k;
+      s_done = 0;
+    }
     named_sync(bar, kSelThreads);
-    const int cnow = s_count;
-    if (cnow > cap_s - kSelThreads)
-      group_compact<kSelThreads>(buf, cnow, k, &s_count, &s_local_thr, nullptr, tid, bar);
+    const int n = s_count;
+    if (n > k) {
+      for (int shift = 56; shift >= 0; shift -= 8) {
+        if (tid < kRadixBins) s_hist[tid] = 0u;
+        named_sync(bar, kSelThreads);
+        const unsigned long long prefix = s_prefix, mask = s_mask;
+        for (int i0 = 0; i0 < n; i0 += kSelThreads) {
+          const int i = i0 + tid;
+          const uint64_t key = i < n ? buf[i] : kEmptyKey;
+          const bool live = i < n && (key & mask) == prefix;
+          const unsigned int bin = live ? (unsigned int)(key >> shift) & 0xFFu : 0x100u;
+          const unsigned int same = __match_any_sync(0xffffffffu, bin);
+          if (live && lane == __ffs(same) - 1) atomicAdd(&s_hist[bin], (unsigned int)__popc(same));
+        }
+        named_sync(bar, kSelThreads);
+        if (tid < 32) {
+          // lane l holds bins 255-8l .. 248-8l (descending); find the bin
+          // where the running count from the top reaches the rank
+          unsigned int c[8], sum = 0;
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            c[j] = s_hist[255 - 8 * lane - j];
+            sum += c[j];
+          }
+          unsigned int incl = sum;
+#pragma unroll
+          for (int off = 1; off < 32; off <<= 1) {
+            const unsigned int t = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += t;
+          }
+          const unsigned int rank = (unsigned int)s_rank;
+          const unsigned int excl = incl - sum;
+          const unsigned int hit = __ballot_sync(0xffffffffu, excl < rank && rank <= incl);
+          if (lane == __ffs(hit) - 1) {
+            unsigned int cum = excl;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              if (cum + c[j] >= rank) {
+                const unsigned int digit = 255u - 8u * lane - j;
+                s_prefix = prefix | ((unsigned long long)digit << shift);
+                s_mask = mask | (0xFFull << shift);
+                s_rank = (int)(rank - cum);
+                s_done = (c[j] == rank - cum) ? 1 : 0;
+                break;
+              }
+              cum += c[j];
+            }
+          }
+        }
+        named_sync(bar, kSelThreads);
+        if (s_done) break;
+      }
+    }
+    // keep every key at or above the prefix (exactly min(n, k) of them)
+    if (tid == 0) s_count = 0;
+    named_sync(bar, kSelThreads);
+    const unsigned long long prefix = s_prefix, mask = s_mask;
+    for (int i0 = 0; i0 < n; i0 += kSelThreads) {
+      const int i = i0 + tid;
+      const uint64_t key = i < n ? buf[i] : kEmptyKey;
+      const bool take = i < n && (key & mask) >= prefix;
+      if (take) atomicMin(&s_min, (unsigned long long)key);
+      warp_append(take, key, sel, &s_count);
+    }
+    named_sync(bar, kSelThreads);
+    kept = sel;
+    nkept = s_count;
+    sorted = false;
+    if (out) {
+      for (int i = nkept + tid; i < kp; i += kSelThreads) sel[i] = kEmptyKey;
+      named_sync(bar, kSelThreads);
+      group_sort_desc<kSelThreads>(sel, kp, tid, bar);
+      sorted = true;
+    }
   }
-  named_sync(bar, kSelThreads);
-  group_compact<kSelThreads>(buf, s_count, k, &s_count, &s_local_thr, nullptr, tid, bar);
-  const int fin = s_count;
-  for (int i = tid; i < kp; i += kSelThreads) mine[i] = i < fin ? buf[i] : kEmptyKey;
+  for (int i = tid; i < kp; i += kSelThreads) mine[i] = i < nkept ? kept[i] : kEmptyKey;
   if (out)
-    for (int i = tid; i < k; i += kSelThreads) out[(size_t)qi * k + i] = i < fin ? buf[i] : kEmptyKey;
+    for (int i = tid; i < k; i += kSelThreads) out[(size_t)qi * k + i] = i < nkept ? kept[i] : kEmptyKey;
   if (tid == 0) {
-    thr[qi] = fin >= k ? buf[k - 1] : 0ull;
+    thr[qi] = nkept >= k ? (sorted ? kept[k - 1] : s_min) : 0ull;
     cnt[qi] = 0u;
   }
 }
@@ -476,10 +660,11 @@ cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsi
   // compactions (a compaction is a bitonic sort of the buffer)
   int cap_s = pow2_ge(kp + kSelThreads);
   if (cap_s < 4096) cap_s = 4096;
-  if (cap_s > 8192) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 * 8);
+  if (cap_s > 8192 || kp > 4096) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)(cap_s + kp) * 8;  // union buffer + kept list
+  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (8192 + 4096) * 8);
   if (e != cudaSuccess) return e;
-  select_kernel<<<M, kSelThreads, (size_t)cap_s * 8, stream>>>(k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
+  select_kernel<<<M, kSelThreads, smem, stream>>>(k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
   return cudaGetLastError();
 }
 

@@ -58,6 +58,39 @@ def algorithmic_bytes(n_rows: int, d: int, m: int) -> int:
     return n_rows * (d + 4) + m * d * 4
 
 
+# DRAM traffic of one launch from an ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum) next to that launch's algorithmic bytes; the ratio
+# scales the bench's average launch. Summaries: profiles/<kernel>_*.md.
+NCU_TRAFFIC = {
+    "gemm_kernel": {"dram_bytes": 1.342146e9 + 6.028544e6, "algorithmic_bytes": 1_737_856 * (DIM + 4) + 64 * DIM,
+                    "profile": "profiles/gemm_kernel_c2_batch64.md"},
+    "scan_kernel": {"dram_bytes": 3.088212e9 + 4.358144e6, "algorithmic_bytes": 4_000_000 * (DIM + 4) + DIM * 4,
+                    "profile": "profiles/scan_kernel_c2_batch1.md"},
+}
+
+
+def kernel_roofline(kt: dict, kernel: str, pk: dict, pk_kind: str, region_ms: float) -> dict:
+    """Roofline of the dominant kernel from the library's per-launch CUDA events
+    over the timed region: algorithmic bytes per launch / mean launch time."""
+    t = kt[kernel]
+    per_launch_bytes = t["bytes"] / t["launches"]
+    per_launch_ms = t["ms"] / t["launches"]
+    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
+    ncu = NCU_TRAFFIC[kernel]
+    return {
+        "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+        "frac": achieved / pk["hbm_gbs"],
+        "traffic": per_launch_bytes * ncu["dram_bytes"] / ncu["algorithmic_bytes"],
+        "kernel": kernel, "launches": t["launches"], "ms_per_launch": per_launch_ms,
+        "algorithmic_bytes_per_launch": per_launch_bytes,
+        "share_of_region": t["ms"] / region_ms,
+        "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
+        "traffic_source": f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
+                          "times this run's mean launch bytes",
+        "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json copy bandwidth)",
+    }
+
+
 # ----------------------------------------------------------------------------
 # clocks during the timed region (NVML sampler)
 # ----------------------------------------------------------------------------
@@ -215,6 +248,9 @@ def main():
     def timed(nsteps, m):
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
+        # per-kernel CUDA events (recorded by the library on this stream)
+        ix.kernel_times(reset=True)
+        ix.set_kernel_timing(True)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -224,12 +260,14 @@ def main():
             launches += step(i, m)
         ev1.record(stream)
         torch.cuda.synchronize()
+        ix.set_kernel_timing(False)
+        kt = ix.kernel_times(reset=True)
         ms = ev0.elapsed_time(ev1)
         if world > 1:
             t = torch.tensor([ms], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
-        return ms, launches
+        return ms, launches, kt
 
     # warm-up (both batch forms), then the timed regions
     for i in range(args.warmup):
@@ -239,8 +277,8 @@ def main():
     ix.sync()
 
     with ClockSampler(local) as clk:
-        ms64, launches = timed(args.steps, BATCH)
-        ms1, launches1 = timed(args.steps, 1) if world == 1 else (None, 0)
+        ms64, launches, kt64 = timed(args.steps, BATCH)
+        ms1, launches1, kt1 = timed(args.steps, 1) if world == 1 else (None, 0, {})
     ix.sync()
 
     # e2e through the public C ABI with host buffers (pinned), N=1: fi8_topk_batch
@@ -291,10 +329,7 @@ def main():
     shard_rows = hi - lo
     per_step_ms = ms64 / args.steps
     value = BATCH * args.steps / (ms64 / 1e3)
-    # dominant kernel: the fused scan+top-K launch; its time per launch is the
-    # step time minus the (tiny) merge at N>1, measured here as the step time.
-    bytes64 = algorithmic_bytes(shard_rows, DIM, BATCH)
-    ach64 = bytes64 / (per_step_ms / 1e3) / 1e9
+    roof64 = kernel_roofline(kt64, "gemm_kernel", pk, pk_kind, per_step_ms * args.steps)
     out = {
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step_ms,
@@ -304,22 +339,15 @@ def main():
                    "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
                    "l2": "corpus 7.7 GB >> 126 MB L2: no flush needed",
                    "corpus_gen_s": round(gen_s, 1)},
-        "roofline": {"bound": "hbm", "achieved": ach64, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": ach64 / pk["hbm_gbs"], "traffic": None,
-                     "kernel": "scan_kernel<true> (fused W8A8 scan + top-K)",
-                     "algorithmic_bytes_per_launch": bytes64,
-                     "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json copy bandwidth)"},
+        "roofline": roof64,
         "gpu_launches": launches + launches1,
         "e2e": e2e,
         "clocks": clk.summary(),
     }
     if ms1 is not None:
         per1 = ms1 / args.steps
-        bytes1 = algorithmic_bytes(shard_rows, DIM, 1)
         out["batch1"] = {"value": 1e3 / per1, "unit": "queries/s", "ms_per_query": per1,
-                         "roofline": {"bound": "hbm", "achieved": bytes1 / (per1 / 1e3) / 1e9,
-                                      "peak": pk["hbm_gbs"], "unit": "GB/s",
-                                      "frac": bytes1 / (per1 / 1e3) / 1e9 / pk["hbm_gbs"]}}
+                         "roofline": kernel_roofline(kt1, "scan_kernel", pk, pk_kind, ms1)}
     if world == 1:
         out["cpu_baseline"] = cpu_baseline()
     print(json.dumps(out))

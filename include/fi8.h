@@ -99,7 +99,27 @@ int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k,
  * many queries take the tcgen05 GEMM path, smaller ones the per-query scan
  * (default 2). Both return identical results. */
 #define FI8_OPT_GEMM_MIN_BATCH 1
+/* FI8_OPT_KERNEL_TIMING: 1 records a CUDA event pair around every kernel the
+ * index launches (on the launch stream), read back by fi8_index_kernel_times;
+ * 0 (default) records nothing. A measurement aid with no counterpart in the
+ * reference. */
+#define FI8_OPT_KERNEL_TIMING 2
 int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
+
+/* Kernel classes reported by fi8_index_kernel_times. */
+#define FI8_KERNEL_SCAN 0     /* fused W8A8 scan + top-K (or scores) */
+#define FI8_KERNEL_GEMM 1     /* tcgen05 GEMM with threshold-filter epilogue */
+#define FI8_KERNEL_SELECT 2   /* per-query exact select of the candidates */
+#define FI8_KERNEL_QUANTIZE 3 /* batch query quantization */
+#define FI8_KERNEL_KINDS 4
+
+/* Totals over the launches timed since the last reset, per kernel class:
+ * launches[i], ms[i] (sum of per-launch device durations) and bytes[i]
+ * (algorithmic bytes: corpus codes + scales of the rows each launch covers,
+ * times the passes it makes, plus its query bytes). Each array holds
+ * FI8_KERNEL_KINDS entries. Waits for the timed launches to finish; reset != 0
+ * then clears the totals. */
+int fi8_index_kernel_times(fi8_index* idx, int64_t* launches, double* ms, double* bytes, int reset);
 
 /* Number of kernels the index's last query call launched (scan: one per 64
  * queries; batched: quantize + a GEMM and a select per row range). */
