@@ -305,7 +305,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kGemmBN + col0), v);
         // branch-free pass: the plain product equals the exact (x86 NaN
-        // semantics) score whenever it is not NaN, and NaN never passes
+        // semantics) score whenever it is not NaN, and NaN never passes. The
+        // score replaces the accumulator in v for the append below.
         uint32_t mask = 0;
         const float4* s4 = reinterpret_cast<const float4*>(scl);
 #pragma unroll
@@ -316,44 +317,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int t = 0; t < 4; t++) {
             const int i = i4 * 4 + t;
             const float sc = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), rsv[t]);
+            v[i] = __float_as_uint(sc);
             mask |= (sc >= Tscore ? 1u : 0u) << i;
           }
         }
-        if (qs == 0.0f) mask = (0.0f >= Tscore) ? 0xFFFFFFFFu : 0u;  // an all-zero query scores exactly 0
+        if (qs == 0.0f) {  // an all-zero query scores exactly 0
+          mask = (0.0f >= Tscore) ? 0xFFFFFFFFu : 0u;
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = 0u;
+        }
         if (col0 + 32 > lim) mask &= (col0 >= lim) ? 0u : ((1u << (uint32_t)(lim - col0)) - 1u);
         if (mask) {
           // Survivors go to this thread's few shared staging slots while they
           // fit; otherwise one reservation in the query's global list takes
-          // the staged keys and this chunk's. A survivor's score is the plain
-          // product (it is not NaN) or exactly 0 for an all-zero query. A
-          // survivor whose key does not beat the threshold (a score tie at
-          // Tscore with a higher index) leaves an empty key, which the select
-          // skips.
+          // the staged keys and this chunk's. A survivor whose key does not
+          // beat the threshold (a score tie at Tscore with a higher index)
+          // leaves an empty key, which the select skips.
           const int nm = __popc(mask);
           uint64_t* dst;
-          unsigned int pos, lim;
+          unsigned int pos, room;
           if (staged + nm <= kStageKeys) {
             dst = my_stage;
             pos = (unsigned int)staged;
-            lim = kStageKeys;
+            room = kStageKeys;
             staged += nm;
           } else {
             pos = atomicAdd(p.cnt + q, (unsigned int)(staged + nm));
             dst = p.cand + (size_t)q * p.cap;
-            lim = (unsigned int)p.cap;
+            room = (unsigned int)p.cap;
             for (int j = 0; j < staged; j++, pos++)
-              if (pos < lim) dst[pos] = my_stage[j];
+              if (pos < room) dst[pos] = my_stage[j];
             staged = 0;
           }
           const uint32_t id0 = p.id_base + (uint32_t)(row0 + col0);
+          // survivors are sparse: visit only the 4-column groups that hold one
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            if ((mask >> i) & 1u) {
-              const float sc =
-                  qs == 0.0f ? 0.0f : __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), scl[i]);
-              const uint64_t key = make_key(sc, id0 + (uint32_t)i);
-              if (pos < lim) dst[pos] = key > T ? key : kEmptyKey;
-              pos++;
+          for (int g = 0; g < 8; g++) {
+            const uint32_t nib = (mask >> (4 * g)) & 0xFu;
+            if (nib) {
+#pragma unroll
+              for (int t = 0; t < 4; t++) {
+                if ((nib >> t) & 1u) {
+                  const int i = 4 * g + t;
+                  const uint64_t key = make_key(__uint_as_float(v[i]), id0 + (uint32_t)i);
+                  if (pos < room) dst[pos] = key > T ? key : kEmptyKey;
+                  pos++;
+                }
+              }
             }
           }
         }
