@@ -17,7 +17,7 @@ FI8_ERR_DEVICE = 5
 FI8_OPT_GEMM_MIN_BATCH = 1
 FI8_OPT_KERNEL_TIMING = 2
 # kernel classes of fi8_index_kernel_times, in index order
-KERNEL_KINDS = ("scan_kernel", "gemm_kernel", "select_kernel", "quantize_kernel")
+KERNEL_KINDS = ("scan_kernel", "gemm_kernel", "select_kernel", "quantize_kernel", "rerank_kernel")
 
 _P = C.c_void_p
 _I32 = C.c_int32
@@ -45,6 +45,12 @@ SIGNATURES = {
     "fi8_keys_unpack": (C.c_int, [_P, _I64, _P, _P]),
     "fi8_merge_keys_async": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P]),
     "fi8_topk1_noalloc": (C.c_int, [_P, _P, _I32, _P, _P]),
+    "fi8_bin_index_create": (C.c_int, [_P, _P, _I32, _P, _P, _P, _I64, _I32, _I32, _I64, _P]),
+    "fi8_bin_index_destroy": (C.c_int, [_P]),
+    "fi8_bin_index_handle": (C.c_int, [_P, _P]),
+    "fi8_bin_query_topk": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
+    "fi8_bin_prefilter_async": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
+    "fi8_bin_rerank_async": (C.c_int, [_P, _P, _I32, _P, _I32, _I32, _P, _P]),
 }
 
 

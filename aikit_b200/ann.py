@@ -101,6 +101,25 @@ class B200Backend:
                               f"{scales.shape[0]}, n={n} dim={dim})")
         return I8Index(self.ctx, bq, scales, n, dim, id_base)
 
+    def NewBinaryI8Index(self, codes, words: int, center, bq, scales, n: int, dim: int,
+                         overquery: int = 16, id_base: int = 0) -> "BinaryI8Index":
+        """A device FlatBinaryI8 shard from the prefilter's packed codes
+        [n*words] uint64 and center [dim] (None: uncentred), plus the FlatI8
+        rows bq [n*dim] int8 and scales [n] (ann/flat_binary_i8.go:57-62).
+        overquery defaults to DefaultOverquery (ann/flat_binary_prefilter.go:51)."""
+        codes = np.ascontiguousarray(codes, dtype=np.uint64).reshape(-1)
+        bq = np.ascontiguousarray(bq, dtype=np.int8).reshape(-1)
+        scales = _f32(scales).reshape(-1)
+        if n <= 0 or dim <= 0:
+            raise Fi8Error(1, f"gpu: empty binary index (n={n} dim={dim})")
+        if codes.shape[0] != n * words or bq.shape[0] != n * dim or scales.shape[0] != n:
+            raise Fi8Error(1, "gpu: binary index shape mismatch")
+        if center is not None:
+            center = _f32(center).reshape(-1)
+            if center.shape[0] != dim:
+                raise Fi8Error(1, f"gpu: center len {center.shape[0]} != dim {dim}")
+        return BinaryI8Index(self.ctx, codes, words, center, bq, scales, n, dim, overquery, id_base)
+
 
 class I8Index:
     """A device-resident FlatI8 shard: I8Index + I8BatchIndex + I8TopKIndex."""
@@ -223,6 +242,88 @@ class I8Index:
         if not rows:
             return np.empty((0, self.dim), np.float32)
         return _f32(np.stack([_f32(q) for q in rows]))
+
+    def __del__(self):
+        try:
+            self.Close()
+        except Exception:
+            pass
+
+
+class BinaryI8Index:
+    """A device-resident FlatBinaryI8 shard (ann/flat_binary_i8.go): the sign-bit
+    Hamming prefilter, then the int8 W8A8 rerank of its shortlist."""
+
+    def __init__(self, ctx: Context, codes, words, center, bq, scales, n, dim, overquery, id_base):
+        h = C.c_void_p()
+        cptr = _p(center) if center is not None else None
+        check(lib().fi8_bin_index_create(ctx.handle, _p(codes), words, cptr, _p(bq), _p(scales), n, dim,
+                                         overquery, id_base, C.byref(h)))
+        self._h = h
+        ih = C.c_void_p()
+        check(lib().fi8_bin_index_handle(h, C.byref(ih)))
+        self._ih = ih
+        self.ctx = ctx
+        self.n = n
+        self.dim = dim
+        self.words = words
+        self.overquery = max(int(overquery), 1)
+        self.id_base = id_base
+
+    def Query(self, q, k: int) -> list[Hit]:
+        """FlatBinaryI8.Query (flat_binary_i8.go:78) for one query."""
+        return self.QueryBatch([q], k)[0]
+
+    def QueryBatch(self, queries, k: int) -> list[list[Hit]]:
+        idx, sc = self.topk_arrays(queries, k)
+        return [[Hit(int(i), float(s)) for i, s in zip(idx[m], sc[m]) if i >= 0] for m in range(idx.shape[0])]
+
+    def topk_arrays(self, queries, k: int):
+        Q = _f32(np.asarray(queries, dtype=np.float32).reshape(-1, self.dim))
+        M = Q.shape[0]
+        idx = np.empty((M, max(k, 0)), np.int32)
+        sc = np.empty((M, max(k, 0)), np.float32)
+        if M == 0:
+            return idx, sc
+        check(lib().fi8_bin_query_topk(self._h, _p(Q), M, k, _p(idx), _p(sc)))
+        return idx, sc
+
+    def prefilter_async(self, d_q: int, M: int, cand: int, d_keys: int, stream: int = 0) -> None:
+        check(lib().fi8_bin_prefilter_async(self._h, C.c_void_p(d_q), M, cand, C.c_void_p(d_keys),
+                                            C.c_void_p(stream or None)))
+
+    def rerank_async(self, d_q: int, M: int, d_short: int, cand: int, k: int, d_keys: int,
+                     stream: int = 0) -> None:
+        check(lib().fi8_bin_rerank_async(self._h, C.c_void_p(d_q), M, C.c_void_p(d_short), cand, k,
+                                         C.c_void_p(d_keys), C.c_void_p(stream or None)))
+
+    def sync(self) -> None:
+        check(lib().fi8_index_sync(self._ih))
+
+    def last_launch_count(self) -> int:
+        v = C.c_int32(0)
+        check(lib().fi8_index_last_launch_count(self._ih, C.byref(v)))
+        return v.value
+
+    def set_kernel_timing(self, on: bool) -> None:
+        from ._ffi import FI8_OPT_KERNEL_TIMING
+        check(lib().fi8_index_set_option(self._ih, FI8_OPT_KERNEL_TIMING, 1 if on else 0))
+
+    def kernel_times(self, reset: bool = True) -> dict:
+        from ._ffi import KERNEL_KINDS
+        nk = len(KERNEL_KINDS)
+        launches = (C.c_int64 * nk)()
+        ms = (C.c_double * nk)()
+        nbytes = (C.c_double * nk)()
+        check(lib().fi8_index_kernel_times(self._ih, launches, ms, nbytes, 1 if reset else 0))
+        return {name: {"launches": int(launches[i]), "ms": float(ms[i]), "bytes": float(nbytes[i])}
+                for i, name in enumerate(KERNEL_KINDS) if launches[i]}
+
+    def Close(self) -> None:
+        if self._h:
+            check(lib().fi8_bin_index_destroy(self._h))
+            self._h = None
+            self._ih = None
 
     def __del__(self):
         try:

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "../../include/fi8.h"
+#include "fi8_binary.cuh"
 #include "fi8_device.cuh"
 #include "fi8_gemm.cuh"
 #include "fi8_scan.cuh"
@@ -603,22 +604,15 @@ int fi8_score_batch(fi8_index* idx, const float* q, int32_t M, float* dst) {
 
 int fi8_score(fi8_index* idx, const float* q, float* dst) { return fi8_score_batch(idx, q, 1, dst); }
 
-int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score) {
-  if (!idx) return fail(FI8_ERR_ARG, "fi8_topk_batch: null index");
-  if (M == 0) return FI8_OK;
-  if (M < 0 || !q || !out_idx || !out_score) return fail(FI8_ERR_ARG, "fi8_topk_batch: bad arguments");
-  if (k <= 0 || (int64_t)k >= idx->n)  // gpu/anncuda/backend.go:577-579
-    return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d n=%lld batch=%d)", k, (long long)idx->n, M);
-  std::lock_guard<std::mutex> lk(idx->mu);
-  DeviceGuard g(idx->device);
-  fi8_index* x = idx;
-  int rc;
+}  // extern "C"
+
+// Top-k of the M queries staged in x->d_q into x->h_keys (M*k keys), with the
+// batched path's overflow fallback. Caller holds x->mu and the device.
+static int topk_staged(fi8_index* x, int32_t M, int32_t k) {
   const size_t nk = (size_t)M * k;
-  if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
+  int rc;
   if ((rc = ensure_device(&x->d_keys, &x->d_keys_cap, nk, "staging keys")) != FI8_OK) return rc;
   if ((rc = ensure_host(&x->h_keys, &x->h_keys_cap, nk, "pinned keys")) != FI8_OK) return rc;
-  FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
-           "H2D queries");
   if ((rc = launch_topk(x, x->d_q, M, k, x->d_keys, x->stream)) != FI8_OK) return rc;
   FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
            "D2H keys");
@@ -639,8 +633,26 @@ int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t
              "D2H err");
     FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
   }
-  if ((rc = check_device_error(x)) != FI8_OK) return rc;
-  return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
+  return check_device_error(x);
+}
+
+extern "C" {
+
+int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_topk_batch: null index");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || !q || !out_idx || !out_score) return fail(FI8_ERR_ARG, "fi8_topk_batch: bad arguments");
+  if (k <= 0 || (int64_t)k >= idx->n)  // gpu/anncuda/backend.go:577-579
+    return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d n=%lld batch=%d)", k, (long long)idx->n, M);
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  fi8_index* x = idx;
+  int rc;
+  if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
+  FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
+           "H2D queries");
+  if ((rc = topk_staged(x, M, k)) != FI8_OK) return rc;
+  return fi8_keys_unpack(x->h_keys, (int64_t)M * k, out_idx, out_score);
 }
 
 int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
@@ -824,3 +836,221 @@ extern "C" int fi8_topk1_noalloc(fi8_index* idx, const float* d_q, int32_t k, ui
   idx->last_launches = 1;
   return FI8_OK;
 }
+
+// ---------------------------------------------------------------------------
+// FlatBinaryI8 (ann/flat_binary_i8.go): a device-resident sign-bit prefilter
+// over an int8 FlatI8 shard. The reference has no device seam for it; this is
+// additive surface for an optional BinaryI8Index-style interface.
+// ---------------------------------------------------------------------------
+struct fi8_bin {
+  fi8_index* ix = nullptr;      // the int8 rows: rerank and the exact fallback
+  int32_t words = 0;            // ceil(dim / 64) (linalg.PackedWords)
+  int32_t wpad = 0;             // row pitch in words (words rounded up to even)
+  int32_t over = 1;             // overquery (max(overquery, 1), prefilter.go:58)
+  uint64_t* d_bits = nullptr;   // [n_alloc][wpad] packed sign bits, zero padded
+  float* d_center = nullptr;    // [dim], or null for an uncentred prefilter
+  uint64_t* d_qbits = nullptr;  // [M][wpad] packed query bits
+  size_t qbits_cap = 0;
+  uint64_t* d_short = nullptr;  // [M][cand] shortlist keys (host entry point)
+  size_t short_cap = 0;
+};
+
+namespace {
+// Shortlists the scan's top-K (and the rerank's sort) support.
+constexpr int32_t kBinMaxCand = kMergeMaxK < kRerankMaxCand ? kMergeMaxK : kRerankMaxCand;
+}  // namespace
+
+// Caller holds b->ix->mu and the device.
+static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
+                                cudaStream_t st) {
+  fi8_index* x = b->ix;
+  const int32_t bpad = b->wpad * 8;
+  ScanGeometry geo;
+  if (cand > kBinMaxCand || !scan_geometry(bpad, cand, true, &geo, true))
+    return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond the device top-K)", cand);
+  int rc;
+  if ((rc = ensure_device(&b->d_qbits, &b->qbits_cap, (size_t)M * b->wpad, "binary query bits")) != FI8_OK)
+    return rc;
+  cudaEvent_t t0 = timer_begin(x, st);
+  cudaError_t e = binary_prep_launch(d_q, M, x->dim, b->d_center, b->wpad, b->d_qbits, st);
+  if (e != cudaSuccess) return cuda_fail(e, "binary_prep_launch");
+  timer_end(x, st, t0, FI8_KERNEL_QUANTIZE, (double)M * x->dim * 4);
+  x->last_launches++;
+  ScanParams p = base_params(x, geo);
+  p.codes = reinterpret_cast<const int8_t*>(b->d_bits);
+  p.scales = nullptr;
+  p.dpad = bpad;
+  const int32_t G = grid_ctas(x, p);
+  const int32_t Mc = std::min(M, kScanMaxM);
+  if ((rc = ensure_topk_scratch(x, Mc, geo.kp, G, st)) != FI8_OK) return rc;
+  p.k = cand;
+  p.kp = geo.kp;
+  p.cap = geo.cap;
+  p.gthr = x->d_gthr;
+  p.counter = x->d_counter;
+  p.counter2 = x->d_counter2;
+  p.lvl1 = x->d_lvl1;
+  p.lvl2 = x->d_lvl2;
+  for (int32_t m0 = 0; m0 < M; m0 += Mc) {
+    const int32_t mm = std::min(Mc, M - m0);
+    p.qbits = b->d_qbits + (size_t)m0 * b->wpad;
+    p.out_keys = d_keys + (size_t)m0 * cand;
+    t0 = timer_begin(x, st);
+    e = scan_launch(p, true, mm, G, st, true);
+    if (e != cudaSuccess) return cuda_fail(e, "scan_launch(binary)");
+    timer_end(x, st, t0, FI8_KERNEL_SCAN, (double)mm * ((double)x->n * bpad + (double)b->wpad * 8));
+    x->last_launches++;
+  }
+  return FI8_OK;
+}
+
+static int launch_bin_rerank(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand,
+                             int32_t k, uint64_t* d_keys, cudaStream_t st) {
+  fi8_index* x = b->ix;
+  if (cand > kRerankMaxCand || k > cand)
+    return fail(FI8_ERR_DECLINED, "gpu: rerank declined (cand=%d k=%d)", cand, k);
+  cudaEvent_t t0 = timer_begin(x, st);
+  cudaError_t e = rerank_launch(d_q, M, x->dim, x->dpad, x->d_codes, x->d_scales, x->n, x->id_base, d_short, cand,
+                                k, d_keys, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rerank_launch");
+  timer_end(x, st, t0, FI8_KERNEL_RERANK, (double)M * cand * (x->dpad + 4 + 8));
+  x->last_launches++;
+  return FI8_OK;
+}
+
+extern "C" {
+
+int fi8_bin_index_create(fi8_ctx* ctx, const uint64_t* codes, int32_t words, const float* center,
+                         const int8_t* i8, const float* scales, int64_t n, int32_t dim, int32_t overquery,
+                         int64_t id_base, fi8_bin** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_bin_index_create: null out");
+  *out = nullptr;
+  if (!ctx || !codes) return fail(FI8_ERR_ARG, "fi8_bin_index_create: null argument");
+  if (dim <= 0 || words != (dim + 63) / 64)  // linalg.PackedWords
+    return fail(FI8_ERR_ARG, "fi8_bin_index_create: words=%d does not match dim %d", words, dim);
+  const int32_t wpad = (words + 1) / 2 * 2;
+  if (wpad * 8 > kScanMaxDpad)
+    return fail(FI8_ERR_DECLINED, "fi8_bin_index_create: dim %d exceeds the supported packed width", dim);
+  fi8_index* ix = nullptr;
+  int rc = fi8_index_create(ctx, i8, scales, n, dim, id_base, &ix);
+  if (rc != FI8_OK) return rc;
+  fi8_bin* b = new (std::nothrow) fi8_bin;
+  if (!b) {
+    fi8_index_destroy(ix);
+    return fail(FI8_ERR_OOM, "fi8_bin_index_create: host allocation");
+  }
+  b->ix = ix;
+  b->words = words;
+  b->wpad = wpad;
+  b->over = overquery < 1 ? 1 : overquery;
+  DeviceGuard g(ix->device);
+  const size_t pitch = (size_t)wpad * 8;
+  cudaError_t e = cudaMalloc(&b->d_bits, (size_t)ix->n_alloc * pitch);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_bits, 0, (size_t)ix->n_alloc * pitch, ix->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(b->d_bits, pitch, codes, (size_t)words * 8, (size_t)words * 8, (size_t)n,
+                          cudaMemcpyHostToDevice, ix->stream);
+  if (e == cudaSuccess && center) {
+    e = cudaMalloc(&b->d_center, (size_t)dim * sizeof(float));
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(b->d_center, center, (size_t)dim * sizeof(float), cudaMemcpyHostToDevice, ix->stream);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
+  if (e != cudaSuccess) {
+    rc = cuda_fail(e, "gpu: binary index upload failed");
+    fi8_bin_index_destroy(b);
+    return rc;
+  }
+  *out = b;
+  return FI8_OK;
+}
+
+int fi8_bin_index_destroy(fi8_bin* b) {
+  if (!b) return FI8_OK;
+  if (b->ix) {
+    {
+      std::lock_guard<std::mutex> lk(b->ix->mu);
+    }
+    DeviceGuard g(b->ix->device);
+    cudaStreamSynchronize(b->ix->stream);
+    cudaFree(b->d_bits);
+    cudaFree(b->d_center);
+    cudaFree(b->d_qbits);
+    cudaFree(b->d_short);
+    fi8_index_destroy(b->ix);
+  }
+  delete b;
+  return FI8_OK;
+}
+
+int fi8_bin_index_handle(fi8_bin* b, fi8_index** out) {
+  if (!b || !out) return fail(FI8_ERR_ARG, "fi8_bin_index_handle: null argument");
+  *out = b->ix;
+  return FI8_OK;
+}
+
+int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score) {
+  if (!b) return fail(FI8_ERR_ARG, "fi8_bin_query_topk: null index");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || !q || !out_idx || !out_score) return fail(FI8_ERR_ARG, "fi8_bin_query_topk: bad arguments");
+  fi8_index* x = b->ix;
+  // k <= 0 and k >= n return the whole corpus in the reference
+  // (flat_binary_i8.go:95-97 -> FlatI8.query); the device declines them.
+  if (k <= 0 || (int64_t)k >= x->n)
+    return fail(FI8_ERR_DECLINED, "gpu: binary TopK declined (k=%d n=%lld)", k, (long long)x->n);
+  const int64_t cand = (int64_t)k * b->over;
+  std::lock_guard<std::mutex> lk(x->mu);
+  DeviceGuard g(x->device);
+  int rc;
+  if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
+  FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
+           "H2D queries");
+  if (cand >= x->n) {
+    // the candidate set is the whole corpus: FlatI8's exact scan
+    // (flat_binary_i8.go:95-97)
+    if ((rc = topk_staged(x, M, k)) != FI8_OK) return rc;
+    return fi8_keys_unpack(x->h_keys, (int64_t)M * k, out_idx, out_score);
+  }
+  const size_t nk = (size_t)M * k;
+  x->last_launches = 0;
+  if ((rc = ensure_device(&b->d_short, &b->short_cap, (size_t)M * cand, "shortlist")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&x->d_keys, &x->d_keys_cap, nk, "staging keys")) != FI8_OK) return rc;
+  if ((rc = ensure_host(&x->h_keys, &x->h_keys_cap, nk, "pinned keys")) != FI8_OK) return rc;
+  if ((rc = launch_bin_prefilter(b, x->d_q, M, (int32_t)cand, b->d_short, x->stream)) != FI8_OK) return rc;
+  if ((rc = launch_bin_rerank(b, x->d_q, M, b->d_short, (int32_t)cand, k, x->d_keys, x->stream)) != FI8_OK)
+    return rc;
+  FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
+           "D2H keys");
+  FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
+           "D2H err");
+  FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+  if ((rc = check_device_error(x)) != FI8_OK) return rc;
+  return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
+}
+
+int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
+                            void* stream) {
+  if (!b) return fail(FI8_ERR_ARG, "fi8_bin_prefilter_async: null index");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || !d_q || !d_keys) return fail(FI8_ERR_ARG, "fi8_bin_prefilter_async: bad arguments");
+  if (cand <= 0) return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d)", cand);
+  std::lock_guard<std::mutex> lk(b->ix->mu);
+  DeviceGuard g(b->ix->device);
+  b->ix->last_launches = 0;
+  return launch_bin_prefilter(b, d_q, M, cand, d_keys, static_cast<cudaStream_t>(stream));
+}
+
+int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,
+                         uint64_t* d_keys, void* stream) {
+  if (!b) return fail(FI8_ERR_ARG, "fi8_bin_rerank_async: null index");
+  if (M == 0) return FI8_OK;
+  if (M < 0 || !d_q || !d_short || !d_keys || cand <= 0)
+    return fail(FI8_ERR_ARG, "fi8_bin_rerank_async: bad arguments");
+  if (k <= 0) return fail(FI8_ERR_DECLINED, "gpu: rerank declined (k=%d)", k);
+  std::lock_guard<std::mutex> lk(b->ix->mu);
+  DeviceGuard g(b->ix->device);
+  b->ix->last_launches = 0;
+  return launch_bin_rerank(b, d_q, M, d_short, cand, k, d_keys, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

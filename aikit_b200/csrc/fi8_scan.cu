@@ -46,9 +46,24 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One 16-byte chunk of a row against the same chunk of the query: four dp4a
+// (int8 W8A8 rows) or four popcounts of the XOR (packed sign bits: the
+// Hamming distance of linalg/hamming.go:54-73).
+template <bool BIN>
+__device__ __forceinline__ int chunk_op(const int4 a, const int4 b, int acc) {
+  if (BIN) return acc + __popc(a.x ^ b.x) + __popc(a.y ^ b.y) + __popc(a.z ^ b.z) + __popc(a.w ^ b.w);
+  acc = __dp4a(a.x, b.x, acc);
+  acc = __dp4a(a.y, b.y, acc);
+  acc = __dp4a(a.z, b.z, acc);
+  return __dp4a(a.w, b.w, acc);
+}
+
 // CPL: 16-byte chunks per lane per row (dpad = 128*CPL), 0 = generic pitch.
 // RPG: rows per 8-lane quarter-warp per pass; a tile is R = 32*RPG*passes rows.
-template <bool TOPK, int CPL, int RPG>
+// BIN: rows are packed sign bits and the score of a row is minus its Hamming
+// distance to the query's bits (no scales), so the top-K keys are the rows
+// nearest in (distance asc, index asc) -- the prefilter's candidate order.
+template <bool TOPK, int CPL, int RPG, bool BIN>
 __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t s_full[kMaxStages];
@@ -73,7 +88,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
   const int dpad = p.dpad;
   const int S = p.stages;
   const uint32_t code_bytes = (uint32_t)R * (uint32_t)dpad;
-  const uint32_t stage_bytes = code_bytes + (uint32_t)R * 4u;
+  const uint32_t stage_bytes = code_bytes + (BIN ? 0u : (uint32_t)R * 4u);
 
   unsigned char* stages = smem;
   int8_t* q_s = reinterpret_cast<int8_t*>(smem + (size_t)S * stage_bytes);
@@ -111,7 +126,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
         unsigned char* st = stages + (size_t)s * stage_bytes;
         mbar_arrive_expect_tx(&s_full[s], stage_bytes);
         bulk_g2s(st, p.codes + (size_t)tile * code_bytes, code_bytes, &s_full[s]);
-        bulk_g2s(st + code_bytes, p.scales + (size_t)tile * R, (uint32_t)R * 4u, &s_full[s]);
+        if (!BIN) bulk_g2s(st + code_bytes, p.scales + (size_t)tile * R, (uint32_t)R * 4u, &s_full[s]);
       }
       if (s_abort) {
         // let the copies already issued land before the CTA can exit (bounded)
@@ -128,6 +143,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
     const int bar = 1 + g;
     uint64_t* buf = bufs + (TOPK ? (size_t)g * p.cap : 0);
 
+    if (BIN) {
+      // the query's packed sign bits, prepared by the caller
+      const int8_t* qb = reinterpret_cast<const int8_t*>(p.qbits) + (size_t)y * dpad;
+      for (int i = tid; i < dpad; i += kConsumerThreads) q_s[i] = qb[i];
+      if (tid == 0) s_qscale = 0.0f;
+    } else {
     // quantize this CTA's query (quant.go:43-71) into shared memory
     const float* q = p.q + (size_t)y * p.d;
     float m = 0.0f;
@@ -151,6 +172,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
       const float inv = __fdiv_rn(1.0f, sc);
       for (int i = tid; i < dpad; i += kConsumerThreads) q_s[i] = i < p.d ? quant_code(q[i], inv) : (int8_t)0;
       if (tid == 0) s_qscale = sc;
+    }
     }
     named_sync(kBarConsumers, kConsumerThreads);
     const float qscale = s_qscale;
@@ -190,12 +212,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
 #pragma unroll
             for (int i = 0; i < RPG; i++) {
               const int4 a = reinterpret_cast<const int4*>(st + (size_t)(base + i) * dpad)[lane8 + 8 * j];
-              int t = acc[i][j & 1];
-              t = __dp4a(a.x, qreg[j].x, t);
-              t = __dp4a(a.y, qreg[j].y, t);
-              t = __dp4a(a.z, qreg[j].z, t);
-              t = __dp4a(a.w, qreg[j].w, t);
-              acc[i][j & 1] = t;
+              acc[i][j & 1] = chunk_op<BIN>(a, qreg[j], acc[i][j & 1]);
             }
           }
 #pragma unroll
@@ -209,21 +226,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
           for (; c + 8 < chunks; c += 16) {
             const int4 a = rowp[c], b = qp[c];
             const int4 a2 = rowp[c + 8], b2 = qp[c + 8];
-            a0 = __dp4a(a.x, b.x, a0);
-            a0 = __dp4a(a.y, b.y, a0);
-            a0 = __dp4a(a.z, b.z, a0);
-            a0 = __dp4a(a.w, b.w, a0);
-            a1 = __dp4a(a2.x, b2.x, a1);
-            a1 = __dp4a(a2.y, b2.y, a1);
-            a1 = __dp4a(a2.z, b2.z, a1);
-            a1 = __dp4a(a2.w, b2.w, a1);
+            a0 = chunk_op<BIN>(a, b, a0);
+            a1 = chunk_op<BIN>(a2, b2, a1);
           }
           if (c < chunks) {
             const int4 a = rowp[c], b = qp[c];
-            a0 = __dp4a(a.x, b.x, a0);
-            a0 = __dp4a(a.y, b.y, a0);
-            a0 = __dp4a(a.z, b.z, a0);
-            a0 = __dp4a(a.w, b.w, a0);
+            a0 = chunk_op<BIN>(a, b, a0);
           }
           vals[0] = a0 + a1;
         }
@@ -247,7 +255,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
         const int64_t gr = row0 + r;
         const bool mine = owner && (gr < p.n);
         float score = 0.0f;
-        if (mine) score = w8a8_score(vals[0], qscale, sc_s[r]);
+        if (mine) score = BIN ? (float)(-vals[0]) : w8a8_score(vals[0], qscale, sc_s[r]);
         if (TOPK) {
           uint64_t key = kEmptyKey;
           bool take = false;
@@ -369,23 +377,33 @@ constexpr Shape kShapes[] = {{1, 8}, {2, 4}, {3, 2}, {4, 2}, {6, 1}, {8, 1}, {12
 template <bool TOPK>
 ScanFn pick_kernel(int cpl) {
   switch (cpl) {
-    case 1: return scan_kernel<TOPK, 1, 8>;
-    case 2: return scan_kernel<TOPK, 2, 4>;
-    case 3: return scan_kernel<TOPK, 3, 2>;
-    case 4: return scan_kernel<TOPK, 4, 2>;
-    case 6: return scan_kernel<TOPK, 6, 1>;
-    case 8: return scan_kernel<TOPK, 8, 1>;
-    case 12: return scan_kernel<TOPK, 12, 1>;
-    case 16: return scan_kernel<TOPK, 16, 1>;
-    default: return scan_kernel<TOPK, 0, 1>;
+    case 1: return scan_kernel<TOPK, 1, 8, false>;
+    case 2: return scan_kernel<TOPK, 2, 4, false>;
+    case 3: return scan_kernel<TOPK, 3, 2, false>;
+    case 4: return scan_kernel<TOPK, 4, 2, false>;
+    case 6: return scan_kernel<TOPK, 6, 1, false>;
+    case 8: return scan_kernel<TOPK, 8, 1, false>;
+    case 12: return scan_kernel<TOPK, 12, 1, false>;
+    case 16: return scan_kernel<TOPK, 16, 1, false>;
+    default: return scan_kernel<TOPK, 0, 1, false>;
   }
 }
 
-int rows_per_group(int dpad, int* cpl_out) {
+// Packed sign bits: 128-byte rows (d in (960, 1024]) and 256-byte rows get
+// specialised kernels, every other pitch the generic one.
+ScanFn pick_binary_kernel(int cpl) {
+  switch (cpl) {
+    case 1: return scan_kernel<true, 1, 8, true>;
+    case 2: return scan_kernel<true, 2, 4, true>;
+    default: return scan_kernel<true, 0, 1, true>;
+  }
+}
+
+int rows_per_group(int dpad, bool binary, int* cpl_out) {
   *cpl_out = 0;
   if (dpad % 128 == 0)
     for (const Shape& s : kShapes)
-      if (s.cpl * 128 == dpad) {
+      if (s.cpl * 128 == dpad && (!binary || s.cpl <= 2)) {
         *cpl_out = s.cpl;
         return s.rpg;
       }
@@ -394,15 +412,16 @@ int rows_per_group(int dpad, int* cpl_out) {
 
 }  // namespace
 
-bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g) {
+bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g, bool binary) {
   if (dpad <= 0 || dpad % 16 != 0 || dpad > kScanMaxDpad) return false;
+  if (binary && !topk) return false;
   int cpl = 0;
-  const int rpg = rows_per_group(dpad, &cpl);
+  const int rpg = rows_per_group(dpad, binary, &cpl);
   // Tile: one pass of 32*RPG rows, doubled (more passes) while it stays at or
   // under 32 KB; at most 256 rows so it divides the allocation padding.
   int R = 32 * rpg;
   while (R < 256 && (size_t)(2 * R) * dpad <= 32 * 1024) R *= 2;
-  const size_t stage = (size_t)R * (dpad + 4);
+  const size_t stage = (size_t)R * (dpad + (binary ? 0 : 4));
   int cap = 0, kp = 0;
   if (topk) {
     if (k <= 0) return false;
@@ -433,12 +452,13 @@ bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g) {
   return true;
 }
 
-cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cudaStream_t stream) {
+cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cudaStream_t stream, bool binary) {
   if (p.stages > kMaxStages || p.stages % kGroups != 0 || p.stages < 2) return cudaErrorInvalidValue;
+  if (binary && (!topk || !p.qbits)) return cudaErrorInvalidValue;
   int cpl = 0;
-  const int rpg = rows_per_group(p.dpad, &cpl);
+  const int rpg = rows_per_group(p.dpad, binary, &cpl);
   if (p.rows_per_tile % (32 * rpg) != 0) return cudaErrorInvalidValue;
-  ScanFn fn = topk ? pick_kernel<true>(cpl) : pick_kernel<false>(cpl);
+  ScanFn fn = binary ? pick_binary_kernel(cpl) : topk ? pick_kernel<true>(cpl) : pick_kernel<false>(cpl);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)G, (unsigned)M);

@@ -31,6 +31,9 @@ struct ScanParams {
   uint64_t* lvl1;            // [M][G][kp] per-CTA top-kp lists
   uint64_t* lvl2;            // [M][NB][kp] per-block top-kp lists
   uint64_t* out_keys;        // [M][k] final keys, 0 = empty
+  // binary (packed sign bit) mode: codes are [n_alloc][dpad] bytes of packed
+  // bits, scales unused, and qbits holds each query's packed bits
+  const uint64_t* qbits;     // [M][dpad / 8]
   // score mode
   float* out_scores;         // [M][n]
   unsigned int* err;         // device error flags (bit 0: wait timeout)
@@ -50,8 +53,9 @@ constexpr int32_t kScanMaxCap = 4096;
 // CTAs whose lists one first-level merge combines.
 constexpr int32_t kMergeBlock = 8;
 
-bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g);
-cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cudaStream_t stream);
+bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g, bool binary = false);
+cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cudaStream_t stream,
+                        bool binary = false);
 
 inline int32_t scan_blocks(int32_t G) { return (G + kMergeBlock - 1) / kMergeBlock; }
 

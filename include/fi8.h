@@ -110,8 +110,9 @@ int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
 #define FI8_KERNEL_SCAN 0     /* fused W8A8 scan + top-K (or scores) */
 #define FI8_KERNEL_GEMM 1     /* tcgen05 GEMM with threshold-filter epilogue */
 #define FI8_KERNEL_SELECT 2   /* per-query exact select of the candidates */
-#define FI8_KERNEL_QUANTIZE 3 /* batch query quantization */
-#define FI8_KERNEL_KINDS 4
+#define FI8_KERNEL_QUANTIZE 3 /* query quantization / sign-bit packing */
+#define FI8_KERNEL_RERANK 4   /* FlatBinaryI8 shortlist rerank */
+#define FI8_KERNEL_KINDS 5
 
 /* Totals over the launches timed since the last reset, per kernel class:
  * launches[i], ms[i] (sum of per-launch device durations) and bytes[i]
@@ -150,6 +151,52 @@ int fi8_merge_keys_async(fi8_ctx* ctx, const uint64_t* d_in, int32_t nsrc, int32
  * share the array, so two calls that overlap on the GPU race: serialize them.
  * Does not synchronize; device errors surface at fi8_index_sync. */
 int fi8_topk1_noalloc(fi8_index* idx, const float* d_q, int32_t k, uint64_t* d_keys, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * FlatBinaryI8 (ann/flat_binary_i8.go): the sign-bit Hamming prefilter over a
+ * FlatI8 shard, then an int8 W8A8 rerank of the shortlist. The reference has
+ * no device seam for this type (it always runs on the CPU); these entry points
+ * are additive surface for an optional BinaryI8Index interface, detected by
+ * type assertion the way I8TopKIndex is (ann/backend.go:50-55).
+ * ------------------------------------------------------------------------- */
+
+/* Build from the prefilter's packed codes [n*words] (binaryPrefilter.codes,
+ * ann/flat_binary_prefilter.go:87-95; words = ceil(dim/64)), its center [dim]
+ * (NULL for an uncentred prefilter, prefilter.go:79-84) and the FlatI8 rows
+ * i8 [n*dim] / scales [n] (ann/flat_i8.go:31-66). overquery below 1 is taken
+ * as 1 (prefilter.go:58). id_base as for fi8_index_create. All host arrays are
+ * copied. */
+int fi8_bin_index_create(fi8_ctx* ctx, const uint64_t* codes, int32_t words, const float* center,
+                         const int8_t* i8, const float* scales, int64_t n, int32_t dim, int32_t overquery,
+                         int64_t id_base, fi8_bin** out);
+int fi8_bin_index_destroy(fi8_bin* b);
+
+/* The FlatI8 index inside b (owned by b): for fi8_index_* options, timing and
+ * launch counts. */
+int fi8_bin_index_handle(fi8_bin* b, fi8_index** out);
+
+/* FlatBinaryI8.Query for M queries (ann/flat_binary_i8.go:86-109): q [M*dim]
+ * host f32; out_idx/out_score [M*k], as fi8_topk_batch. With cand = k *
+ * overquery: when cand >= n this is FlatI8's exact top-k (:95-97); otherwise
+ * the cand rows nearest the centred query's sign bits in Hamming distance,
+ * ties by ascending id (prefilterHist, prefilter.go:145-216), reranked by
+ * W8A8 score (rerank, :122-153). Declines k <= 0 and k >= n (the reference
+ * returns the whole corpus there), and cand above the device limit (2048). */
+int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score);
+
+/* Device-resident halves, for sharded use: every rank prefilters its shard,
+ * the M x cand keys are all-gathered and merged (fi8_merge_keys_async) into the
+ * global shortlist -- the global cand nearest by (distance, id), as the
+ * reference computes it over the whole corpus -- then every rank reranks the
+ * shortlist rows it holds and the M x k results are merged again.
+ * fi8_bin_prefilter_async: d_q [M*dim] f32 -> d_keys [M*cand] packed keys of
+ * (-distance, global id), sorted, 0-padded. fi8_bin_rerank_async: d_short
+ * [M*cand] keys (rows of other shards are skipped) -> d_keys [M*k] W8A8 keys,
+ * sorted, 0-padded. Stream semantics as fi8_topk_batch_async. */
+int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
+                            void* stream);
+int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,
+                         uint64_t* d_keys, void* stream);
 
 #ifdef __cplusplus
 }
