@@ -849,57 +849,77 @@ struct fi8_bin {
   int32_t over = 1;             // overquery (max(overquery, 1), prefilter.go:58)
   uint64_t* d_bits = nullptr;   // [n_alloc][wpad] packed sign bits, zero padded
   float* d_center = nullptr;    // [dim], or null for an uncentred prefilter
+  // per-call scratch, grown on demand
   uint64_t* d_qbits = nullptr;  // [M][wpad] packed query bits
   size_t qbits_cap = 0;
+  uint16_t* d_dist = nullptr;   // [M][n_alloc] Hamming distances
+  size_t dist_cap = 0;
+  unsigned int* d_hist = nullptr;    // [M][nbins]
+  size_t hist_cap = 0;
+  unsigned int* d_counts = nullptr;  // [M][P][2]
+  size_t counts_cap = 0;
+  uint64_t* d_parts = nullptr;  // [parts][M][k] rerank slices
+  size_t parts_cap = 0;
   uint64_t* d_short = nullptr;  // [M][cand] shortlist keys (host entry point)
   size_t short_cap = 0;
 };
 
 namespace {
-// Shortlists the scan's top-K (and the rerank's sort) support.
+// Shortlists the key merge (cross-shard), the shortlist sort and the rerank
+// support.
 constexpr int32_t kBinMaxCand = kMergeMaxK < kRerankMaxCand ? kMergeMaxK : kRerankMaxCand;
+// Queries per distance pass: bounds the distance scratch (M x n u16).
+constexpr int32_t kBinMaxM = 16;
 }  // namespace
 
-// Caller holds b->ix->mu and the device.
+// The prefilter (packing, the distance pass with its histogram, the cut and
+// the shortlist) for M queries. sorted: each query's keys sorted descending,
+// as a cross-shard key merge needs. Caller holds b->ix->mu and the device.
 static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
-                                cudaStream_t st) {
+                                bool sorted, cudaStream_t st) {
   fi8_index* x = b->ix;
   const int32_t bpad = b->wpad * 8;
+  const int32_t nbins = bpad * 8 + 1;
   ScanGeometry geo;
-  if (cand > kBinMaxCand || !scan_geometry(bpad, cand, true, &geo, true))
-    return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond the device top-K)", cand);
+  if (cand > kBinMaxCand || !scan_geometry(bpad, 0, false, &geo, true))
+    return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond %d)", cand, kBinMaxCand);
+  const int32_t Mc = std::min(M, kBinMaxM);
+  const int32_t P = shortlist_segments(x->sm_count);
   int rc;
-  if ((rc = ensure_device(&b->d_qbits, &b->qbits_cap, (size_t)M * b->wpad, "binary query bits")) != FI8_OK)
+  if ((rc = ensure_device(&b->d_qbits, &b->qbits_cap, (size_t)Mc * b->wpad, "binary query bits")) != FI8_OK)
     return rc;
-  cudaEvent_t t0 = timer_begin(x, st);
-  cudaError_t e = binary_prep_launch(d_q, M, x->dim, b->d_center, b->wpad, b->d_qbits, st);
-  if (e != cudaSuccess) return cuda_fail(e, "binary_prep_launch");
-  timer_end(x, st, t0, FI8_KERNEL_QUANTIZE, (double)M * x->dim * 4);
-  x->last_launches++;
+  if ((rc = ensure_device(&b->d_dist, &b->dist_cap, (size_t)Mc * x->n_alloc, "binary distances")) != FI8_OK)
+    return rc;
+  if ((rc = ensure_device(&b->d_hist, &b->hist_cap, (size_t)Mc * nbins, "binary histogram")) != FI8_OK) return rc;
+  if ((rc = ensure_device(&b->d_counts, &b->counts_cap, (size_t)Mc * P * 2, "binary counts")) != FI8_OK) return rc;
   ScanParams p = base_params(x, geo);
   p.codes = reinterpret_cast<const int8_t*>(b->d_bits);
   p.scales = nullptr;
   p.dpad = bpad;
+  p.out_dist = b->d_dist;
+  p.dist_stride = x->n_alloc;
+  p.hist = b->d_hist;
+  p.nbins = nbins;
+  p.qbits = b->d_qbits;
   const int32_t G = grid_ctas(x, p);
-  const int32_t Mc = std::min(M, kScanMaxM);
-  if ((rc = ensure_topk_scratch(x, Mc, geo.kp, G, st)) != FI8_OK) return rc;
-  p.k = cand;
-  p.kp = geo.kp;
-  p.cap = geo.cap;
-  p.gthr = x->d_gthr;
-  p.counter = x->d_counter;
-  p.counter2 = x->d_counter2;
-  p.lvl1 = x->d_lvl1;
-  p.lvl2 = x->d_lvl2;
   for (int32_t m0 = 0; m0 < M; m0 += Mc) {
     const int32_t mm = std::min(Mc, M - m0);
-    p.qbits = b->d_qbits + (size_t)m0 * b->wpad;
-    p.out_keys = d_keys + (size_t)m0 * cand;
+    const float* q = d_q + (size_t)m0 * x->dim;
+    cudaEvent_t t0 = timer_begin(x, st);
+    cudaError_t e = binary_prep_launch(q, mm, x->dim, b->d_center, b->wpad, b->d_qbits, b->d_hist, nbins, st);
+    if (e != cudaSuccess) return cuda_fail(e, "binary_prep_launch");
+    timer_end(x, st, t0, FI8_KERNEL_QUANTIZE, (double)mm * x->dim * 4);
     t0 = timer_begin(x, st);
-    e = scan_launch(p, true, mm, G, st, true);
+    e = scan_launch(p, false, mm, G, st, true);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(binary)");
-    timer_end(x, st, t0, FI8_KERNEL_SCAN, (double)mm * ((double)x->n * bpad + (double)b->wpad * 8));
-    x->last_launches++;
+    // the packed codes once per query, plus the u16 distance written per row
+    timer_end(x, st, t0, FI8_KERNEL_SCAN, (double)mm * ((double)x->n * bpad + (double)bpad + 2.0 * x->n));
+    t0 = timer_begin(x, st);
+    e = shortlist_launch(b->d_dist, x->n, x->n_alloc, mm, b->d_hist, nbins, cand, P, b->d_counts, x->id_base,
+                         d_keys + (size_t)m0 * cand, sorted, st);
+    if (e != cudaSuccess) return cuda_fail(e, "shortlist_launch");
+    timer_end(x, st, t0, FI8_KERNEL_SELECT, (double)mm * 2.0 * 2.0 * x->n);
+    x->last_launches += sorted ? 5 : 4;
   }
   return FI8_OK;
 }
@@ -907,14 +927,18 @@ static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t
 static int launch_bin_rerank(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand,
                              int32_t k, uint64_t* d_keys, cudaStream_t st) {
   fi8_index* x = b->ix;
-  if (cand > kRerankMaxCand || k > cand)
+  if (cand > kRerankMaxCand || k > cand || k > kMergeMaxK)
     return fail(FI8_ERR_DECLINED, "gpu: rerank declined (cand=%d k=%d)", cand, k);
+  int rc;
+  if ((rc = ensure_device(&b->d_parts, &b->parts_cap, (size_t)rerank_parts(cand) * M * k, "rerank parts")) !=
+      FI8_OK)
+    return rc;
   cudaEvent_t t0 = timer_begin(x, st);
   cudaError_t e = rerank_launch(d_q, M, x->dim, x->dpad, x->d_codes, x->d_scales, x->n, x->id_base, d_short, cand,
-                                k, d_keys, st);
+                                k, b->d_parts, d_keys, st);
   if (e != cudaSuccess) return cuda_fail(e, "rerank_launch");
   timer_end(x, st, t0, FI8_KERNEL_RERANK, (double)M * cand * (x->dpad + 4 + 8));
-  x->last_launches++;
+  x->last_launches += 2;
   return FI8_OK;
 }
 
@@ -976,6 +1000,10 @@ int fi8_bin_index_destroy(fi8_bin* b) {
     cudaFree(b->d_bits);
     cudaFree(b->d_center);
     cudaFree(b->d_qbits);
+    cudaFree(b->d_dist);
+    cudaFree(b->d_hist);
+    cudaFree(b->d_counts);
+    cudaFree(b->d_parts);
     cudaFree(b->d_short);
     fi8_index_destroy(b->ix);
   }
@@ -1016,7 +1044,9 @@ int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t
   if ((rc = ensure_device(&b->d_short, &b->short_cap, (size_t)M * cand, "shortlist")) != FI8_OK) return rc;
   if ((rc = ensure_device(&x->d_keys, &x->d_keys_cap, nk, "staging keys")) != FI8_OK) return rc;
   if ((rc = ensure_host(&x->h_keys, &x->h_keys_cap, nk, "pinned keys")) != FI8_OK) return rc;
-  if ((rc = launch_bin_prefilter(b, x->d_q, M, (int32_t)cand, b->d_short, x->stream)) != FI8_OK) return rc;
+  if (cand > kBinMaxCand)
+    return fail(FI8_ERR_DECLINED, "gpu: binary TopK declined (cand=%lld beyond %d)", (long long)cand, kBinMaxCand);
+  if ((rc = launch_bin_prefilter(b, x->d_q, M, (int32_t)cand, b->d_short, false, x->stream)) != FI8_OK) return rc;
   if ((rc = launch_bin_rerank(b, x->d_q, M, b->d_short, (int32_t)cand, k, x->d_keys, x->stream)) != FI8_OK)
     return rc;
   FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
@@ -1037,7 +1067,7 @@ int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t can
   std::lock_guard<std::mutex> lk(b->ix->mu);
   DeviceGuard g(b->ix->device);
   b->ix->last_launches = 0;
-  return launch_bin_prefilter(b, d_q, M, cand, d_keys, static_cast<cudaStream_t>(stream));
+  return launch_bin_prefilter(b, d_q, M, cand, d_keys, true, static_cast<cudaStream_t>(stream));
 }
 
 int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,

@@ -1,6 +1,7 @@
 // fi8_binary.cuh -- host-visible declarations for the FlatBinaryI8 device path:
-// query sign-bit packing and the int8 rerank of a Hamming shortlist. The
-// Hamming scan itself is the scan kernel's binary mode (fi8_scan.cuh).
+// query sign-bit packing, the prefilter's shortlist from the distance
+// histogram, and the int8 rerank of the shortlist. The distance pass itself is
+// the scan kernel's binary histogram mode (fi8_scan.cuh).
 #pragma once
 
 #include <cstdint>
@@ -10,9 +11,26 @@ namespace fi8 {
 
 // qbits[y][w] = the packed sign bits of (q[y] - center) (center may be null):
 // bit i%64 of word i/64 is set iff q[y][i] - center[i] >= 0 in float32, bits
-// past d and words past ceil(d/64) are zero. wpad = row pitch in words.
+// past d are zero; wpad = row pitch in words. Also zeroes hist[y][0..nbins).
 cudaError_t binary_prep_launch(const float* q, int32_t M, int32_t d, const float* center, int32_t wpad,
-                               uint64_t* qbits, cudaStream_t stream);
+                               uint64_t* qbits, unsigned int* hist, int32_t nbins, cudaStream_t stream);
+
+// Row segments the shortlist kernels split a corpus into (counts holds
+// [M][P][2] entries).
+int32_t shortlist_segments(int32_t sm_count);
+
+// From each query's distances dist[y][0..n) (row stride dstride, a multiple of
+// 8) and histogram hist[y][0..nbins): out[y][0..cand) = packed keys
+// (-distance, id_base + row) of prefilterHist's cand rows -- every row below
+// the cut t, then the first ties at t in id order -- 0 past the rows there
+// are. sorted: also sort each query's keys descending (for a key merge).
+cudaError_t shortlist_launch(const uint16_t* dist, int64_t n, int64_t dstride, int32_t M, const unsigned int* hist,
+                             int32_t nbins, int32_t cand, int32_t P, unsigned int* counts, uint32_t id_base,
+                             uint64_t* out, bool sorted, cudaStream_t stream);
+
+// CTAs (slices of the shortlist) one query's rerank uses; parts holds
+// [rerank_parts(cand)][M][k] keys.
+int32_t rerank_parts(int32_t cand);
 
 // Exact W8A8 top-k over a shortlist: for each query y, the entries of
 // shortlist[y][0..cand) (packed keys whose index is a global row id; 0 =
@@ -21,9 +39,9 @@ cudaError_t binary_prep_launch(const float* q, int32_t M, int32_t d, const float
 // out[y][0..k) receives the best k keys, sorted, 0-padded.
 cudaError_t rerank_launch(const float* q, int32_t M, int32_t d, int32_t dpad, const int8_t* codes,
                           const float* scales, int64_t n, uint32_t id_base, const uint64_t* shortlist,
-                          int32_t cand, int32_t k, uint64_t* out, cudaStream_t stream);
+                          int32_t cand, int32_t k, uint64_t* parts, uint64_t* out, cudaStream_t stream);
 
-// Largest shortlist (cand) the rerank sorts in shared memory.
+// Largest shortlist (cand) the shortlist sort and the rerank support.
 constexpr int32_t kRerankMaxCand = 4096;
 
 }  // namespace fi8

@@ -60,9 +60,10 @@ __device__ __forceinline__ int chunk_op(const int4 a, const int4 b, int acc) {
 
 // CPL: 16-byte chunks per lane per row (dpad = 128*CPL), 0 = generic pitch.
 // RPG: rows per 8-lane quarter-warp per pass; a tile is R = 32*RPG*passes rows.
-// BIN: rows are packed sign bits and the score of a row is minus its Hamming
-// distance to the query's bits (no scales), so the top-K keys are the rows
-// nearest in (distance asc, index asc) -- the prefilter's candidate order.
+// BIN: rows are packed sign bits and a row's value is its Hamming distance to
+// the query's bits (no scales). Used without TOPK: every row's distance is
+// stored (u16) and counted into a (bits+1)-bin histogram, the first pass of
+// prefilterHist (ann/flat_binary_prefilter.go:145-178).
 template <bool TOPK, int CPL, int RPG, bool BIN>
 __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -148,6 +149,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
       const int8_t* qb = reinterpret_cast<const int8_t*>(p.qbits) + (size_t)y * dpad;
       for (int i = tid; i < dpad; i += kConsumerThreads) q_s[i] = qb[i];
       if (tid == 0) s_qscale = 0.0f;
+      if (!TOPK)
+        for (int i = tid; i < p.nbins; i += kConsumerThreads) reinterpret_cast<unsigned int*>(bufs)[i] = 0u;
     } else {
     // quantize this CTA's query (quant.go:43-71) into shared memory
     const float* q = p.q + (size_t)y * p.d;
@@ -265,7 +268,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
           }
           warp_append(take, key, buf, &s_count[g]);
         } else if (mine) {
-          p.out_scores[(size_t)y * p.n + gr] = score;
+          if (BIN) {
+            p.out_dist[(size_t)y * p.dist_stride + gr] = (uint16_t)vals[0];
+            atomicAdd(reinterpret_cast<unsigned int*>(bufs) + vals[0], 1u);
+          } else {
+            p.out_scores[(size_t)y * p.n + gr] = score;
+          }
         }
       }
       // this warp is done reading the stage
@@ -290,6 +298,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
       group_compact(buf, s_count[g], p.k, &s_count[g], &s_local_thr[g], p.gthr + y, gtid, bar);
       // the group's list: its best keys, sorted, empty-padded to kp
       for (int i = s_count[g] + gtid; i < p.kp; i += kGroupThreads) buf[i] = kEmptyKey;
+    }
+    if (BIN && !TOPK) {
+      // this CTA's histogram into the query's
+      named_sync(kBarConsumers, kConsumerThreads);
+      const unsigned int* hs = reinterpret_cast<const unsigned int*>(bufs);
+      for (int b = tid; b < p.nbins; b += kConsumerThreads)
+        if (hs[b]) atomicAdd(p.hist + (size_t)y * p.nbins + b, hs[b]);
     }
   }
 
@@ -389,13 +404,13 @@ ScanFn pick_kernel(int cpl) {
   }
 }
 
-// Packed sign bits: 128-byte rows (d in (960, 1024]) and 256-byte rows get
-// specialised kernels, every other pitch the generic one.
+// Packed sign bits (histogram mode): 128-byte rows (d in (960, 1024]) and
+// 256-byte rows get specialised kernels, every other pitch the generic one.
 ScanFn pick_binary_kernel(int cpl) {
   switch (cpl) {
-    case 1: return scan_kernel<true, 1, 8, true>;
-    case 2: return scan_kernel<true, 2, 4, true>;
-    default: return scan_kernel<true, 0, 1, true>;
+    case 1: return scan_kernel<false, 1, 8, true>;
+    case 2: return scan_kernel<false, 2, 4, true>;
+    default: return scan_kernel<false, 0, 1, true>;
   }
 }
 
@@ -414,7 +429,7 @@ int rows_per_group(int dpad, bool binary, int* cpl_out) {
 
 bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g, bool binary) {
   if (dpad <= 0 || dpad % 16 != 0 || dpad > kScanMaxDpad) return false;
-  if (binary && !topk) return false;
+  if (binary && topk) return false;
   int cpl = 0;
   const int rpg = rows_per_group(dpad, binary, &cpl);
   // Tile: one pass of 32*RPG rows, doubled (more passes) while it stays at or
@@ -430,7 +445,9 @@ bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g, bool bin
     kp = pow2_at_least(k);
     if (cap > kScanMaxCap) return false;
   }
-  const size_t fixed = (size_t)dpad + (size_t)kGroups * cap * 8;
+  // query row, then the groups' candidate buffers (top-K) or the distance
+  // histogram of dpad*8 + 1 bins (binary)
+  const size_t fixed = (size_t)dpad + (size_t)kGroups * cap * 8 + (binary ? ((size_t)dpad * 8 + 1) * 4 : 0);
   // Ring depth: an even count (stage s always belongs to consumer group s % 2;
   // with an odd count the groups would share stages, and because bulk copies
   // complete out of order a parity wait could then observe the wrong phase),
@@ -454,7 +471,8 @@ bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g, bool bin
 
 cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cudaStream_t stream, bool binary) {
   if (p.stages > kMaxStages || p.stages % kGroups != 0 || p.stages < 2) return cudaErrorInvalidValue;
-  if (binary && (!topk || !p.qbits)) return cudaErrorInvalidValue;
+  if (binary && (topk || !p.qbits || !p.hist || !p.out_dist || p.nbins != p.dpad * 8 + 1))
+    return cudaErrorInvalidValue;
   int cpl = 0;
   const int rpg = rows_per_group(p.dpad, binary, &cpl);
   if (p.rows_per_tile % (32 * rpg) != 0) return cudaErrorInvalidValue;

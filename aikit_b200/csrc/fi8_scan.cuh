@@ -31,9 +31,13 @@ struct ScanParams {
   uint64_t* lvl1;            // [M][G][kp] per-CTA top-kp lists
   uint64_t* lvl2;            // [M][NB][kp] per-block top-kp lists
   uint64_t* out_keys;        // [M][k] final keys, 0 = empty
-  // binary (packed sign bit) mode: codes are [n_alloc][dpad] bytes of packed
-  // bits, scales unused, and qbits holds each query's packed bits
+  // binary (packed sign bit) histogram mode: codes are [n_alloc][dpad] bytes
+  // of packed bits, scales unused, qbits holds each query's packed bits
   const uint64_t* qbits;     // [M][dpad / 8]
+  uint16_t* out_dist;        // [M][dist_stride] Hamming distances
+  int64_t dist_stride;
+  unsigned int* hist;        // [M][nbins] distance counts (accumulated into)
+  int32_t nbins;             // dpad * 8 + 1
   // score mode
   float* out_scores;         // [M][n]
   unsigned int* err;         // device error flags (bit 0: wait timeout)

@@ -133,7 +133,12 @@ typedef struct {
   float* out_f;     /* optional float rows */
   int8_t* out_q;    /* optional codes */
   float* out_s;     /* optional scales */
+  const float* center;  /* sign codes: subtracted before the sign test (may be NULL) */
+  uint64_t* out_bits;   /* optional packed sign codes, ceil(d/64) words per row */
+  double* out_sum;      /* optional column sums, one d-vector per 4096-row block */
 } job_t;
+
+enum { SUM_BLOCK = 4096 };
 
 static void gen_row(const job_t* jb, int64_t row, float* v) {
   const int64_t d = jb->d;
@@ -158,10 +163,24 @@ static void gen_row(const job_t* jb, int64_t row, float* v) {
 static void* run_job(void* p) {
   const job_t* jb = (const job_t*)p;
   float* tmp = (float*)malloc(sizeof(float) * (size_t)(jb->d > 0 ? jb->d : 1));
+  const int64_t words = (jb->d + 63) / 64;
   for (int64_t r = jb->r0; r < jb->r1; r++) {
     const int64_t row = jb->row0 + r;
     float* v = jb->out_f ? jb->out_f + r * jb->d : tmp;
     gen_row(jb, row, v);
+    if (jb->out_sum) {
+      double* acc = jb->out_sum + (r / SUM_BLOCK) * jb->d;
+      for (int64_t j = 0; j < jb->d; j++) acc[j] += (double)v[j];
+    }
+    if (jb->out_bits) {
+      /* PackSignBitsRow of v - center (linalg/hamming.go:28-37) */
+      uint64_t* w = jb->out_bits + r * words;
+      memset(w, 0, sizeof(uint64_t) * (size_t)words);
+      for (int64_t j = 0; j < jb->d; j++) {
+        const float x = jb->center ? v[j] - jb->center[j] : v[j];
+        if (x >= 0.0f) w[j >> 6] |= 1ull << (j & 63);
+      }
+    }
     if (jb->out_q) {
       if (jb->kind == KIND_TIES) {
         for (int64_t j = 0; j < jb->d; j++) jb->out_q[r * jb->d + j] = (int8_t)v[j];
@@ -180,7 +199,8 @@ static void run_parallel(job_t base, int64_t nrows, int nthreads) {
   if (nthreads > nrows) nthreads = (int)(nrows > 0 ? nrows : 1);
   pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)nthreads);
   job_t* jobs = (job_t*)malloc(sizeof(job_t) * (size_t)nthreads);
-  const int64_t per = (nrows + nthreads - 1) / nthreads;
+  int64_t per = (nrows + nthreads - 1) / nthreads;
+  if (base.out_sum) per = (per + SUM_BLOCK - 1) / SUM_BLOCK * SUM_BLOCK;  /* a block never spans threads */
   int started = 0;
   for (int t = 0; t < nthreads; t++) {
     jobs[t] = base;
@@ -216,6 +236,54 @@ void syn_rows(int kind, uint64_t seed, uint64_t stream, const float* centers, in
   base.row0 = row0;
   base.d = d;
   base.out_f = out_f;
+  base.out_q = out_q;
+  base.out_s = out_s;
+  run_parallel(base, nrows, nthreads);
+}
+
+/* Column sums over rows [row0, row0+nrows) in float64, in the order: rows
+ * summed within 4096-row blocks, then the blocks in row order. The result does
+ * not depend on the thread count. out_sum [d]. */
+void syn_column_sums(int kind, uint64_t seed, uint64_t stream, const float* centers, int64_t ncl, float sigma,
+                     int64_t row0, int64_t nrows, int64_t d, double* out_sum, int nthreads) {
+  const int64_t nblk = (nrows + SUM_BLOCK - 1) / SUM_BLOCK;
+  double* part = (double*)calloc((size_t)(nblk > 0 ? nblk : 1) * (size_t)d, sizeof(double));
+  job_t base;
+  memset(&base, 0, sizeof(base));
+  base.kind = kind;
+  base.seed = seed;
+  base.stream = stream;
+  base.centers = centers;
+  base.ncl = ncl > 0 ? ncl : 1;
+  base.sigma = sigma;
+  base.row0 = row0;
+  base.d = d;
+  base.out_sum = part;
+  run_parallel(base, nrows, nthreads);
+  for (int64_t j = 0; j < d; j++) out_sum[j] = 0.0;
+  for (int64_t b = 0; b < nblk; b++)
+    for (int64_t j = 0; j < d; j++) out_sum[j] += part[b * d + j];
+  free(part);
+}
+
+/* Rows [row0, row0+nrows) as a FlatBinaryI8 corpus: packed sign codes of
+ * (v - center) (center may be NULL) into out_bits [nrows][ceil(d/64)] and, if
+ * out_q is given, the QuantizeRowInt8 codes and scales. */
+void syn_binary_rows(int kind, uint64_t seed, uint64_t stream, const float* centers, int64_t ncl, float sigma,
+                     int64_t row0, int64_t nrows, int64_t d, const float* center, uint64_t* out_bits,
+                     int8_t* out_q, float* out_s, int nthreads) {
+  job_t base;
+  memset(&base, 0, sizeof(base));
+  base.kind = kind;
+  base.seed = seed;
+  base.stream = stream;
+  base.centers = centers;
+  base.ncl = ncl > 0 ? ncl : 1;
+  base.sigma = sigma;
+  base.row0 = row0;
+  base.d = d;
+  base.center = center;
+  base.out_bits = out_bits;
   base.out_q = out_q;
   base.out_s = out_s;
   run_parallel(base, nrows, nthreads);

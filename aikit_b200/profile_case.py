@@ -22,7 +22,8 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=100)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
-    ap.add_argument("--mode", choices=["topk", "score"], default="topk")
+    ap.add_argument("--mode", choices=["topk", "score", "binary"], default="topk")
+    ap.add_argument("--over", type=int, default=100, help="binary mode: overquery (cand = k * over)")
     ap.add_argument("--trace", action="store_true",
                     help="also report per-kernel device time (torch.profiler / CUPTI) over the reps")
     a = ap.parse_args()
@@ -31,9 +32,11 @@ def main() -> None:
     from aikit_b200 import synth
     from aikit_b200.ann import B200Backend
 
+    be = B200Backend(0)
+    if a.mode == "binary":
+        return binary_case(a, be)
     r = synth.Recipe(synth.MIXTURE, a.dim, seed=20260, ncl=1000, sigma=0.3)
     bq, bs = r.codes(a.rows)
-    be = B200Backend(0)
     ix = be.NewI8Index(bq, bs, a.rows, a.dim)
     Q = torch.from_numpy(r.queries(a.batch)).cuda()
     keys = torch.zeros((a.batch, a.k), dtype=torch.int64, device="cuda")
@@ -76,6 +79,37 @@ def main() -> None:
     if kernels is not None:
         out["kernels"] = kernels
     print(json.dumps(out))
+
+
+def binary_case(a, be) -> None:
+    """FlatBinaryI8 on a UNIT corpus (the C4 recipe): --reps batch queries of
+    prefilter + rerank, device-resident, one stream."""
+    import torch
+    from aikit_b200 import synth
+    r = synth.Recipe(synth.UNIT, a.dim, seed=20264)
+    ctr = r.center(a.rows)
+    bits, q8, sc = r.binary(a.rows, ctr)
+    bix = be.NewBinaryI8Index(bits, bits.shape[1], ctr, q8, sc, a.rows, a.dim, a.over)
+    cand = a.k * a.over
+    Q = torch.from_numpy(r.queries(a.batch)).cuda()
+    short = torch.zeros((a.batch, cand), dtype=torch.int64, device="cuda")
+    keys = torch.zeros((a.batch, a.k), dtype=torch.int64, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    times = []
+    for _ in range(a.reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        bix.prefilter_async(Q.data_ptr(), a.batch, cand, short.data_ptr(), stream.cuda_stream)
+        bix.rerank_async(Q.data_ptr(), a.batch, short.data_ptr(), cand, a.k, keys.data_ptr(), stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    bix.sync()
+    gbs = [a.batch * a.rows * bits.shape[1] * 8 / (t * 1e-3) / 1e9 for t in times]
+    print(json.dumps({"mode": "binary", "rows": a.rows, "dim": a.dim, "k": a.k, "cand": cand, "batch": a.batch,
+                      "ms": times, "codes_gbs_per_pass": gbs}))
 
 
 if __name__ == "__main__":

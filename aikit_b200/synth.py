@@ -32,6 +32,10 @@ def lib():
         L.syn_rows.argtypes = [C.c_int, C.c_uint64, C.c_uint64, P, C.c_int64, C.c_float, C.c_int64,
                                C.c_int64, C.c_int64, P, P, P, C.c_int]
         L.syn_normal_rows.argtypes = [C.c_uint64, C.c_uint64, C.c_int64, C.c_int64, C.c_int64, P]
+        L.syn_column_sums.argtypes = [C.c_int, C.c_uint64, C.c_uint64, P, C.c_int64, C.c_float, C.c_int64,
+                                      C.c_int64, C.c_int64, P, C.c_int]
+        L.syn_binary_rows.argtypes = [C.c_int, C.c_uint64, C.c_uint64, P, C.c_int64, C.c_float, C.c_int64,
+                                      C.c_int64, C.c_int64, P, P, P, P, C.c_int]
         L.syn_quantize_row.restype = C.c_float
         L.syn_quantize_row.argtypes = [P, C.c_int64, P, C.c_float]
         _lib = L
@@ -74,6 +78,28 @@ class Recipe:
         s = out_s if out_s is not None else np.empty(n, np.float32)
         self._call(stream, row0, n, None, q, s, nthreads)
         return q, s
+
+    def center(self, n: int, row0: int = 0, nthreads: int = 0) -> np.ndarray:
+        """float32(column mean) of rows [row0, row0+n), accumulated in float64
+        (the centring of newBinaryPrefilter, ann/flat_binary_prefilter.go:64-85,
+        summed block-wise so it can be generated in parallel)."""
+        acc = np.empty(self.d, np.float64)
+        lib().syn_column_sums(self.kind, self.seed, CORPUS, _p(self._centers), self.ncl, self.sigma,
+                              row0, n, self.d, _p(acc), _threads(nthreads))
+        return (acc / float(n)).astype(np.float32)
+
+    def binary(self, n: int, center=None, row0: int = 0, nthreads: int = 0, with_codes: bool = True):
+        """A FlatBinaryI8 corpus without materialising float rows: packed sign
+        codes [n, ceil(d/64)] uint64 of (v - center), and the int8 rows and
+        scales (None when with_codes is False)."""
+        words = (self.d + 63) // 64
+        bits = np.empty((n, words), np.uint64)
+        q = np.empty((n, self.d), np.int8) if with_codes else None
+        s = np.empty(n, np.float32) if with_codes else None
+        ctr = None if center is None else np.ascontiguousarray(center, np.float32)
+        lib().syn_binary_rows(self.kind, self.seed, CORPUS, _p(self._centers), self.ncl, self.sigma, row0, n,
+                              self.d, _p(ctr), _p(bits), _p(q), _p(s), _threads(nthreads))
+        return bits, q, s
 
     def queries(self, m: int, row0: int = 0, nthreads: int = 0) -> np.ndarray:
         return self.floats(m, row0=row0, stream=QUERIES, nthreads=nthreads)

@@ -64,26 +64,29 @@ NCU_TRAFFIC = {
 }
 
 
-def kernel_roofline(kt: dict, kernel: str, pk: dict, pk_kind: str, region_ms: float) -> dict:
+def kernel_roofline(kt: dict, kernel: str, pk: dict, pk_kind: str, region_ms: float,
+                    ncu_key: str | None = None) -> dict:
     """Roofline of the dominant kernel from the library's per-launch CUDA events
     over the timed region: algorithmic bytes per launch / mean launch time."""
     t = kt[kernel]
     per_launch_bytes = t["bytes"] / t["launches"]
     per_launch_ms = t["ms"] / t["launches"]
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
-    ncu = NCU_TRAFFIC[kernel]
-    return {
+    ncu = NCU_TRAFFIC.get(ncu_key or kernel)
+    out = {
         "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
         "frac": achieved / pk["hbm_gbs"],
-        "traffic": per_launch_bytes * ncu["dram_bytes"] / ncu["algorithmic_bytes"],
+        "traffic": per_launch_bytes * ncu["dram_bytes"] / ncu["algorithmic_bytes"] if ncu else None,
         "kernel": kernel, "launches": t["launches"], "ms_per_launch": per_launch_ms,
         "algorithmic_bytes_per_launch": per_launch_bytes,
         "share_of_region": t["ms"] / region_ms,
         "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
-        "traffic_source": f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
-                          "times this run's mean launch bytes",
         "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json copy bandwidth)",
     }
+    if ncu:
+        out["traffic_source"] = (f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
+                                 "times this run's mean launch bytes")
+    return out
 
 
 # ----------------------------------------------------------------------------
@@ -344,9 +347,112 @@ def main():
         out["batch1"] = {"value": 1e3 / per1, "unit": "queries/s", "ms_per_query": per1,
                          "roofline": kernel_roofline(kt1, "scan_kernel", pk, pk_kind, ms1)}
     if world == 1:
+        out["flat_binary"] = binary_leg(be, args, stream, pk, pk_kind, local)
         out["cpu_baseline"] = cpu_baseline()
     print(json.dumps(out))
     return 0
+
+
+# ----------------------------------------------------------------------------
+# FlatBinaryI8 (C4 row shape): sign-bit Hamming prefilter + int8 rerank
+# ----------------------------------------------------------------------------
+BIN_ROWS = 4_000_000   # sample of C4's 25M-row per-GPU shard (C4: 2e8 rows over 8 GPUs)
+BIN_DIM = 1024
+BIN_K = 10
+BIN_OVER = 100         # cand = K * over = 1000, BASELINE's shortlist
+
+
+def binary_leg(be, args, stream, pk, pk_kind, local):
+    """Batch-1 FlatBinaryI8 queries on a C4-shaped shard: device-resident
+    prefilter + rerank timed on the device, then the host entry point."""
+    import torch
+    from aikit_b200 import synth
+    from aikit_b200.ann import unpack_keys
+    r = synth.Recipe(synth.UNIT, BIN_DIM, seed=SEED + 4)
+    t0 = time.time()
+    ctr = r.center(BIN_ROWS)
+    bits, q8, sc = r.binary(BIN_ROWS, ctr)
+    gen_s = time.time() - t0
+    bix = be.NewBinaryI8Index(bits, bits.shape[1], ctr, q8, sc, BIN_ROWS, BIN_DIM, BIN_OVER)
+    del q8, sc
+    cand = BIN_K * BIN_OVER
+    nb = 16
+    Qh = r.queries(nb)
+    Qd = torch.from_numpy(Qh).cuda()
+    short = torch.zeros((1, cand), dtype=torch.int64, device="cuda")
+    keys = torch.zeros((1, BIN_K), dtype=torch.int64, device="cuda")
+    st = stream.cuda_stream
+
+    def step(i):
+        bix.prefilter_async(Qd[i % nb].data_ptr(), 1, cand, short.data_ptr(), st)
+        n = bix.last_launch_count()
+        bix.rerank_async(Qd[i % nb].data_ptr(), 1, short.data_ptr(), cand, BIN_K, keys.data_ptr(), st)
+        return n + bix.last_launch_count()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    bix.sync()
+    bix.kernel_times(reset=True)
+    bix.set_kernel_timing(True)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        launches = 0
+        for i in range(args.steps):
+            launches += step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    bix.set_kernel_timing(False)
+    kt = bix.kernel_times(reset=True)
+    ms = ev0.elapsed_time(ev1)
+    bix.sync()
+    gidx, _ = unpack_keys(keys.cpu().numpy().view(np.uint64))
+    assert (gidx[0] >= 0).all(), "binary top-K came back short"
+    # e2e: the host entry point (fi8_bin_query_topk) from pinned query rows
+    Qpin = torch.from_numpy(Qh.copy()).pin_memory().numpy()
+    bix.topk_arrays(Qpin[0:1], BIN_K)
+    t1 = time.perf_counter()
+    for i in range(args.steps):
+        bix.topk_arrays(Qpin[i % nb:i % nb + 1], BIN_K)
+    e2e_s = time.perf_counter() - t1
+    out = {
+        "metric": "FlatBinaryI8 top-K queries/sec", "value": args.steps / (ms / 1e3), "unit": "queries/s",
+        "ms_per_query": ms / args.steps, "dtype": "u64 popcount + int8 rerank",
+        "config": {"workload": f"C4 row shape: d={BIN_DIM} sign codes (128 B) of centred N(0,1) rows + int8 "
+                               f"copies, K={BIN_K}, overquery {BIN_OVER} (cand {cand}), batch 1, "
+                               f"{BIN_ROWS:,} rows (a sample of C4's 25M-row per-GPU shard)",
+                   "n_rows": BIN_ROWS, "codes_bytes": int(bits.nbytes), "l2": "codes 512 MB > 126 MB L2",
+                   "corpus_gen_s": round(gen_s, 1)},
+        "roofline": kernel_roofline(kt, "scan_kernel", pk, pk_kind, ms, ncu_key="scan_kernel_binary"),
+        "gpu_launches": launches,
+        "e2e": {"value": args.steps / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": BIN_DIM * 4,
+                "d2h_bytes_per_step": BIN_K * 8, "api": "fi8_bin_query_topk (include/fi8.h), pinned host query"},
+        "clocks": clk.summary(),
+        "cpu_baseline": binary_cpu_baseline(bits, ctr, Qh, r),
+    }
+    bix.Close()
+    return out
+
+
+def binary_cpu_baseline(bits, ctr, Qh, r, budget_s: float = 6.0):
+    """The reference algorithm (oracle port of FlatBinaryI8.Query) on a row
+    sample of the same corpus, scaled linearly to the shard."""
+    import oracle
+    rows = 1_000_000
+    q8, sc = r.codes(rows)  # the UNIT recipe's FlatI8 rows (same arithmetic as r.binary's)
+    done, t0 = 0, time.perf_counter()
+    while done < len(Qh) and (done < 2 or time.perf_counter() - t0 < budget_s):
+        oracle.flat_binary_i8_query(bits[:rows], ctr, q8, sc, BIN_OVER, Qh[done], BIN_K, nthreads=1)
+        done += 1
+    dt = time.perf_counter() - t0
+    per_query = dt / done * (BIN_ROWS / rows)
+    return {"value": 1.0 / per_query, "unit": "queries/s", "cores": 1, "kind": "port",
+            "sample": f"{done} FlatBinaryI8.Query calls (pack, prefilterHist, rerank) on one thread over "
+                      f"{rows:,} of {BIN_ROWS:,} rows, time scaled by {BIN_ROWS // rows}x (the reference "
+                      f"splits the Hamming scan over GOMAXPROCS workers; this port runs it on one)"}
 
 
 def reference_arm(args, world):

@@ -354,3 +354,19 @@ def test_synth_quantizer_matches_oracle():
     for i in range(len(v)):
         q2, s2 = synth.quantize_row(v[i])
         assert q2.tobytes() == q1[i].tobytes() and s2 == s1[i]
+
+
+def test_synth_binary_corpus_matches_oracle():
+    """The bench's FlatBinaryI8 generator (no float rows kept) produces the
+    oracle's packed sign codes and int8 rows for the same floats; its centre is
+    the float64 column mean (block-summed)."""
+    r = synth.Recipe(synth.MIXTURE, 200, seed=8, ncl=6, sigma=0.3)
+    n = 9000
+    v = r.floats(n)
+    ctr = r.center(n)
+    want_ctr = (v.astype(np.float64).sum(axis=0) / n).astype(np.float32)
+    assert np.abs(ctr.astype(np.float64) - want_ctr).max() <= 1e-7
+    bits, q, s = r.binary(n, ctr)
+    assert bits.tobytes() == oracle.pack_codes(v, ctr).tobytes()
+    bq, bs = oracle.quantize_rows(v)
+    assert q.tobytes() == bq.tobytes() and s.tobytes() == bs.tobytes()
