@@ -49,7 +49,7 @@ SIGNATURES = {
     "fi8_bin_index_destroy": (C.c_int, [_P]),
     "fi8_bin_index_handle": (C.c_int, [_P, _P]),
     "fi8_bin_query_topk": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
-    "fi8_bin_prefilter_async": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
+    "fi8_bin_prefilter_async": (C.c_int, [_P, _P, _I32, _I32, _P, _I32, _P]),
     "fi8_bin_rerank_async": (C.c_int, [_P, _P, _I32, _P, _I32, _I32, _P, _P]),
 }
 

@@ -288,9 +288,12 @@ class BinaryI8Index:
         check(lib().fi8_bin_query_topk(self._h, _p(Q), M, k, _p(idx), _p(sc)))
         return idx, sc
 
-    def prefilter_async(self, d_q: int, M: int, cand: int, d_keys: int, stream: int = 0) -> None:
+    def prefilter_async(self, d_q: int, M: int, cand: int, d_keys: int, stream: int = 0,
+                        sorted_keys: bool = True) -> None:
+        """The shortlist keys (-distance, global id) into d_keys [M][cand];
+        sorted_keys=False skips the sort (fine for the rerank, not a merge)."""
         check(lib().fi8_bin_prefilter_async(self._h, C.c_void_p(d_q), M, cand, C.c_void_p(d_keys),
-                                            C.c_void_p(stream or None)))
+                                            1 if sorted_keys else 0, C.c_void_p(stream or None)))
 
     def rerank_async(self, d_q: int, M: int, d_short: int, cand: int, k: int, d_keys: int,
                      stream: int = 0) -> None:

@@ -1058,7 +1058,7 @@ int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t
   return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
 }
 
-int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
+int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys, int32_t sorted,
                             void* stream) {
   if (!b) return fail(FI8_ERR_ARG, "fi8_bin_prefilter_async: null index");
   if (M == 0) return FI8_OK;
@@ -1067,7 +1067,7 @@ int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t can
   std::lock_guard<std::mutex> lk(b->ix->mu);
   DeviceGuard g(b->ix->device);
   b->ix->last_launches = 0;
-  return launch_bin_prefilter(b, d_q, M, cand, d_keys, true, static_cast<cudaStream_t>(stream));
+  return launch_bin_prefilter(b, d_q, M, cand, d_keys, sorted != 0, static_cast<cudaStream_t>(stream));
 }
 
 int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,

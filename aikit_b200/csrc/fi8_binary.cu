@@ -53,11 +53,33 @@ __global__ void __launch_bounds__(1024) binary_prep_kernel(const float* q, int d
   for (int b = threadIdx.x; b < nbins; b += blockDim.x) hist[(size_t)y * nbins + b] = 0u;
 }
 
+// Block-wide (kSegThreads) exclusive prefix of v; *total = the sum.
+__device__ __forceinline__ long long block_excl_scan64(long long v, long long* total) {
+  __shared__ long long s_w[kSegThreads / 32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  long long incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const long long x = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += x;
+  }
+  if (lane == 31) s_w[w] = incl;
+  __syncthreads();
+  long long wbase = 0, all = 0;
+#pragma unroll
+  for (int i = 0; i < kSegThreads / 32; i++) {
+    if (i < w) wbase += s_w[i];
+    all += s_w[i];
+  }
+  __syncthreads();
+  *total = all;
+  return wbase + incl - v;
+}
+
 // prefilterHist's cut (prefilter.go:182-189): the smallest t with
 // cum(t) + hist[t] >= cand; *lt = cum(t) (rows below t). t = nbins when the
 // corpus holds fewer than cand rows (every row is taken). Block-wide.
 __device__ void find_cut(const unsigned int* hist, int nbins, int64_t cand, int* t_out, int64_t* lt_out) {
-  __shared__ long long s_part[kSegThreads];
   __shared__ int s_t;
   __shared__ long long s_lt;
   const int tid = threadIdx.x;
@@ -65,23 +87,14 @@ __device__ void find_cut(const unsigned int* hist, int nbins, int64_t cand, int*
   const int b0 = tid * per, b1 = min(nbins, b0 + per);
   long long mine = 0;
   for (int b = b0; b < b1; b++) mine += hist[b];
-  s_part[tid] = mine;
+  long long all;
+  const long long before = block_excl_scan64(mine, &all);
   if (tid == 0) {
     s_t = nbins;
-    s_lt = 0;
+    s_lt = all;  // fewer than cand rows: all of them are below the cut
   }
   __syncthreads();
-  if (tid == 0) {  // exclusive prefix over the 256 partial sums
-    long long run = 0;
-    for (int i = 0; i < kSegThreads; i++) {
-      const long long v = s_part[i];
-      s_part[i] = run;
-      run += v;
-    }
-  }
-  __syncthreads();
-  const long long before = s_part[tid];
-  if (before < cand && before + mine >= cand) {
+  if (before < cand && before + mine >= cand) {  // exactly one thread
     long long cum = before;
     for (int b = b0; b < b1; b++) {
       if (cum + (long long)hist[b] >= cand) {
@@ -93,14 +106,6 @@ __device__ void find_cut(const unsigned int* hist, int nbins, int64_t cand, int*
     }
   }
   __syncthreads();
-  if (s_t == nbins) {  // fewer than cand rows: all of them are below the cut
-    if (tid == 0) {
-      long long all = 0;
-      for (int i = 0; i < nbins; i++) all += hist[i];
-      s_lt = all;
-    }
-    __syncthreads();
-  }
   *t_out = s_t;
   *lt_out = s_lt;
 }
@@ -209,23 +214,21 @@ __global__ void __launch_bounds__(kSegThreads) shortlist_emit_kernel(const uint1
   int64_t lt_all;
   find_cut(hist + (size_t)y * nbins, nbins, cand, &t, &lt_all);
   const int64_t budget = cand - lt_all;
-  __shared__ long long s_ltp, s_eqp, s_eqall;
-  if (threadIdx.x == 0) {
-    long long a = 0, b = 0, e = 0;
-    const unsigned int* cy = counts + (size_t)y * P * 2;
-    for (int i = 0; i < P; i++) {
-      if (i < p) {
-        a += cy[2 * i];
-        b += cy[2 * i + 1];
-      }
-      e += cy[2 * i + 1];
+  // lower segments' counts (below t, at t) and all segments' ties at t
+  long long a = 0, b = 0, e = 0;
+  const unsigned int* cy = counts + (size_t)y * P * 2;
+  for (int i = threadIdx.x; i < P; i += kSegThreads) {
+    const unsigned int l = cy[2 * i], q = cy[2 * i + 1];
+    if (i < p) {
+      a += l;
+      b += q;
     }
-    s_ltp = a;
-    s_eqp = b;
-    s_eqall = e;
+    e += q;
   }
-  __syncthreads();
-  int64_t ltp = s_ltp, eqp = s_eqp;
+  long long ltp, eqp, eq_all;
+  block_excl_scan64(a, &ltp);
+  block_excl_scan64(b, &eqp);
+  block_excl_scan64(e, &eq_all);
   uint64_t* oy = out + (size_t)y * cand;
   int64_t lo, hi;
   seg_bounds(n, P, p, &lo, &hi);
@@ -262,7 +265,7 @@ __global__ void __launch_bounds__(kSegThreads) shortlist_emit_kernel(const uint1
     eqp += te;
   }
   if (p == 0) {
-    const int64_t eq_taken = s_eqall < budget ? s_eqall : budget;
+    const int64_t eq_taken = eq_all < budget ? eq_all : budget;
     for (int64_t i = lt_all + eq_taken + threadIdx.x; i < cand; i += kSegThreads) oy[i] = kEmptyKey;
   }
 }

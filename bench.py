@@ -61,6 +61,10 @@ NCU_TRAFFIC = {
                     "profile": "profiles/gemm_kernel_c2_batch64.md"},
     "scan_kernel": {"dram_bytes": 3.088212e9 + 4.358144e6, "algorithmic_bytes": 4_000_000 * (DIM + 4) + DIM * 4,
                     "profile": "profiles/scan_kernel_c2_batch1.md"},
+    # binary (Hamming histogram) mode: 4M rows x 128-byte codes, plus the u16 distance written per row
+    "scan_kernel_binary": {"dram_bytes": 512.031744e6 + 10.409216e6,
+                           "algorithmic_bytes": 4_000_000 * 128 + 128 + 2 * 4_000_000,
+                           "profile": "profiles/scan_kernel_binary_c4.md"},
 }
 
 
@@ -384,7 +388,7 @@ def binary_leg(be, args, stream, pk, pk_kind, local):
     st = stream.cuda_stream
 
     def step(i):
-        bix.prefilter_async(Qd[i % nb].data_ptr(), 1, cand, short.data_ptr(), st)
+        bix.prefilter_async(Qd[i % nb].data_ptr(), 1, cand, short.data_ptr(), st, sorted_keys=False)
         n = bix.last_launch_count()
         bix.rerank_async(Qd[i % nb].data_ptr(), 1, short.data_ptr(), cand, BIN_K, keys.data_ptr(), st)
         return n + bix.last_launch_count()

@@ -190,10 +190,12 @@ int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t
  * reference computes it over the whole corpus -- then every rank reranks the
  * shortlist rows it holds and the M x k results are merged again.
  * fi8_bin_prefilter_async: d_q [M*dim] f32 -> d_keys [M*cand] packed keys of
- * (-distance, global id), sorted, 0-padded. fi8_bin_rerank_async: d_short
+ * (-distance, global id), 0-padded; sorted != 0 sorts each query's keys
+ * descending, which the key merge needs (the rerank takes any order).
+ * fi8_bin_rerank_async: d_short
  * [M*cand] keys (rows of other shards are skipped) -> d_keys [M*k] W8A8 keys,
  * sorted, 0-padded. Stream semantics as fi8_topk_batch_async. */
-int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
+int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys, int32_t sorted,
                             void* stream);
 int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,
                          uint64_t* d_keys, void* stream);
