@@ -25,7 +25,7 @@
 //            lanes 32*(w%4).. = its queries, and one quarter of the 256
 //            columns), a branch-free float pre-filter against the query's
 //            threshold, then the exact key test and append for survivors.
-// No TMA multicast is used anywhere.
+// Every TMA load here is a plain single-CTA load into this CTA's shared memory.
 #include <cuda.h>
 
 #include "fi8_device.cuh"

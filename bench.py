@@ -216,9 +216,9 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from aikit_b200.dist import ShardedTopK, shard_bounds
     n_total = args.rows
-    lo = n_total * rank // world
-    hi = n_total * (rank + 1) // world
+    lo, hi = shard_bounds(n_total, world, rank)
     recipe = synth.Recipe(synth.MIXTURE, DIM, seed=SEED, ncl=NCL, sigma=SIGMA)
     t0 = time.time()
     bq, bs = recipe.codes(hi - lo, row0=lo)
@@ -234,18 +234,13 @@ def main():
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     st = stream.cuda_stream
-    keys_local = torch.zeros((BATCH, K), dtype=torch.int64, device="cuda")
-    gathered = torch.zeros((world, BATCH, K), dtype=torch.int64, device="cuda")
-    merged = torch.zeros((BATCH, K), dtype=torch.int64, device="cuda")
+    sharded = ShardedTopK(ix, be.ctx, world, stream)
+    result = {}
 
     def step(i, m=BATCH):
-        ix.topk_async(Qd[i % nb].data_ptr(), m, K, keys_local.data_ptr(), st)
-        launches = ix.last_launch_count()
-        if world > 1:  # multi-GPU runs the batch-64 form only
-            dist.all_gather_into_tensor(gathered.view(-1), keys_local.view(-1))
-            be.ctx.merge_keys_async(gathered.data_ptr(), world, m, K, merged.data_ptr(), st)
-            launches += 1
-        return launches
+        # multi-GPU runs the batch-64 form only: local scan, all-gather, merge
+        result["keys"] = sharded.topk_async(Qd[i % nb].data_ptr(), m, K)
+        return ix.last_launch_count() + (1 if world > 1 else 0)
 
     def timed(nsteps, m):
         ev0 = torch.cuda.Event(enable_timing=True)
@@ -306,7 +301,7 @@ def main():
         for i in range(args.steps):
             Qd[i % nb].copy_(Qpin[i % nb], non_blocking=True)
             step(i)
-            hk.copy_(merged, non_blocking=True)
+            hk.copy_(result["keys"], non_blocking=True)
             torch.cuda.synchronize()
             unpack_keys(hk.numpy().view(np.uint64))
         e2e_s = time.perf_counter() - t0
@@ -318,8 +313,7 @@ def main():
                "api": "fi8_topk_batch_async + NCCL all-gather + fi8_merge_keys_async, pinned host I/O"}
 
     # sanity: spot-check one query of the last batch against the device answer shape
-    got = merged if world > 1 else keys_local
-    gidx, _ = unpack_keys(got.cpu().numpy().view(np.uint64))
+    gidx, _ = unpack_keys(result["keys"].cpu().numpy().view(np.uint64))
     assert (gidx[0] >= 0).all(), "top-K came back short"
 
     if world > 1:
