@@ -522,6 +522,7 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
     p.row_lo = ranges[i].row_lo;
     p.row_hi = ranges[i].row_hi;
     p.rtiles = (p.row_hi - p.row_lo + kGemmBN - 1) / kGemmBN;
+    p.producer_waits = i == 0 ? 1 : 0;  // the first range follows the quantize kernel
     const int64_t units = (int64_t)p.qtiles * p.rtiles;
     const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(x->sm_count, units));
     t0 = timer_begin(x, st);

@@ -78,6 +78,12 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// Programmatic dependent launch: let the next kernel in the stream be
+// scheduled now, and (per thread) wait until the previous one has completed
+// and its memory is visible.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -175,9 +181,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
+  pdl_launch_dependents();
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
+    // The corpus tiles depend on nothing earlier in the stream; the query tile
+    // A does, on the quantize kernel, which only the first range's launch
+    // follows directly. Later ranges stream while the previous select runs.
     if (lane == 0) {
+      if (p.producer_waits) pdl_wait_prior();
       int64_t step = 0;
       for (int64_t u = 0; u < my_units && !s_abort; u++) {
         const int64_t unit = blockIdx.x + u * G;
@@ -256,6 +267,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       cp_async8(my_scale + 2 * lane, p.scales + row0 + cq * 64 + 2 * lane);
     }
     cp_async_commit();
+    // thresholds, counts and the candidate list come from the previous select
+    pdl_wait_prior();
     // per-query state of the current query tile (constant within a launch)
     // (a lane without a query gets qs = 0 and Tscore = +inf: it never passes)
     int cur_qt = -1, q = 0;
@@ -488,6 +501,8 @@ __global__ void __launch_bounds__(kSelThreads, 1)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   constexpr int bar = 1;
+  pdl_launch_dependents();
+  pdl_wait_prior();  // the range's GEMM has completed
   if (tid == 0) {
     s_count = 0;
     s_local_thr = 0;
@@ -652,8 +667,17 @@ cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Ge
                         cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
   if (e != cudaSuccess) return e;
-  gemm_kernel<<<G, kGemmThreads, kGemmSmem, stream>>>(tmA, tmB, p);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)G);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = kGemmSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_kernel, tmA, tmB, p);
 }
 
 cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,
@@ -674,8 +698,17 @@ cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsi
   const size_t smem = (size_t)(cap_s + kp) * 8;  // union buffer + kept list
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (8192 + 4096) * 8);
   if (e != cudaSuccess) return e;
-  select_kernel<<<M, kSelThreads, smem, stream>>>(k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)M);
+  cfg.blockDim = dim3(kSelThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, select_kernel, k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
 }
 
 }  // namespace fi8

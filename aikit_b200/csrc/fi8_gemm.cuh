@@ -32,6 +32,7 @@ struct GemmParams {
   uint64_t* cand;        // [M][cap] candidate keys
   int32_t cap;
   unsigned int* err;
+  int32_t producer_waits;  // 1: the producer waits for the previous kernel (it wrote A)
 };
 
 // Build a 2-D SWIZZLE_128B tensor map over an int8 matrix [rows][pitch]
