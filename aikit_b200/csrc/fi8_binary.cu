@@ -139,6 +139,8 @@ __global__ void __launch_bounds__(kSegThreads) shortlist_count_kernel(const uint
                                                                       int nbins,
                                                                       int64_t cand, int P, unsigned int* counts) {
   const int p = blockIdx.x, y = blockIdx.y;
+  pdl_launch_dependents();
+  pdl_wait_prior();  // the distance pass has completed
   int t;
   int64_t lt_all;
   find_cut(hist + (size_t)y * nbins, nbins, cand, &t, &lt_all);
@@ -210,6 +212,8 @@ __global__ void __launch_bounds__(kSegThreads) shortlist_emit_kernel(const uint1
                                                                      int64_t cand, int P, const unsigned int* counts,
                                                                      uint32_t id_base, uint64_t* out) {
   const int p = blockIdx.x, y = blockIdx.y;
+  pdl_launch_dependents();
+  pdl_wait_prior();  // the segment counts are complete
   int t;
   int64_t lt_all;
   find_cut(hist + (size_t)y * nbins, nbins, cand, &t, &lt_all);
@@ -275,6 +279,8 @@ __global__ void __launch_bounds__(1024) sort_keys_kernel(uint64_t* keys, int can
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* buf = reinterpret_cast<uint64_t*>(smem);
   uint64_t* ky = keys + (size_t)blockIdx.x * cand;
+  pdl_launch_dependents();
+  pdl_wait_prior();
   for (int i = threadIdx.x; i < candp; i += 1024) buf[i] = i < cand ? ky[i] : kEmptyKey;
   named_sync(1, 1024);
   group_sort_desc<1024>(buf, candp, threadIdx.x, 1);
@@ -296,6 +302,7 @@ __global__ void __launch_bounds__(kRerankThreads) rerank_kernel(const float* q, 
   int8_t* q_s = reinterpret_cast<int8_t*>(smem + (size_t)kp * 8);  // [dpad]
   const int p = blockIdx.x, y = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();
 
   // quantize the query (quant.go:43-71, all-zero -> scale 0)
   const float* qy = q + (size_t)y * d;
@@ -325,6 +332,7 @@ __global__ void __launch_bounds__(kRerankThreads) rerank_kernel(const float* q, 
   __syncthreads();
   const float qscale = s_qscale;
 
+  pdl_wait_prior();  // the shortlist is complete
   const int lane8 = lane & 7;
   const int e = p * kRerankRowsPerCta + (tid >> 3);
   const int chunks = dpad >> 4;
@@ -389,19 +397,17 @@ cudaError_t shortlist_launch(const uint16_t* dist, int64_t n, int64_t dstride, i
                              bool sorted, cudaStream_t stream) {
   if (M <= 0 || cand <= 0 || P <= 0 || dstride % kRowsPerThread != 0) return cudaErrorInvalidValue;
   dim3 grid((unsigned)P, (unsigned)M);
-  shortlist_count_kernel<<<grid, kSegThreads, 0, stream>>>(dist, n, dstride, hist, nbins, cand, P, counts);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(shortlist_count_kernel, grid, dim3(kSegThreads), 0, stream, dist, n, dstride, hist,
+                             nbins, (int64_t)cand, P, counts);
   if (e != cudaSuccess) return e;
-  shortlist_emit_kernel<<<grid, kSegThreads, 0, stream>>>(dist, n, dstride, hist, nbins, cand, P, counts, id_base,
-                                                          out);
-  e = cudaGetLastError();
+  e = launch_pdl(shortlist_emit_kernel, grid, dim3(kSegThreads), 0, stream, dist, n, dstride, hist, nbins,
+                 (int64_t)cand, P, (const unsigned int*)counts, id_base, out);
   if (e != cudaSuccess || !sorted) return e;
   if (cand > kRerankMaxCand) return cudaErrorInvalidValue;
   const int candp = pow2_ceil(cand);
   e = cudaFuncSetAttribute(sort_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRerankMaxCand * 8);
   if (e != cudaSuccess) return e;
-  sort_keys_kernel<<<M, 1024, (size_t)candp * 8, stream>>>(out, cand, candp);
-  return cudaGetLastError();
+  return launch_pdl(sort_keys_kernel, dim3((unsigned)M), dim3(1024), (size_t)candp * 8, stream, out, cand, candp);
 }
 
 int32_t rerank_parts(int32_t cand) { return (cand + kRerankRowsPerCta - 1) / kRerankRowsPerCta; }
@@ -417,11 +423,10 @@ cudaError_t rerank_launch(const float* q, int32_t M, int32_t d, int32_t dpad, co
   cudaError_t e = cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)((size_t)kRerankMaxCand * 8 + 2048));
   if (e != cudaSuccess) return e;
-  rerank_kernel<<<dim3((unsigned)P, (unsigned)M), kRerankThreads, smem, stream>>>(
-      q, d, dpad, codes, scales, n, id_base, shortlist, cand, k, kp, M, parts);
-  e = cudaGetLastError();
+  e = launch_pdl(rerank_kernel, dim3((unsigned)P, (unsigned)M), dim3(kRerankThreads), smem, stream, q, d, dpad, codes,
+                 scales, n, id_base, shortlist, cand, k, kp, M, parts);
   if (e != cudaSuccess) return e;
-  return merge_keys_launch(parts, P, M, k, out, stream);
+  return merge_keys_launch(parts, P, M, k, out, stream, true);
 }
 
 }  // namespace fi8

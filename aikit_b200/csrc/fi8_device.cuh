@@ -107,6 +107,33 @@ __device__ __forceinline__ float w8a8_score(int32_t dot, float qscale, float row
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). A kernel launched with
+// launch_pdl may be scheduled before the previous kernel in its stream has
+// finished: pdl_launch_dependents lets the next kernel be scheduled, and
+// pdl_wait_prior (per thread) waits until the previous kernel has completed
+// and its memory is visible. Without a programmatic dependency both are
+// no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... Exp, typename... Act>
+cudaError_t launch_pdl(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Act&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Exp>(args)...);
+}
+
+// ---------------------------------------------------------------------------
 // Bounded waits. Every spin in this library gives up after kWaitLimitNs of
 // wall time (globaltimer), records an error and lets the kernel unwind.
 // ---------------------------------------------------------------------------

@@ -97,6 +97,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
 
   const int64_t my_tiles = (p.ntiles > cta) ? (p.ntiles - cta + G - 1) / G : 0;
 
+  pdl_launch_dependents();
   if (tid == 0) {
     for (int s = 0; s < S; s++) {
       mbar_init(&s_full[s], 1);
@@ -144,6 +145,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
     const int bar = 1 + g;
     uint64_t* buf = bufs + (TOPK ? (size_t)g * p.cap : 0);
 
+    // the query (and, binary, the zeroed histogram) may come from the kernel
+    // just before this one; the producer streams the corpus meanwhile
+    pdl_wait_prior();
     if (BIN) {
       // the query's packed sign bits, prepared by the caller
       const int8_t* qb = reinterpret_cast<const int8_t*>(p.qbits) + (size_t)y * dpad;
@@ -371,6 +375,8 @@ __global__ void __launch_bounds__(kGroupThreads, 1)
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* slots = reinterpret_cast<uint64_t*>(smem);
   const int y = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait_prior();
   merge_global_lists(in + (size_t)y * k, nsrc, k, (size_t)M * k, kp, slots, nslots, threadIdx.x, 1);
   for (int i = threadIdx.x; i < k; i += kGroupThreads) out[(size_t)y * k + i] = slots[i];
 }
@@ -480,13 +486,15 @@ cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cu
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)G, (unsigned)M);
+  if (binary)  // follows the query packing kernel
+    return launch_pdl(fn, grid, dim3(kBlockThreads), (size_t)p.smem_bytes, stream, p);
   void* args[] = {const_cast<ScanParams*>(&p)};
   return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, dim3(kBlockThreads), args,
                           (size_t)p.smem_bytes, stream);
 }
 
 cudaError_t merge_keys_launch(const uint64_t* in, int32_t nsrc, int32_t M, int32_t k, uint64_t* out,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, bool pdl) {
   if (k <= 0 || k > kMergeMaxK || nsrc <= 0 || M <= 0) return cudaErrorInvalidValue;
   const int kp = pow2_at_least(k);
   int nslots = (int)(kSmemBudget / ((size_t)kp * 8));
@@ -495,6 +503,9 @@ cudaError_t merge_keys_launch(const uint64_t* in, int32_t nsrc, int32_t M, int32
   cudaError_t e = cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBudget);
   if (e != cudaSuccess) return e;
+  if (pdl)
+    return launch_pdl(merge_keys_kernel, dim3((unsigned)M), dim3(kGroupThreads), (size_t)nslots * kp * 8, stream, in,
+                      nsrc, M, k, kp, nslots, out);
   merge_keys_kernel<<<M, kGroupThreads, (size_t)nslots * kp * 8, stream>>>(in, nsrc, M, k, kp, nslots, out);
   return cudaGetLastError();
 }

@@ -65,8 +65,9 @@ inline int32_t scan_blocks(int32_t G) { return (G + kMergeBlock - 1) / kMergeBlo
 
 // Merge nsrc key lists per query ([nsrc][M][k], each sorted descending, 0 =
 // empty) into the top k per query ([M][k]). One CTA per query.
+// pdl: launched as a programmatic dependent of the kernel before it.
 cudaError_t merge_keys_launch(const uint64_t* in, int32_t nsrc, int32_t M, int32_t k,
-                              uint64_t* out, cudaStream_t stream);
+                              uint64_t* out, cudaStream_t stream, bool pdl = false);
 constexpr int32_t kMergeMaxK = 2048;
 
 }  // namespace fi8

@@ -397,21 +397,25 @@ def binary_leg(be, args, stream, pk, pk_kind, local):
         step(i)
     torch.cuda.synchronize()
     bix.sync()
-    bix.kernel_times(reset=True)
-    bix.set_kernel_timing(True)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+
+    def timed(kernel_events):
+        bix.kernel_times(reset=True)
+        bix.set_kernel_timing(kernel_events)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         ev0.record(stream)
-        launches = 0
+        n_launch = 0
         for i in range(args.steps):
-            launches += step(i)
+            n_launch += step(i)
         ev1.record(stream)
         torch.cuda.synchronize()
-    bix.set_kernel_timing(False)
-    kt = bix.kernel_times(reset=True)
-    ms = ev0.elapsed_time(ev1)
+        bix.set_kernel_timing(False)
+        return ev0.elapsed_time(ev1), n_launch, bix.kernel_times(reset=True)
+
+    with ClockSampler(local) as clk:
+        ms, launches, _ = timed(False)       # the headline: launches back to back
+        ms_ev, _, kt = timed(True)           # the same steps with per-kernel events
     bix.sync()
     gidx, _ = unpack_keys(keys.cpu().numpy().view(np.uint64))
     assert (gidx[0] >= 0).all(), "binary top-K came back short"
@@ -430,7 +434,8 @@ def binary_leg(be, args, stream, pk, pk_kind, local):
                                f"{BIN_ROWS:,} rows (a sample of C4's 25M-row per-GPU shard)",
                    "n_rows": BIN_ROWS, "codes_bytes": int(bits.nbytes), "l2": "codes 512 MB > 126 MB L2",
                    "corpus_gen_s": round(gen_s, 1)},
-        "roofline": kernel_roofline(kt, "scan_kernel", pk, pk_kind, ms, ncu_key="scan_kernel_binary"),
+        "roofline": dict(kernel_roofline(kt, "scan_kernel", pk, pk_kind, ms_ev, ncu_key="scan_kernel_binary"),
+                         kernel_events_pass_ms_per_query=ms_ev / args.steps),
         "gpu_launches": launches,
         "e2e": {"value": args.steps / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": BIN_DIM * 4,
                 "d2h_bytes_per_step": BIN_K * 8, "api": "fi8_bin_query_topk (include/fi8.h), pinned host query"},
