@@ -40,6 +40,16 @@ def _p(a: np.ndarray):
     return a.ctypes.data_as(C.c_void_p)
 
 
+def keep_bitmap(keep) -> np.ndarray:
+    """A keep predicate as the ABI's bitmap: keep[id] truthy -> bit id%64 of
+    word id/64 (uint64 words, little-endian bit order)."""
+    bits = np.packbits(np.asarray(keep, dtype=bool), bitorder="little")
+    pad = (-bits.size) % 8
+    if pad:
+        bits = np.concatenate([bits, np.zeros(pad, np.uint8)])
+    return bits.view(np.uint64)
+
+
 def device_count() -> int:
     n = C.c_int(0)
     check(lib().fi8_device_count(C.byref(n)))
@@ -172,16 +182,27 @@ class I8Index:
             out.append(row)
         return out
 
-    def topk_arrays(self, queries, k: int):
-        """TopKBatch as arrays: (int32 [M,k], float32 [M,k]), index -1 = empty."""
+    def topk_arrays(self, queries, k: int, keep=None):
+        """TopKBatch as arrays: (int32 [M,k], float32 [M,k]), index -1 = empty.
+        keep: optional boolean array over global ids (QueryFilter)."""
         Q = self._queries(queries)
         M = Q.shape[0]
         idx = np.empty((M, max(k, 0)), np.int32)
         sc = np.empty((M, max(k, 0)), np.float32)
         if M == 0:
             return idx, sc
-        check(lib().fi8_topk_batch(self._h, _p(Q), M, k, _p(idx), _p(sc)))
+        if keep is None:
+            check(lib().fi8_topk_batch(self._h, _p(Q), M, k, _p(idx), _p(sc)))
+        else:
+            bm = keep_bitmap(keep)
+            check(lib().fi8_topk_batch_keep(self._h, _p(Q), M, k, _p(bm), len(keep), _p(idx), _p(sc)))
         return idx, sc
+
+    def QueryFilterBatch(self, queries, k: int, keep) -> list[list[Hit]]:
+        """FlatI8.QueryFilter (ann/flat_i8.go:136) for a batch: keep[id]
+        (a boolean array over global ids) selects the rows that may be hit."""
+        idx, sc = self.topk_arrays(queries, k, keep=keep)
+        return [[Hit(int(i), float(s)) for i, s in zip(idx[m], sc[m]) if i >= 0] for m in range(idx.shape[0])]
 
     def max_k(self) -> int:
         v = C.c_int32(0)
@@ -189,9 +210,15 @@ class I8Index:
         return v.value
 
     # -- device-resident forms ------------------------------------------
-    def topk_async(self, d_q: int, M: int, k: int, d_keys: int, stream: int = 0) -> None:
-        check(lib().fi8_topk_batch_async(self._h, C.c_void_p(d_q), M, k, C.c_void_p(d_keys),
-                                         C.c_void_p(stream or None)))
+    def topk_async(self, d_q: int, M: int, k: int, d_keys: int, stream: int = 0, d_keep: int = 0,
+                   keep_nbits: int = 0) -> None:
+        """Device-resident top-k; d_keep: optional device keep bitmap."""
+        if d_keep:
+            check(lib().fi8_topk_batch_async_keep(self._h, C.c_void_p(d_q), M, k, C.c_void_p(d_keep), keep_nbits,
+                                                  C.c_void_p(d_keys), C.c_void_p(stream or None)))
+        else:
+            check(lib().fi8_topk_batch_async(self._h, C.c_void_p(d_q), M, k, C.c_void_p(d_keys),
+                                             C.c_void_p(stream or None)))
 
     def topk1_noalloc(self, d_q: int, k: int, d_keys: int, stream: int = 0) -> None:
         """fi8_topk1_noalloc: one query's top-k with the library's fixed scratch
@@ -274,26 +301,37 @@ class BinaryI8Index:
         """FlatBinaryI8.Query (flat_binary_i8.go:78) for one query."""
         return self.QueryBatch([q], k)[0]
 
-    def QueryBatch(self, queries, k: int) -> list[list[Hit]]:
-        idx, sc = self.topk_arrays(queries, k)
+    def QueryFilter(self, q, k: int, keep) -> list[Hit]:
+        """FlatBinaryI8.QueryFilter (flat_binary_i8.go:83): keep[id] (boolean
+        array over global ids) applies in the prefilter."""
+        return self.QueryBatch([q], k, keep=keep)[0]
+
+    def QueryBatch(self, queries, k: int, keep=None) -> list[list[Hit]]:
+        idx, sc = self.topk_arrays(queries, k, keep=keep)
         return [[Hit(int(i), float(s)) for i, s in zip(idx[m], sc[m]) if i >= 0] for m in range(idx.shape[0])]
 
-    def topk_arrays(self, queries, k: int):
+    def topk_arrays(self, queries, k: int, keep=None):
         Q = _f32(np.asarray(queries, dtype=np.float32).reshape(-1, self.dim))
         M = Q.shape[0]
         idx = np.empty((M, max(k, 0)), np.int32)
         sc = np.empty((M, max(k, 0)), np.float32)
         if M == 0:
             return idx, sc
-        check(lib().fi8_bin_query_topk(self._h, _p(Q), M, k, _p(idx), _p(sc)))
+        if keep is None:
+            check(lib().fi8_bin_query_topk(self._h, _p(Q), M, k, _p(idx), _p(sc)))
+        else:
+            bm = keep_bitmap(keep)
+            check(lib().fi8_bin_query_topk_keep(self._h, _p(Q), M, k, _p(bm), len(keep), _p(idx), _p(sc)))
         return idx, sc
 
     def prefilter_async(self, d_q: int, M: int, cand: int, d_keys: int, stream: int = 0,
-                        sorted_keys: bool = True) -> None:
+                        sorted_keys: bool = True, d_keep: int = 0, keep_nbits: int = 0) -> None:
         """The shortlist keys (-distance, global id) into d_keys [M][cand];
-        sorted_keys=False skips the sort (fine for the rerank, not a merge)."""
-        check(lib().fi8_bin_prefilter_async(self._h, C.c_void_p(d_q), M, cand, C.c_void_p(d_keys),
-                                            1 if sorted_keys else 0, C.c_void_p(stream or None)))
+        sorted_keys=False skips the sort (fine for the rerank, not a merge);
+        d_keep: optional device keep bitmap over global ids."""
+        check(lib().fi8_bin_prefilter_async_keep(self._h, C.c_void_p(d_q), M, cand, C.c_void_p(d_keep or None),
+                                                 keep_nbits, C.c_void_p(d_keys), 1 if sorted_keys else 0,
+                                                 C.c_void_p(stream or None)))
 
     def rerank_async(self, d_q: int, M: int, d_short: int, cand: int, k: int, d_keys: int,
                      stream: int = 0) -> None:

@@ -165,6 +165,12 @@ struct fi8_index {
   int32_t gemm_min_batch = 2;  // batches of at least this many queries use the GEMM path
   int32_t last_launches = 0;   // kernels launched by the last query call
 
+  // keep filter of the call in progress (QueryFilter), null when none
+  const uint64_t* cur_keep = nullptr;
+  int64_t cur_keep_nbits = 0;
+  uint64_t* d_keep = nullptr;  // device copy of a host bitmap
+  size_t keep_cap = 0;
+
   // optional per-launch timing (FI8_OPT_KERNEL_TIMING)
   struct TimedLaunch {
     int kind;
@@ -276,6 +282,7 @@ static void index_free(fi8_index* x) {
   cudaFree(x->d_cnt);
   cudaFree(x->d_cand);
   cudaFree(x->d_topk);
+  cudaFree(x->d_keep);
   if (x->h_keys) cudaFreeHost(x->h_keys);
   if (x->h_err) cudaFreeHost(x->h_err);
   for (auto& t : x->timed) {
@@ -404,6 +411,8 @@ static ScanParams base_params(fi8_index* x, const ScanGeometry& geo) {
   p.id_base = x->id_base;
   p.smem_bytes = (int32_t)geo.smem_bytes;
   p.err = x->d_err;
+  p.keep = x->cur_keep;
+  p.keep_nbits = x->cur_keep_nbits;
   return p;
 }
 
@@ -518,6 +527,8 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
   p.cand = x->d_cand;
   p.cap = cap;
   p.err = x->d_err;
+  p.keep = x->cur_keep;
+  p.keep_nbits = x->cur_keep_nbits;
   for (size_t i = 0; i < ranges.size(); i++) {
     p.row_lo = ranges[i].row_lo;
     p.row_hi = ranges[i].row_hi;
@@ -607,6 +618,34 @@ int fi8_score(fi8_index* idx, const float* q, float* dst) { return fi8_score_bat
 
 }  // extern "C"
 
+// The keep filter of one call: set on entry, cleared on every exit path.
+struct KeepScope {
+  fi8_index* x;
+  KeepScope(fi8_index* ix, const uint64_t* keep, int64_t nbits) : x(ix) {
+    x->cur_keep = keep;
+    x->cur_keep_nbits = keep ? nbits : 0;
+  }
+  ~KeepScope() {
+    x->cur_keep = nullptr;
+    x->cur_keep_nbits = 0;
+  }
+};
+
+// Copy a host keep bitmap (nbits bits over global ids) to the index's device
+// buffer on its stream; returns the device pointer through *out.
+static int stage_keep(fi8_index* x, const uint64_t* keep, int64_t nbits, const uint64_t** out) {
+  *out = nullptr;
+  if (!keep) return FI8_OK;
+  if (nbits < 0) return fail(FI8_ERR_ARG, "fi8: keep bitmap with negative length");
+  const size_t words = (size_t)((nbits + 63) / 64);
+  int rc;
+  if ((rc = ensure_device(&x->d_keep, &x->keep_cap, words, "keep bitmap")) != FI8_OK) return rc;
+  if (words)
+    FI8_CUDA(cudaMemcpyAsync(x->d_keep, keep, words * 8, cudaMemcpyHostToDevice, x->stream), "H2D keep");
+  *out = x->d_keep;
+  return FI8_OK;
+}
+
 // Top-k of the M queries staged in x->d_q into x->h_keys (M*k keys), with the
 // batched path's overflow fallback. Caller holds x->mu and the device.
 static int topk_staged(fi8_index* x, int32_t M, int32_t k) {
@@ -639,7 +678,8 @@ static int topk_staged(fi8_index* x, int32_t M, int32_t k) {
 
 extern "C" {
 
-int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score) {
+int fi8_topk_batch_keep(fi8_index* idx, const float* q, int32_t M, int32_t k, const uint64_t* keep, int64_t nbits,
+                        int32_t* out_idx, float* out_score) {
   if (!idx) return fail(FI8_ERR_ARG, "fi8_topk_batch: null index");
   if (M == 0) return FI8_OK;
   if (M < 0 || !q || !out_idx || !out_score) return fail(FI8_ERR_ARG, "fi8_topk_batch: bad arguments");
@@ -649,6 +689,9 @@ int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t
   DeviceGuard g(idx->device);
   fi8_index* x = idx;
   int rc;
+  const uint64_t* d_keep = nullptr;
+  if ((rc = stage_keep(x, keep, nbits, &d_keep)) != FI8_OK) return rc;
+  KeepScope ks(x, d_keep, nbits);
   if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
   FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
            "H2D queries");
@@ -656,17 +699,27 @@ int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t
   return fi8_keys_unpack(x->h_keys, (int64_t)M * k, out_idx, out_score);
 }
 
-int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
-                         void* stream) {
+int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score) {
+  return fi8_topk_batch_keep(idx, q, M, k, nullptr, 0, out_idx, out_score);
+}
+
+int fi8_topk_batch_async_keep(fi8_index* idx, const float* d_q, int32_t M, int32_t k, const uint64_t* d_keep,
+                              int64_t nbits, uint64_t* d_keys, void* stream) {
   if (!idx) return fail(FI8_ERR_ARG, "fi8_topk_batch_async: null index");
   if (M == 0) return FI8_OK;
-  if (M < 0 || !d_q || !d_keys) return fail(FI8_ERR_ARG, "fi8_topk_batch_async: bad arguments");
+  if (M < 0 || !d_q || !d_keys || nbits < 0) return fail(FI8_ERR_ARG, "fi8_topk_batch_async: bad arguments");
   // k >= n is allowed here: a row shard smaller than k contributes all of its
   // rows (sorted, then empty slots) to the cross-shard merge.
   if (k <= 0) return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d)", k);
   std::lock_guard<std::mutex> lk(idx->mu);
   DeviceGuard g(idx->device);
+  KeepScope ks(idx, d_keep, nbits);
   return launch_topk(idx, d_q, M, k, d_keys, static_cast<cudaStream_t>(stream));
+}
+
+int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                         void* stream) {
+  return fi8_topk_batch_async_keep(idx, d_q, M, k, nullptr, 0, d_keys, stream);
 }
 
 int fi8_index_set_option(fi8_index* idx, int option, int64_t value) {
@@ -1019,6 +1072,11 @@ int fi8_bin_index_handle(fi8_bin* b, fi8_index** out) {
 }
 
 int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score) {
+  return fi8_bin_query_topk_keep(b, q, M, k, nullptr, 0, out_idx, out_score);
+}
+
+int fi8_bin_query_topk_keep(fi8_bin* b, const float* q, int32_t M, int32_t k, const uint64_t* keep, int64_t nbits,
+                            int32_t* out_idx, float* out_score) {
   if (!b) return fail(FI8_ERR_ARG, "fi8_bin_query_topk: null index");
   if (M == 0) return FI8_OK;
   if (M < 0 || !q || !out_idx || !out_score) return fail(FI8_ERR_ARG, "fi8_bin_query_topk: bad arguments");
@@ -1031,6 +1089,9 @@ int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t
   std::lock_guard<std::mutex> lk(x->mu);
   DeviceGuard g(x->device);
   int rc;
+  const uint64_t* d_keep = nullptr;
+  if ((rc = stage_keep(x, keep, nbits, &d_keep)) != FI8_OK) return rc;
+  KeepScope ks(x, d_keep, nbits);
   if ((rc = ensure_device(&x->d_q, &x->d_q_cap, (size_t)M * x->dim, "staging q")) != FI8_OK) return rc;
   FI8_CUDA(cudaMemcpyAsync(x->d_q, q, (size_t)M * x->dim * sizeof(float), cudaMemcpyHostToDevice, x->stream),
            "H2D queries");
@@ -1059,16 +1120,22 @@ int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t
   return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
 }
 
-int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys, int32_t sorted,
-                            void* stream) {
+int fi8_bin_prefilter_async_keep(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, const uint64_t* d_keep,
+                                 int64_t nbits, uint64_t* d_keys, int32_t sorted, void* stream) {
   if (!b) return fail(FI8_ERR_ARG, "fi8_bin_prefilter_async: null index");
   if (M == 0) return FI8_OK;
-  if (M < 0 || !d_q || !d_keys) return fail(FI8_ERR_ARG, "fi8_bin_prefilter_async: bad arguments");
+  if (M < 0 || !d_q || !d_keys || nbits < 0) return fail(FI8_ERR_ARG, "fi8_bin_prefilter_async: bad arguments");
   if (cand <= 0) return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d)", cand);
   std::lock_guard<std::mutex> lk(b->ix->mu);
   DeviceGuard g(b->ix->device);
+  KeepScope ks(b->ix, d_keep, nbits);
   b->ix->last_launches = 0;
   return launch_bin_prefilter(b, d_q, M, cand, d_keys, sorted != 0, static_cast<cudaStream_t>(stream));
+}
+
+int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys, int32_t sorted,
+                            void* stream) {
+  return fi8_bin_prefilter_async_keep(b, d_q, M, cand, nullptr, 0, d_keys, sorted, stream);
 }
 
 int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,

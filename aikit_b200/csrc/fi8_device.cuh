@@ -107,6 +107,27 @@ __device__ __forceinline__ float w8a8_score(int32_t dot, float qscale, float row
 }
 
 // ---------------------------------------------------------------------------
+// Keep filters (QueryFilter's keep(id), ann/flat_i8.go:136): a bitmap over
+// global row ids, bit id%64 of word id/64; ids at or past nbits are not kept.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool keep_bit(const uint64_t* keep, int64_t nbits, uint64_t id) {
+  return (int64_t)id < nbits && ((__ldg(keep + (id >> 6)) >> (id & 63)) & 1ull);
+}
+
+// The 32 keep bits of ids [start, start + 32), bit i for id start + i.
+__device__ __forceinline__ uint32_t keep_bits32(const uint64_t* keep, int64_t nbits, uint64_t start) {
+  if ((int64_t)start >= nbits) return 0u;
+  const uint64_t w = start >> 6;
+  const uint32_t sh = (uint32_t)(start & 63);
+  uint64_t lo = __ldg(keep + w) >> sh;
+  if (sh > 32 && (int64_t)((w + 1) << 6) < nbits) lo |= __ldg(keep + w + 1) << (64 - sh);
+  uint32_t bits = (uint32_t)lo;
+  const int64_t valid = nbits - (int64_t)start;
+  if (valid < 32) bits &= (1u << valid) - 1u;
+  return bits;
+}
+
+// ---------------------------------------------------------------------------
 // Programmatic dependent launch (PDL). A kernel launched with
 // launch_pdl may be scheduled before the previous kernel in its stream has
 // finished: pdl_launch_dependents lets the next kernel be scheduled, and

@@ -334,6 +334,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int i = 0; i < 32; i++) v[i] = 0u;
         }
         if (col0 + 32 > lim) mask &= (col0 >= lim) ? 0u : ((1u << (uint32_t)(lim - col0)) - 1u);
+        if (p.keep && mask) mask &= keep_bits32(p.keep, p.keep_nbits, (uint64_t)p.id_base + row0 + col0);
         if (mask) {
           // Survivors go to this thread's few shared staging slots while they
           // fit; otherwise one reservation in the query's global list takes

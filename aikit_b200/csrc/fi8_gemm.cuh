@@ -33,6 +33,8 @@ struct GemmParams {
   int32_t cap;
   unsigned int* err;
   int32_t producer_waits;  // 1: the producer waits for the previous kernel (it wrote A)
+  const uint64_t* keep;    // optional keep bitmap over global ids
+  int64_t keep_nbits;
 };
 
 // Build a 2-D SWIZZLE_128B tensor map over an int8 matrix [rows][pitch]

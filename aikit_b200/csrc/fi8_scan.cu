@@ -261,20 +261,22 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
         const int r = base + (lane8 >> (3 - LOGR));
         const int64_t gr = row0 + r;
         const bool mine = owner && (gr < p.n);
+        const bool kept = mine && (!p.keep || keep_bit(p.keep, p.keep_nbits, p.id_base + (uint64_t)gr));
         float score = 0.0f;
         if (mine) score = BIN ? (float)(-vals[0]) : w8a8_score(vals[0], qscale, sc_s[r]);
         if (TOPK) {
           uint64_t key = kEmptyKey;
           bool take = false;
-          if (mine && score == score) {
+          if (kept && score == score) {
             key = make_key(score, p.id_base + (uint32_t)gr);
             take = key > thr;
           }
           warp_append(take, key, buf, &s_count[g]);
         } else if (mine) {
           if (BIN) {
-            p.out_dist[(size_t)y * p.dist_stride + gr] = (uint16_t)vals[0];
-            atomicAdd(reinterpret_cast<unsigned int*>(bufs) + vals[0], 1u);
+            // a filtered-out row gets a distance above every cut and no count
+            p.out_dist[(size_t)y * p.dist_stride + gr] = kept ? (uint16_t)vals[0] : (uint16_t)0xFFFFu;
+            if (kept) atomicAdd(reinterpret_cast<unsigned int*>(bufs) + vals[0], 1u);
           } else {
             p.out_scores[(size_t)y * p.n + gr] = score;
           }

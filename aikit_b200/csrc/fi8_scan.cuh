@@ -20,6 +20,8 @@ struct ScanParams {
   int64_t ntiles;        // n_alloc / R
   const float* q;        // [M][d] f32 queries
   uint32_t id_base;      // global id of row 0 (row sharding)
+  const uint64_t* keep;  // optional keep bitmap over global ids (top-K and binary modes)
+  int64_t keep_nbits;
   int32_t smem_bytes;    // dynamic shared memory of the launch
   // top-K mode
   int32_t k;

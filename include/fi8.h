@@ -80,6 +80,16 @@ int fi8_score_batch(fi8_index* idx, const float* q, int32_t M, float* dst);
 int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx,
                    float* out_score);
 
+/* FlatI8.QueryFilter (ann/flat_i8.go:136) for a batch: fi8_topk_batch over
+ * the rows whose keep bit is set. keep is a host bitmap over GLOBAL row ids
+ * (bit id%64 of word id/64; ids at or past nbits are not kept), shared by the
+ * M queries, in place of the reference's keep(id) callback. The reference
+ * runs filtered queries on the CPU (flat_i8.go:176-198 only offers the
+ * device the unfiltered case); this is additive. Same declines as
+ * fi8_topk_batch; fewer than k kept rows pad with index -1. */
+int fi8_topk_batch_keep(fi8_index* idx, const float* q, int32_t M, int32_t k, const uint64_t* keep,
+                        int64_t nbits, int32_t* out_idx, float* out_score);
+
 /* Largest k the device top-K answers for this index. */
 int fi8_topk_max_k(fi8_index* idx, int32_t* out);
 
@@ -94,6 +104,10 @@ int fi8_topk_max_k(fi8_index* idx, int32_t* out);
  * share the index's scratch); issue them on one stream. */
 int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
                          void* stream);
+/* fi8_topk_batch_async restricted by a device keep bitmap d_keep (as
+ * fi8_topk_batch_keep; NULL = every row). */
+int fi8_topk_batch_async_keep(fi8_index* idx, const float* d_q, int32_t M, int32_t k, const uint64_t* d_keep,
+                              int64_t nbits, uint64_t* d_keys, void* stream);
 
 /* Tuning knobs of an index. FI8_OPT_GEMM_MIN_BATCH: batches of at least this
  * many queries take the tcgen05 GEMM path, smaller ones the per-query scan
@@ -184,6 +198,13 @@ int fi8_bin_index_handle(fi8_bin* b, fi8_index** out);
  * returns the whole corpus there), and cand above the device limit (2048). */
 int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score);
 
+/* FlatBinaryI8.QueryFilter (flat_binary_i8.go:83): the keep filter applies in
+ * the prefilter, as prefilterHeap does (prefilter.go:227-313): the shortlist
+ * is the cand nearest KEPT rows under (distance, id). keep as for
+ * fi8_topk_batch_keep. */
+int fi8_bin_query_topk_keep(fi8_bin* b, const float* q, int32_t M, int32_t k, const uint64_t* keep, int64_t nbits,
+                            int32_t* out_idx, float* out_score);
+
 /* Device-resident halves, for sharded use: every rank prefilters its shard,
  * the M x cand keys are all-gathered and merged (fi8_merge_keys_async) into the
  * global shortlist -- the global cand nearest by (distance, id), as the
@@ -199,6 +220,9 @@ int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t can
                             void* stream);
 int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,
                          uint64_t* d_keys, void* stream);
+/* fi8_bin_prefilter_async over the rows of a device keep bitmap (NULL = all). */
+int fi8_bin_prefilter_async_keep(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, const uint64_t* d_keep,
+                                 int64_t nbits, uint64_t* d_keys, int32_t sorted, void* stream);
 
 #ifdef __cplusplus
 }
