@@ -41,6 +41,7 @@ SIGNATURES = {
     "fi8_index_set_option": (C.c_int, [_P, C.c_int, _I64]),
     "fi8_index_last_launch_count": (C.c_int, [_P, _P]),
     "fi8_index_kernel_times": (C.c_int, [_P, _P, _P, _P, C.c_int]),
+    "fi8_index_kernel_log": (C.c_int, [_P, _I32, _P, _P, _P, _P]),
     "fi8_index_sync": (C.c_int, [_P]),
     "fi8_keys_unpack": (C.c_int, [_P, _I64, _P, _P]),
     "fi8_merge_keys_async": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P]),

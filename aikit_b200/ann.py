@@ -251,6 +251,16 @@ class I8Index:
         return {name: {"launches": int(launches[i]), "ms": float(ms[i]), "bytes": float(nbytes[i])}
                 for i, name in enumerate(KERNEL_KINDS) if launches[i]}
 
+    def kernel_log(self, cap: int = 4096) -> list:
+        """The timed launches in order: (kernel class, device ms, algorithmic bytes)."""
+        from ._ffi import KERNEL_KINDS
+        n = C.c_int32(0)
+        kinds = (C.c_int32 * cap)()
+        ms = (C.c_double * cap)()
+        nbytes = (C.c_double * cap)()
+        check(lib().fi8_index_kernel_log(self._h, cap, C.byref(n), kinds, ms, nbytes))
+        return [(KERNEL_KINDS[kinds[i]], ms[i], nbytes[i]) for i in range(n.value)]
+
     def set_gemm_min_batch(self, m: int) -> None:
         """Batches of at least m queries use the tensor-core GEMM path."""
         from ._ffi import FI8_OPT_GEMM_MIN_BATCH

@@ -468,11 +468,16 @@ static int32_t pow2_ge_host(int64_t x) {
   return p;
 }
 
-// Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles.
+// Row ranges [0,s1), [s1, s1*F1), ... rounded to 256-row tiles. A range
+// admits about k*F candidates per query. Every range costs a GEMM launch and a
+// select, so the growth factor starts at 16 (the first ranges are short and
+// latency-bound, and their candidates are dense per tile) and rises to 64
+// once ranges are long enough (from 16K rows) that the extra candidates
+// spread thinly over many tiles, within a quarter of the per-query buffer.
 static void plan_ranges(int64_t n, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
-  // Growth factor: a range admits ~k*F candidates per query; 16 keeps each
-  // select small while the number of ranges stays logarithmic.
-  const int64_t F = std::min<int64_t>(16, std::max<int64_t>(4, cap / (4 * (int64_t)k)));
+  const int64_t room = std::max<int64_t>(4, cap / (4 * (int64_t)k));
+  const int64_t F1 = std::min<int64_t>(16, room);
+  const int64_t F2 = std::min<int64_t>(64, room);
   int64_t hi = std::max<int64_t>(k, 1024);
   hi = (hi + kGemmBN - 1) / kGemmBN * kGemmBN;
   int64_t lo = 0;
@@ -480,6 +485,7 @@ static void plan_ranges(int64_t n, int32_t k, int32_t cap, std::vector<GemmLevel
     const int64_t h = std::min<int64_t>(n, hi);
     out->push_back(GemmLevel{lo, h});
     lo = h;
+    const int64_t F = lo >= 16 * 1024 ? F2 : F1;
     hi = (lo * F + kGemmBN - 1) / kGemmBN * kGemmBN;
   }
 }
@@ -770,6 +776,26 @@ int fi8_index_kernel_times(fi8_index* idx, int64_t* launches, double* ms, double
     }
     idx->timed.clear();
   }
+  return FI8_OK;
+}
+
+int fi8_index_kernel_log(fi8_index* idx, int32_t cap, int32_t* count, int32_t* kinds, double* ms, double* bytes) {
+  if (!idx || !count || (cap > 0 && (!kinds || !ms || !bytes)))
+    return fail(FI8_ERR_ARG, "fi8_index_kernel_log: null argument");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  int32_t c = 0;
+  for (const auto& t : idx->timed) {
+    if (c >= cap) break;
+    FI8_CUDA(cudaEventSynchronize(t.e1), "fi8_index_kernel_log: event sync");
+    float dt = 0.0f;
+    FI8_CUDA(cudaEventElapsedTime(&dt, t.e0, t.e1), "fi8_index_kernel_log: elapsed time");
+    kinds[c] = t.kind;
+    ms[c] = dt;
+    bytes[c] = t.bytes;
+    c++;
+  }
+  *count = c;
   return FI8_OK;
 }
 

@@ -677,11 +677,13 @@ cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsi
                           cudaStream_t stream) {
   // buffer: the carried list plus room for a few thousand candidates between
   // compactions (a compaction is a bitonic sort of the buffer)
-  int cap_s = pow2_ge(kp + kSelThreads);
-  if (cap_s < 4096) cap_s = 4096;
-  if (cap_s > 8192 || kp > 4096) return cudaErrorInvalidValue;
+  // union buffer: room for the carried list plus a range's candidates (about
+  // k * F of them) in one piece, so the radix select runs in shared memory;
+  // a larger union takes the streaming form
+  const int cap_s = 16384;
+  if (kp > 4096) return cudaErrorInvalidValue;
   const size_t smem = (size_t)(cap_s + kp) * 8;  // union buffer + kept list
-  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (8192 + 4096) * 8);
+  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (16384 + 4096) * 8);
   if (e != cudaSuccess) return e;
   return launch_pdl(select_kernel, dim3((unsigned)M), dim3(kSelThreads), smem, stream, k, kp, cap_s, topk, thr, cnt,
                     cand, cap, out, err);

@@ -44,7 +44,9 @@ def main() -> None:
     torch.cuda.set_stream(stream)
     times = []
     prof = None
-    if a.trace:
+    if a.trace and a.mode == "topk":  # per-launch device times from the library's events
+        ix.set_kernel_timing(True)
+    if a.trace and a.mode != "topk":
         from torch.profiler import ProfilerActivity, profile
         prof = profile(activities=[ProfilerActivity.CUDA])
         prof.__enter__()
@@ -62,6 +64,16 @@ def main() -> None:
         times.append(e0.elapsed_time(e1))
     ix.sync()
     kernels = None
+    launch_log = None
+    if a.trace and a.mode == "topk":
+        log = ix.kernel_log()
+        per = len(log) // max(a.reps, 1)
+        launch_log = [(name, round(ms * 1e3, 1)) for name, ms, _ in log[-per:]]  # the last call
+        kernels = {}
+        for name, ms, _ in log[per:]:  # all but the first (cold) call
+            t = kernels.setdefault(name, {"calls_per_rep": 0.0, "us_per_rep": 0.0})
+            t["calls_per_rep"] += 1.0 / max(a.reps - 1, 1)
+            t["us_per_rep"] += ms * 1e3 / max(a.reps - 1, 1)
     if prof is not None:
         prof.__exit__(None, None, None)
         agg = {}
@@ -78,6 +90,8 @@ def main() -> None:
     out = {"rows": a.rows, "dim": a.dim, "k": a.k, "batch": a.batch, "ms": times, "gbs_per_pass": gbs}
     if kernels is not None:
         out["kernels"] = kernels
+    if launch_log is not None:
+        out["last_call_launches_us"] = launch_log
     print(json.dumps(out))
 
 

@@ -136,6 +136,11 @@ int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
  * then clears the totals. */
 int fi8_index_kernel_times(fi8_index* idx, int64_t* launches, double* ms, double* bytes, int reset);
 
+/* The timed launches themselves, in launch order (up to cap of them, *count
+ * set): kernel class, device ms and algorithmic bytes of each. Does not reset;
+ * read it before fi8_index_kernel_times(..., reset = 1). */
+int fi8_index_kernel_log(fi8_index* idx, int32_t cap, int32_t* count, int32_t* kinds, double* ms, double* bytes);
+
 /* Number of kernels the index's last query call launched (scan: one per 64
  * queries; batched: quantize + a GEMM and a select per row range). */
 int fi8_index_last_launch_count(fi8_index* idx, int32_t* out);
