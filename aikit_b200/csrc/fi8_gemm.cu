@@ -605,9 +605,23 @@ __global__ void __launch_bounds__(kSelThreads, 1)
     nkept = s_count;
     sorted = false;
     if (out) {
-      for (int i = nkept + tid; i < kp; i += kSelThreads) sel[i] = kEmptyKey;
-      named_sync(bar, kSelThreads);
-      group_sort_desc<kSelThreads>(sel, kp, tid, bar);
+      if (nkept <= kSelThreads) {
+        // rank placement: each kept key's position is the number of kept keys
+        // above it (keys are distinct); one pass, no sorting network
+        uint64_t* ranked = buf;  // the union buffer is free now
+        if (tid < nkept) {
+          const uint64_t key = sel[tid];
+          int rank = 0;
+          for (int j = 0; j < nkept; j++) rank += sel[j] > key;
+          ranked[rank] = key;
+        }
+        named_sync(bar, kSelThreads);
+        kept = ranked;
+      } else {
+        for (int i = nkept + tid; i < kp; i += kSelThreads) sel[i] = kEmptyKey;
+        named_sync(bar, kSelThreads);
+        group_sort_desc<kSelThreads>(sel, kp, tid, bar);
+      }
       sorted = true;
     }
   }
