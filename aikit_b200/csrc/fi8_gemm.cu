@@ -286,7 +286,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         q = qt * kGemmBM + j;
         qs = valid_q ? p.qscale[qt * kGemmBM + r] : 0.0f;
         T = valid_q ? p.thr[q] : ~0ull;
-        Tscore = !valid_q ? INFINITY : (T == 0ull) ? -INFINITY : key_score(T);
+        // T is the k-th best key of rows below this range, and every row of
+        // this range has a larger index, so a row scoring exactly T's score
+        // loses the (score desc, index asc) comparison: only scores strictly
+        // above pass, i.e. scores >= the next float up. With no threshold
+        // yet (T == 0) every non-NaN score passes, -inf included.
+        Tscore = !valid_q ? INFINITY : (T == 0ull) ? -INFINITY : nextafterf(key_score(T), INFINITY);
       }
       if (s_abort) break;
       // this unit's scales (copied during the previous unit) have landed;
@@ -339,7 +344,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // Survivors go to this thread's few shared staging slots while they
           // fit; otherwise one reservation in the query's global list takes
           // the staged keys and this chunk's. A survivor whose key does not
-          // beat the threshold (a score tie at Tscore with a higher index)
+          // beat the threshold (possible only at T's score when T is +inf)
           // leaves an empty key, which the select skips.
           const int nm = __popc(mask);
           uint64_t* dst;
@@ -440,196 +445,161 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* q, int M, in
   for (int i = tid; i < kp; i += blockDim.x) topk[(size_t)qi * kp + i] = kEmptyKey;
 }
 
-// One CTA of 1024 threads per query: fold this range's candidates into the
-// running top-k. The carried list holds keys of earlier ranges (all >= the
+// One CTA of 512 threads per query: fold this range's candidates into the
+// running top-k. The carried list holds keys of earlier ranges (all above the
 // threshold the candidates passed), so top-k of the union is exact.
-constexpr int kSelThreads = 1024;
+//
+// An MSD radix select (8-bit digits, most significant first) over the union,
+// read from global memory (L2) on every pass, finds the digit prefix that
+// exactly the k best keys match or exceed: keys are distinct, so the walk ends
+// at a digit bucket whose whole count is still needed. One more pass keeps
+// those keys. Shared memory holds only the histogram and the kept list, so
+// many queries' CTAs share an SM and a large batch selects in one wave. Only
+// the last range's select orders its keys (its output is the answer).
+constexpr int kSelThreads = 512;
+constexpr int kSelUnroll = 4;
 constexpr int kRadixBins = 256;
 
-// Streaming form, for a union larger than the shared buffer: append, and sort
-// and cut the buffer to the best k whenever it nears full. Leaves the kept
-// keys sorted in buf[0..*s_count).
-__device__ void select_stream(int k, int cap_s, const uint64_t* mine, int kp, const uint64_t* src, int n_c,
-                              uint64_t* buf, int* s_count, unsigned long long* s_local_thr, int tid, int bar) {
-  for (int i0 = 0; i0 < kp; i0 += kSelThreads) {
-    const int i = i0 + tid;
-    const uint64_t key = i < kp ? mine[i] : kEmptyKey;
-    warp_append(key != kEmptyKey, key, buf, s_count);
-  }
-  named_sync(bar, kSelThreads);
-  if (*s_count > cap_s - kSelThreads)
-    group_compact<kSelThreads>(buf, *s_count, k, s_count, s_local_thr, nullptr, tid, bar);
-  for (int b0 = 0; b0 < n_c; b0 += kSelThreads) {
-    const int e = b0 + tid;
-    uint64_t key = kEmptyKey;
-    bool take = false;
-    if (e < n_c) {
-      key = src[e];
-      take = key > *s_local_thr;
-    }
-    warp_append(take, key, buf, s_count);
-    named_sync(bar, kSelThreads);
-    const int cnow = *s_count;
-    if (cnow > cap_s - kSelThreads)
-      group_compact<kSelThreads>(buf, cnow, k, s_count, s_local_thr, nullptr, tid, bar);
-  }
-  named_sync(bar, kSelThreads);
-  group_compact<kSelThreads>(buf, *s_count, k, s_count, s_local_thr, nullptr, tid, bar);
+// Slot i of a query's union: its carried list, then this range's candidates.
+__device__ __forceinline__ uint64_t union_key(const uint64_t* mine, int kp, const uint64_t* src, int n_all, int i) {
+  if (i >= n_all) return kEmptyKey;
+  return i < kp ? __ldcg(mine + i) : __ldcg(src + (i - kp));
 }
 
-// Usual form: the union fits in shared memory. An MSD radix select (8-bit
-// digits, most significant first) finds the digit prefix that exactly the k
-// best keys match or exceed -- keys are distinct, so the walk ends at a digit
-// bucket whose whole count is still needed -- and one pass keeps those keys.
-// Only the last range's select sorts (its output is the answer).
-__global__ void __launch_bounds__(kSelThreads, 1)
-    select_kernel(int k, int kp, int cap_s, uint64_t* topk, unsigned long long* thr, unsigned int* cnt,
-                  const uint64_t* cand, int cap, uint64_t* out, unsigned int* err) {
+__global__ void __launch_bounds__(kSelThreads)
+    select_kernel(int k, int kp, uint64_t* topk, unsigned long long* thr, unsigned int* cnt, const uint64_t* cand,
+                  int cap, uint64_t* out, unsigned int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_count;
-  __shared__ unsigned long long s_local_thr, s_prefix, s_mask, s_min;
+  __shared__ unsigned long long s_prefix, s_mask, s_min;
   __shared__ unsigned int s_hist[kRadixBins];
+  __shared__ unsigned int s_total;
   __shared__ int s_rank, s_done;
-  uint64_t* buf = reinterpret_cast<uint64_t*>(smem);  // [cap_s] the union
-  uint64_t* sel = buf + cap_s;                         // [kp] the kept keys
+  uint64_t* sel = reinterpret_cast<uint64_t*>(smem);  // [kp] the kept keys
+  uint64_t* ranked = sel + kp;                          // [kp] their order (last range)
   const int qi = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  constexpr int bar = 1;
   pdl_launch_dependents();
   pdl_wait_prior();  // the range's GEMM has completed
-  if (tid == 0) {
-    s_count = 0;
-    s_local_thr = 0;
-  }
-  named_sync(bar, kSelThreads);
   uint64_t* mine = topk + (size_t)qi * kp;
   const unsigned int c_all = cnt[qi];
   if (c_all > (unsigned int)cap && tid == 0) atomicOr(err, 2u);  // candidates were dropped
   const int n_c = (int)(c_all < (unsigned int)cap ? c_all : (unsigned int)cap);
   const uint64_t* src = cand + (size_t)qi * cap;
-
-  const uint64_t* kept;  // the kept keys (<= kp of them) and how many
-  int nkept;
-  bool sorted;
-  if (kp + n_c > cap_s) {
-    select_stream(k, cap_s, mine, kp, src, n_c, buf, &s_count, &s_local_thr, tid, bar);
-    kept = buf;
-    nkept = s_count;
-    sorted = true;
-  } else {
-    for (int i0 = 0; i0 < kp; i0 += kSelThreads) {
-      const int i = i0 + tid;
-      const uint64_t key = i < kp ? mine[i] : kEmptyKey;
-      warp_append(key != kEmptyKey, key, buf, &s_count);
-    }
-    for (int b0 = 0; b0 < n_c; b0 += kSelThreads) {
-      const int e = b0 + tid;
-      const uint64_t key = e < n_c ? src[e] : kEmptyKey;
-      warp_append(key != kEmptyKey, key, buf, &s_count);
-    }
-    if (tid == 0) {
-      s_prefix = 0ull;
-      s_mask = 0ull;
-      s_min = ~0ull;
-      s_rank = k;
-      s_done = 0;
-    }
-    named_sync(bar, kSelThreads);
-    const int n = s_count;
-    if (n > k) {
-      for (int shift = 56; shift >= 0; shift -= 8) {
-        if (tid < kRadixBins) s_hist[tid] = 0u;
-        named_sync(bar, kSelThreads);
-        const unsigned long long prefix = s_prefix, mask = s_mask;
-        for (int i0 = 0; i0 < n; i0 += kSelThreads) {
-          const int i = i0 + tid;
-          const uint64_t key = i < n ? buf[i] : kEmptyKey;
-          const bool live = i < n && (key & mask) == prefix;
-          const unsigned int bin = live ? (unsigned int)(key >> shift) & 0xFFu : 0x100u;
-          const unsigned int same = __match_any_sync(0xffffffffu, bin);
-          if (live && lane == __ffs(same) - 1) atomicAdd(&s_hist[bin], (unsigned int)__popc(same));
-        }
-        named_sync(bar, kSelThreads);
-        if (tid < 32) {
-          // lane l holds bins 255-8l .. 248-8l (descending); find the bin
-          // where the running count from the top reaches the rank
-          unsigned int c[8], sum = 0;
+  const int n_all = kp + n_c;  // slots of the union; empty keys (0) are skipped
+  if (tid == 0) {
+    s_prefix = 0ull;
+    s_mask = 0ull;
+    s_min = ~0ull;
+    s_rank = k;
+    s_done = 0;
+    s_count = 0;
+    s_total = 0;
+  }
+  __syncthreads();
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    if (tid < kRadixBins) s_hist[tid] = 0u;
+    __syncthreads();
+    const unsigned long long prefix = s_prefix, mask = s_mask;
+    for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
+      uint64_t keys[kSelUnroll];  // loads first, so their L2 latencies overlap
 #pragma unroll
-          for (int j = 0; j < 8; j++) {
-            c[j] = s_hist[255 - 8 * lane - j];
-            sum += c[j];
-          }
-          unsigned int incl = sum;
+      for (int u = 0; u < kSelUnroll; u++) keys[u] = union_key(mine, kp, src, n_all, i0 + u * kSelThreads + tid);
 #pragma unroll
-          for (int off = 1; off < 32; off <<= 1) {
-            const unsigned int t = __shfl_up_sync(0xffffffffu, incl, off);
-            if (lane >= off) incl += t;
-          }
-          const unsigned int rank = (unsigned int)s_rank;
-          const unsigned int excl = incl - sum;
-          const unsigned int hit = __ballot_sync(0xffffffffu, excl < rank && rank <= incl);
-          if (lane == __ffs(hit) - 1) {
-            unsigned int cum = excl;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-              if (cum + c[j] >= rank) {
-                const unsigned int digit = 255u - 8u * lane - j;
-                s_prefix = prefix | ((unsigned long long)digit << shift);
-                s_mask = mask | (0xFFull << shift);
-                s_rank = (int)(rank - cum);
-                s_done = (c[j] == rank - cum) ? 1 : 0;
-                break;
-              }
-              cum += c[j];
-            }
-          }
-        }
-        named_sync(bar, kSelThreads);
-        if (s_done) break;
+      for (int u = 0; u < kSelUnroll; u++) {
+        const uint64_t key = keys[u];
+        const bool live = key != kEmptyKey && (key & mask) == prefix;
+        const unsigned int bin = live ? (unsigned int)(key >> shift) & 0xFFu : 0x100u;
+        const unsigned int same = __match_any_sync(0xffffffffu, bin);
+        if (live && lane == __ffs(same) - 1) atomicAdd(&s_hist[bin], (unsigned int)__popc(same));
       }
     }
-    // keep every key at or above the prefix (exactly min(n, k) of them)
-    if (tid == 0) s_count = 0;
-    named_sync(bar, kSelThreads);
-    const unsigned long long prefix = s_prefix, mask = s_mask;
-    for (int i0 = 0; i0 < n; i0 += kSelThreads) {
-      const int i = i0 + tid;
-      const uint64_t key = i < n ? buf[i] : kEmptyKey;
-      const bool take = i < n && (key & mask) >= prefix;
+    __syncthreads();
+    if (tid < 32) {
+      // lane l holds bins 255-8l .. 248-8l (descending); find the bin where
+      // the running count from the top reaches the rank
+      unsigned int c[8], sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        c[j] = s_hist[255 - 8 * lane - j];
+        sum += c[j];
+      }
+      unsigned int incl = sum;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const unsigned int t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+      }
+      const unsigned int total = __shfl_sync(0xffffffffu, incl, 31);
+      const unsigned int rank = (unsigned int)s_rank;
+      if (shift == 56 && lane == 0) s_total = total;
+      if (shift == 56 && total <= rank) {
+        if (lane == 0) s_done = 2;  // k or fewer keys in all: keep them all
+      } else {
+        const unsigned int excl = incl - sum;
+        const unsigned int hit = __ballot_sync(0xffffffffu, excl < rank && rank <= incl);
+        if (lane == __ffs(hit) - 1) {
+          unsigned int cum = excl;
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            if (cum + c[j] >= rank) {
+              const unsigned int digit = 255u - 8u * lane - j;
+              s_prefix = prefix | ((unsigned long long)digit << shift);
+              s_mask = mask | (0xFFull << shift);
+              s_rank = (int)(rank - cum);
+              s_done = (c[j] == rank - cum) ? 1 : 0;
+              break;
+            }
+            cum += c[j];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (s_done) break;
+  }
+  // keep every non-empty key at or above the prefix (exactly min(total, k))
+  const unsigned long long prefix = s_done == 2 ? 0ull : s_prefix;
+  const unsigned long long mask = s_done == 2 ? 0ull : s_mask;
+  for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
+    uint64_t keys[kSelUnroll];
+#pragma unroll
+    for (int u = 0; u < kSelUnroll; u++) keys[u] = union_key(mine, kp, src, n_all, i0 + u * kSelThreads + tid);
+#pragma unroll
+    for (int u = 0; u < kSelUnroll; u++) {
+      const uint64_t key = keys[u];
+      const bool take = key != kEmptyKey && (key & mask) >= prefix;
       if (take) atomicMin(&s_min, (unsigned long long)key);
       warp_append(take, key, sel, &s_count);
     }
-    named_sync(bar, kSelThreads);
-    kept = sel;
-    nkept = s_count;
-    sorted = false;
-    if (out) {
-      if (nkept <= kSelThreads) {
-        // rank placement: each kept key's position is the number of kept keys
-        // above it (keys are distinct); one pass, no sorting network
-        uint64_t* ranked = buf;  // the union buffer is free now
-        if (tid < nkept) {
-          const uint64_t key = sel[tid];
-          int rank = 0;
-          for (int j = 0; j < nkept; j++) rank += sel[j] > key;
-          ranked[rank] = key;
-        }
-        named_sync(bar, kSelThreads);
-        kept = ranked;
-      } else {
-        for (int i = nkept + tid; i < kp; i += kSelThreads) sel[i] = kEmptyKey;
-        named_sync(bar, kSelThreads);
-        group_sort_desc<kSelThreads>(sel, kp, tid, bar);
+  }
+  __syncthreads();
+  const int nkept = s_count;
+  const uint64_t* kept = sel;
+  if (out) {
+    if (nkept <= 512) {
+      // rank placement: a kept key's position is the number of kept keys
+      // above it (keys are distinct); a sorting network beyond that
+      for (int i = tid; i < nkept; i += kSelThreads) {
+        const uint64_t key = sel[i];
+        int rank = 0;
+        for (int j = 0; j < nkept; j++) rank += sel[j] > key;
+        ranked[rank] = key;
       }
-      sorted = true;
+    } else {
+      for (int i = tid; i < kp; i += kSelThreads) ranked[i] = i < nkept ? sel[i] : kEmptyKey;
+      named_sync(1, kSelThreads);
+      group_sort_desc<kSelThreads>(ranked, kp, tid, 1);
     }
+    __syncthreads();
+    kept = ranked;
   }
   for (int i = tid; i < kp; i += kSelThreads) mine[i] = i < nkept ? kept[i] : kEmptyKey;
   if (out)
     for (int i = tid; i < k; i += kSelThreads) out[(size_t)qi * k + i] = i < nkept ? kept[i] : kEmptyKey;
   if (tid == 0) {
-    thr[qi] = nkept >= k ? (sorted ? kept[k - 1] : s_min) : 0ull;
+    thr[qi] = nkept >= k ? s_min : 0ull;
     cnt[qi] = 0u;
   }
 }
@@ -689,18 +659,12 @@ cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, 
 cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsigned long long* thr,
                           unsigned int* cnt, const uint64_t* cand, int32_t cap, uint64_t* out, unsigned int* err,
                           cudaStream_t stream) {
-  // buffer: the carried list plus room for a few thousand candidates between
-  // compactions (a compaction is a bitonic sort of the buffer)
-  // union buffer: room for the carried list plus a range's candidates (about
-  // k * F of them) in one piece, so the radix select runs in shared memory;
-  // a larger union takes the streaming form
-  const int cap_s = 16384;
-  if (kp > 4096) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)(cap_s + kp) * 8;  // union buffer + kept list
-  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (16384 + 4096) * 8);
+  if (kp > 4096 || kp < k) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)2 * kp * 8;  // kept list + its order
+  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 4096 * 8);
   if (e != cudaSuccess) return e;
-  return launch_pdl(select_kernel, dim3((unsigned)M), dim3(kSelThreads), smem, stream, k, kp, cap_s, topk, thr, cnt,
-                    cand, cap, out, err);
+  return launch_pdl(select_kernel, dim3((unsigned)M), dim3(kSelThreads), smem, stream, k, kp, topk, thr, cnt, cand,
+                    cap, out, err);
 }
 
 }  // namespace fi8

@@ -23,6 +23,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--mode", choices=["topk", "score", "binary"], default="topk")
+    ap.add_argument("--recipe", choices=["mixture", "ties", "unit"], default="mixture",
+                    help="corpus: C2/C3 mixture, C5 ties (codes in {-2..2}, scale 1/127), or iid unit rows")
     ap.add_argument("--over", type=int, default=100, help="binary mode: overquery (cand = k * over)")
     ap.add_argument("--trace", action="store_true",
                     help="also report per-kernel device time (torch.profiler / CUPTI) over the reps")
@@ -35,7 +37,12 @@ def main() -> None:
     be = B200Backend(0)
     if a.mode == "binary":
         return binary_case(a, be)
-    r = synth.Recipe(synth.MIXTURE, a.dim, seed=20260, ncl=1000, sigma=0.3)
+    if a.recipe == "ties":
+        r = synth.Recipe(synth.TIES, a.dim, seed=20265)
+    elif a.recipe == "unit":
+        r = synth.Recipe(synth.UNIT, a.dim, seed=20261)
+    else:
+        r = synth.Recipe(synth.MIXTURE, a.dim, seed=20260, ncl=1000, sigma=0.3)
     bq, bs = r.codes(a.rows)
     ix = be.NewI8Index(bq, bs, a.rows, a.dim)
     Q = torch.from_numpy(r.queries(a.batch)).cuda()
