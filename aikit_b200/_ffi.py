@@ -53,6 +53,11 @@ SIGNATURES = {
     "fi8_bin_prefilter_async": (C.c_int, [_P, _P, _I32, _I32, _P, _I32, _P]),
     "fi8_bin_rerank_async": (C.c_int, [_P, _P, _I32, _P, _I32, _I32, _P, _P]),
     "fi8_topk_batch_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _P]),
+    "fi8_index_create_f32": (C.c_int, [_P, _P, _I64, _I32, _I64, _P]),
+    "fi8_index_read_rows": (C.c_int, [_P, _P, _P]),
+    "fi8_bin_index_create_f32": (C.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _P]),
+    "fi8_bin_center": (C.c_int, [_P, _P, _P]),
+    "fi8_bin_read_codes": (C.c_int, [_P, _P]),
     "fi8_topk_batch_async_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _P]),
     "fi8_bin_query_topk_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _P]),
     "fi8_bin_prefilter_async_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _I32, _P]),

@@ -111,6 +111,37 @@ class B200Backend:
                               f"{scales.shape[0]}, n={n} dim={dim})")
         return I8Index(self.ctx, bq, scales, n, dim, id_base)
 
+    def NewI8IndexFromFloats(self, vecs, id_base: int = 0) -> "I8Index":
+        """NewFlatI8 on the device (fi8_index_create_f32): vecs [n, dim] float32
+        rows, quantized on the GPU bit-identically to QuantizeRowInt8."""
+        v = _f32(vecs)
+        if v.ndim != 2 or v.shape[0] == 0 or v.shape[1] == 0:
+            raise Fi8Error(1, f"gpu: empty int8 index (shape {v.shape})")
+        h = C.c_void_p()
+        check(lib().fi8_index_create_f32(self.ctx.handle, _p(v), v.shape[0], v.shape[1], id_base, C.byref(h)))
+        return I8Index._adopt(self.ctx, h, v.shape[0], v.shape[1], id_base)
+
+    def NewBinaryI8IndexFromFloats(self, vecs, overquery: int = 16, centered: bool = True, center=None,
+                                   valid=None, id_base: int = 0) -> "BinaryI8Index":
+        """newFlatBinaryI8 on the device (fi8_bin_index_create_f32): the FlatI8
+        rows and the prefilter's centre and sign codes from [n, dim] float32
+        rows. valid: optional per-row flags (False = a ragged row, left out of
+        the centre with all-zero codes); center: optional given centre (a row
+        shard of a larger corpus)."""
+        v = _f32(vecs)
+        if v.ndim != 2 or v.shape[0] == 0 or v.shape[1] == 0:
+            raise Fi8Error(1, f"gpu: empty binary index (shape {v.shape})")
+        n, dim = v.shape
+        vd = None if valid is None else np.ascontiguousarray(valid, dtype=np.uint8).reshape(-1)
+        if vd is not None and vd.shape[0] != n:
+            raise Fi8Error(1, "gpu: valid flags length != n")
+        ctr = None if center is None else _f32(center).reshape(-1)
+        h = C.c_void_p()
+        check(lib().fi8_bin_index_create_f32(self.ctx.handle, _p(v), _p(vd) if vd is not None else None, n, dim,
+                                             overquery, 1 if centered else 0, _p(ctr) if ctr is not None else None,
+                                             id_base, C.byref(h)))
+        return BinaryI8Index._adopt(self.ctx, h, n, dim, (dim + 63) // 64, overquery, id_base)
+
     def NewBinaryI8Index(self, codes, words: int, center, bq, scales, n: int, dim: int,
                          overquery: int = 16, id_base: int = 0) -> "BinaryI8Index":
         """A device FlatBinaryI8 shard from the prefilter's packed codes
@@ -142,6 +173,19 @@ class I8Index:
         self.n = n
         self.dim = dim
         self.id_base = id_base
+
+    @classmethod
+    def _adopt(cls, ctx: Context, h, n: int, dim: int, id_base: int) -> "I8Index":
+        self = cls.__new__(cls)
+        self._h, self.ctx, self.n, self.dim, self.id_base = h, ctx, n, dim, id_base
+        return self
+
+    def read_rows(self):
+        """The index's int8 rows [n, dim] and scales [n], copied to the host."""
+        bq = np.empty((self.n, self.dim), np.int8)
+        sc = np.empty(self.n, np.float32)
+        check(lib().fi8_index_read_rows(self._h, _p(bq), _p(sc)))
+        return bq, sc
 
     # -- I8Index ---------------------------------------------------------
     def Score(self, q: Sequence[float], dst: np.ndarray) -> None:
@@ -306,6 +350,38 @@ class BinaryI8Index:
         self.words = words
         self.overquery = max(int(overquery), 1)
         self.id_base = id_base
+
+    @classmethod
+    def _adopt(cls, ctx: Context, h, n, dim, words, overquery, id_base) -> "BinaryI8Index":
+        self = cls.__new__(cls)
+        self._h = h
+        ih = C.c_void_p()
+        check(lib().fi8_bin_index_handle(h, C.byref(ih)))
+        self._ih = ih
+        self.ctx, self.n, self.dim, self.words = ctx, n, dim, words
+        self.overquery = max(int(overquery), 1)
+        self.id_base = id_base
+        return self
+
+    def center(self):
+        """The prefilter's centre (float32 [dim]), or None when uncentred."""
+        out = np.empty(self.dim, np.float32)
+        has = C.c_int32(0)
+        check(lib().fi8_bin_center(self._h, _p(out), C.byref(has)))
+        return out if has.value else None
+
+    def read_codes(self) -> np.ndarray:
+        """The packed sign codes [n, words] uint64, copied to the host."""
+        out = np.empty((self.n, self.words), np.uint64)
+        check(lib().fi8_bin_read_codes(self._h, _p(out)))
+        return out
+
+    def read_rows(self):
+        """The FlatI8 rows [n, dim] int8 and scales [n]."""
+        bq = np.empty((self.n, self.dim), np.int8)
+        sc = np.empty(self.n, np.float32)
+        check(lib().fi8_index_read_rows(self._ih, _p(bq), _p(sc)))
+        return bq, sc
 
     def Query(self, q, k: int) -> list[Hit]:
         """FlatBinaryI8.Query (flat_binary_i8.go:78) for one query."""

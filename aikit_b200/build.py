@@ -19,8 +19,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 
-CUDA_SOURCES = ["fi8_api.cu", "fi8_scan.cu", "fi8_gemm.cu", "fi8_binary.cu"]
-CUDA_HEADERS = ["fi8_device.cuh", "fi8_scan.cuh", "fi8_select.cuh", "fi8_gemm.cuh", "fi8_binary.cuh"]
+CUDA_SOURCES = ["fi8_api.cu", "fi8_scan.cu", "fi8_gemm.cu", "fi8_binary.cu", "fi8_build.cu"]
+CUDA_HEADERS = ["fi8_device.cuh", "fi8_scan.cuh", "fi8_select.cuh", "fi8_gemm.cuh", "fi8_binary.cuh", "fi8_build.cuh"]
 SYNTH_SOURCES = ["synth.c"]
 
 NVCC = os.environ.get("NVCC", "nvcc")

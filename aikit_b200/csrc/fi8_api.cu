@@ -20,6 +20,7 @@
 
 #include "../../include/fi8.h"
 #include "fi8_binary.cuh"
+#include "fi8_build.cuh"
 #include "fi8_device.cuh"
 #include "fi8_gemm.cuh"
 #include "fi8_scan.cuh"
@@ -294,23 +295,22 @@ static void index_free(fi8_index* x) {
   delete x;
 }
 
-int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int64_t n, int32_t dim,
-                     int64_t id_base, fi8_index** out) {
-  if (!out) return fail(FI8_ERR_ARG, "fi8_index_create: null out");
+}  // extern "C"
+
+// An index with zeroed device rows of the given shape (no data yet).
+static int index_alloc(fi8_ctx* ctx, int64_t n, int32_t dim, int64_t id_base, const char* who, fi8_index** out) {
   *out = nullptr;
-  if (!ctx) return fail(FI8_ERR_ARG, "fi8_index_create: null ctx");
+  if (!ctx) return fail(FI8_ERR_ARG, "%s: null ctx", who);
   if (n <= 0 || dim <= 0)  // gpu/anncuda/backend.go:125-127
     return fail(FI8_ERR_ARG, "gpu: empty int8 index (n=%lld dim=%d)", (long long)n, dim);
-  if (!codes || !scales) return fail(FI8_ERR_ARG, "fi8_index_create: null codes/scales");
   if (id_base < 0 || id_base + n > 0x7FFFFFFFll)
-    return fail(FI8_ERR_ARG, "fi8_index_create: global indices must fit in 31 bits (id_base=%lld n=%lld)",
+    return fail(FI8_ERR_ARG, "%s: global indices must fit in 31 bits (id_base=%lld n=%lld)", who,
                 (long long)id_base, (long long)n);
   const int32_t dpad = (dim + 15) / 16 * 16;
-  if (dpad > kScanMaxDpad)
-    return fail(FI8_ERR_DECLINED, "fi8_index_create: dim %d exceeds the supported %d", dim, kScanMaxDpad);
+  if (dpad > kScanMaxDpad) return fail(FI8_ERR_DECLINED, "%s: dim %d exceeds the supported %d", who, dim, kScanMaxDpad);
   DeviceGuard g(ctx->device);
   fi8_index* x = new (std::nothrow) fi8_index;
-  if (!x) return fail(FI8_ERR_OOM, "fi8_index_create: host allocation");
+  if (!x) return fail(FI8_ERR_OOM, "%s: host allocation", who);
   x->ctx = ctx;
   x->device = ctx->device;
   x->sm_count = ctx->sm_count;
@@ -327,22 +327,100 @@ int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int
   if (e == cudaSuccess) e = cudaMemsetAsync(x->d_codes, 0, (size_t)x->n_alloc * dpad, x->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(x->d_scales, 0, (size_t)x->n_alloc * sizeof(float), x->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream);
-  if (e == cudaSuccess) {
-    if (dpad == dim)
-      e = cudaMemcpyAsync(x->d_codes, codes, (size_t)n * dim, cudaMemcpyHostToDevice, x->stream);
-    else
-      e = cudaMemcpy2DAsync(x->d_codes, dpad, codes, dim, dim, (size_t)n, cudaMemcpyHostToDevice, x->stream);
-  }
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(x->d_scales, scales, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, x->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
   if (e != cudaSuccess) {
-    const int rc = cuda_fail(e, "gpu: device upload failed");
+    const int rc = cuda_fail(e, "gpu: device allocation failed");
     index_free(x);
     return rc;
   }
-  x->has_tmB = make_tmap_i8(&x->tmB, x->d_codes, (uint64_t)x->n_alloc, (uint64_t)dpad, (uint32_t)kGemmBN);
   *out = x;
+  return FI8_OK;
+}
+
+// Finish an index whose rows are on the device: wait for the uploads, build
+// the corpus tensor map.
+static int index_finish(fi8_index* x) {
+  DeviceGuard g(x->device);
+  FI8_CUDA(cudaStreamSynchronize(x->stream), "gpu: device upload failed");
+  x->has_tmB = make_tmap_i8(&x->tmB, x->d_codes, (uint64_t)x->n_alloc, (uint64_t)x->dpad, (uint32_t)kGemmBN);
+  return FI8_OK;
+}
+
+// Rows of float vectors per staged chunk of the device builds (~128 MB).
+static int64_t build_chunk_rows(int32_t dim) { return std::max<int64_t>(256, ((int64_t)128 << 20) / ((int64_t)dim * 4)); }
+
+extern "C" {
+
+int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int64_t n, int32_t dim,
+                     int64_t id_base, fi8_index** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_index_create: null out");
+  *out = nullptr;
+  if (n > 0 && dim > 0 && (!codes || !scales)) return fail(FI8_ERR_ARG, "fi8_index_create: null codes/scales");
+  fi8_index* x = nullptr;
+  int rc = index_alloc(ctx, n, dim, id_base, "fi8_index_create", &x);
+  if (rc != FI8_OK) return rc;
+  DeviceGuard g(x->device);
+  cudaError_t e;
+  if (x->dpad == dim)
+    e = cudaMemcpyAsync(x->d_codes, codes, (size_t)n * dim, cudaMemcpyHostToDevice, x->stream);
+  else
+    e = cudaMemcpy2DAsync(x->d_codes, x->dpad, codes, dim, dim, (size_t)n, cudaMemcpyHostToDevice, x->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(x->d_scales, scales, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, x->stream);
+  if (e != cudaSuccess || (rc = index_finish(x)) != FI8_OK) {
+    if (e != cudaSuccess) rc = cuda_fail(e, "gpu: device upload failed");
+    index_free(x);
+    return rc;
+  }
+  *out = x;
+  return FI8_OK;
+}
+
+int fi8_index_create_f32(fi8_ctx* ctx, const float* vecs, int64_t n, int32_t dim, int64_t id_base,
+                         fi8_index** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_index_create_f32: null out");
+  *out = nullptr;
+  if (n > 0 && dim > 0 && !vecs) return fail(FI8_ERR_ARG, "fi8_index_create_f32: null vectors");
+  fi8_index* x = nullptr;
+  int rc = index_alloc(ctx, n, dim, id_base, "fi8_index_create_f32", &x);
+  if (rc != FI8_OK) return rc;
+  DeviceGuard g(x->device);
+  const int64_t chunk = std::min<int64_t>(n, build_chunk_rows(dim));
+  float* d_v = nullptr;
+  cudaError_t e = cudaMalloc(&d_v, (size_t)chunk * dim * sizeof(float));
+  for (int64_t r0 = 0; e == cudaSuccess && r0 < n; r0 += chunk) {
+    const int64_t rows = std::min(chunk, n - r0);
+    e = cudaMemcpyAsync(d_v, vecs + (size_t)r0 * dim, (size_t)rows * dim * sizeof(float), cudaMemcpyHostToDevice,
+                        x->stream);
+    if (e == cudaSuccess)
+      e = quantize_rows_launch(d_v, rows, dim, x->dpad, x->d_codes + (size_t)r0 * x->dpad, x->d_scales + r0,
+                               x->stream);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
+  cudaFree(d_v);
+  if (e != cudaSuccess || (rc = index_finish(x)) != FI8_OK) {
+    if (e != cudaSuccess) rc = cuda_fail(e, "gpu: device build failed");
+    index_free(x);
+    return rc;
+  }
+  *out = x;
+  return FI8_OK;
+}
+
+int fi8_index_read_rows(fi8_index* idx, int8_t* codes, float* scales) {
+  if (!idx || !codes || !scales) return fail(FI8_ERR_ARG, "fi8_index_read_rows: null argument");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  fi8_index* x = idx;
+  cudaError_t e;
+  if (x->dpad == x->dim)
+    e = cudaMemcpyAsync(codes, x->d_codes, (size_t)x->n * x->dim, cudaMemcpyDeviceToHost, x->stream);
+  else
+    e = cudaMemcpy2DAsync(codes, x->dim, x->d_codes, x->dpad, x->dim, (size_t)x->n, cudaMemcpyDeviceToHost,
+                          x->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(scales, x->d_scales, (size_t)x->n * sizeof(float), cudaMemcpyDeviceToHost, x->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "fi8_index_read_rows");
   return FI8_OK;
 }
 
@@ -1066,6 +1144,111 @@ int fi8_bin_index_create(fi8_ctx* ctx, const uint64_t* codes, int32_t words, con
     return rc;
   }
   *out = b;
+  return FI8_OK;
+}
+
+int fi8_bin_index_create_f32(fi8_ctx* ctx, const float* vecs, const uint8_t* valid, int64_t n, int32_t dim,
+                             int32_t overquery, int32_t centered, const float* center, int64_t id_base,
+                             fi8_bin** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_bin_index_create_f32: null out");
+  *out = nullptr;
+  if (n > 0 && dim > 0 && !vecs) return fail(FI8_ERR_ARG, "fi8_bin_index_create_f32: null vectors");
+  fi8_index* ix = nullptr;
+  int rc = index_alloc(ctx, n, dim, id_base, "fi8_bin_index_create_f32", &ix);
+  if (rc != FI8_OK) return rc;
+  fi8_bin* b = new (std::nothrow) fi8_bin;
+  if (!b) {
+    index_free(ix);
+    return fail(FI8_ERR_OOM, "fi8_bin_index_create_f32: host allocation");
+  }
+  b->ix = ix;
+  b->words = (dim + 63) / 64;
+  b->wpad = (b->words + 1) / 2 * 2;
+  b->over = overquery < 1 ? 1 : overquery;
+  if (b->wpad * 8 > kScanMaxDpad) {
+    fi8_bin_index_destroy(b);
+    return fail(FI8_ERR_DECLINED, "fi8_bin_index_create_f32: dim %d exceeds the supported packed width", dim);
+  }
+  DeviceGuard g(ix->device);
+  cudaStream_t st = ix->stream;
+  const int64_t chunk = std::min<int64_t>(n, build_chunk_rows(dim));
+  float* d_v = nullptr;
+  uint8_t* d_valid = nullptr;
+  double* d_acc = nullptr;
+  cudaError_t e = cudaMalloc(&b->d_bits, (size_t)ix->n_alloc * b->wpad * 8);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_bits, 0, (size_t)ix->n_alloc * b->wpad * 8, st);
+  if (e == cudaSuccess) e = cudaMalloc(&d_v, (size_t)chunk * dim * sizeof(float));
+  if (e == cudaSuccess && valid) e = cudaMalloc(&d_valid, (size_t)chunk);
+  // The centre: given, computed here (newBinaryPrefilter's float64 mean over
+  // the valid rows, prefilter.go:64-85), or none (uncentred, or no valid row).
+  const bool compute = centered && !center;
+  int64_t used = 0;
+  if (compute) {
+    if (valid)
+      for (int64_t r = 0; r < n; r++) used += valid[r] != 0;
+    else
+      used = n;
+  }
+  const bool has_center = centered && (center || used > 0);
+  if (e == cudaSuccess && has_center) e = cudaMalloc(&b->d_center, (size_t)dim * sizeof(float));
+  if (e == cudaSuccess && has_center && center)
+    e = cudaMemcpyAsync(b->d_center, center, (size_t)dim * sizeof(float), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess && compute && used > 0) {
+    e = cudaMalloc(&d_acc, (size_t)dim * sizeof(double));
+    if (e == cudaSuccess) e = cudaMemsetAsync(d_acc, 0, (size_t)dim * sizeof(double), st);
+  }
+  // pass 1: int8 rows (and the column sums, when the centre is computed here);
+  // pass 2, or the same pass when the centre is known: the sign codes
+  for (int pass = 0; pass < 2 && e == cudaSuccess; pass++) {
+    const bool pack_now = (pass == 0) != (compute && used > 0);
+    if (pass == 1 && !pack_now) break;
+    if (pass == 1 && compute && used > 0) e = center_launch(d_acc, dim, used, b->d_center, st);
+    for (int64_t r0 = 0; e == cudaSuccess && r0 < n; r0 += chunk) {
+      const int64_t rows = std::min(chunk, n - r0);
+      e = cudaMemcpyAsync(d_v, vecs + (size_t)r0 * dim, (size_t)rows * dim * sizeof(float), cudaMemcpyHostToDevice,
+                          st);
+      if (e == cudaSuccess && valid) e = cudaMemcpyAsync(d_valid, valid + r0, (size_t)rows, cudaMemcpyHostToDevice, st);
+      if (e == cudaSuccess && pass == 0)
+        e = quantize_rows_launch(d_v, rows, dim, ix->dpad, ix->d_codes + (size_t)r0 * ix->dpad, ix->d_scales + r0,
+                                 st);
+      if (e == cudaSuccess && pass == 0 && compute && used > 0)
+        e = column_sum_launch(d_v, rows, dim, valid ? d_valid : nullptr, d_acc, st);
+      if (e == cudaSuccess && pack_now)
+        e = pack_rows_launch(d_v, rows, dim, has_center ? b->d_center : nullptr, valid ? d_valid : nullptr, b->wpad,
+                             b->d_bits + (size_t)r0 * b->wpad, st);
+      // the staging buffers are reused by the next chunk's copies
+      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+  }
+  cudaFree(d_v);
+  cudaFree(d_valid);
+  cudaFree(d_acc);
+  if (e != cudaSuccess || (rc = index_finish(ix)) != FI8_OK) {
+    if (e != cudaSuccess) rc = cuda_fail(e, "gpu: binary device build failed");
+    fi8_bin_index_destroy(b);
+    return rc;
+  }
+  *out = b;
+  return FI8_OK;
+}
+
+int fi8_bin_center(fi8_bin* b, float* out, int32_t* has_center) {
+  if (!b || !out || !has_center) return fail(FI8_ERR_ARG, "fi8_bin_center: null argument");
+  std::lock_guard<std::mutex> lk(b->ix->mu);
+  DeviceGuard g(b->ix->device);
+  *has_center = b->d_center ? 1 : 0;
+  if (b->d_center)
+    FI8_CUDA(cudaMemcpy(out, b->d_center, (size_t)b->ix->dim * sizeof(float), cudaMemcpyDeviceToHost), "D2H center");
+  return FI8_OK;
+}
+
+int fi8_bin_read_codes(fi8_bin* b, uint64_t* codes) {
+  if (!b || !codes) return fail(FI8_ERR_ARG, "fi8_bin_read_codes: null argument");
+  std::lock_guard<std::mutex> lk(b->ix->mu);
+  DeviceGuard g(b->ix->device);
+  FI8_CUDA(cudaMemcpy2D(codes, (size_t)b->words * 8, b->d_bits, (size_t)b->wpad * 8, (size_t)b->words * 8,
+                        (size_t)b->ix->n, cudaMemcpyDeviceToHost),
+           "D2H codes");
   return FI8_OK;
 }
 

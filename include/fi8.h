@@ -58,6 +58,19 @@ int fi8_ctx_sm_count(fi8_ctx* ctx, int* out);
 int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int64_t n,
                      int32_t dim, int64_t id_base, fi8_index** out);
 
+/* NewFlatI8 on the device (ann/flat_i8.go:74-109): vecs [n*dim] f32 host rows
+ * are copied in chunks and quantized on the GPU exactly as QuantizeRowInt8
+ * does (linalg/quant.go:43-71; an all-zero row gets scale 1). Ragged input is
+ * the caller's to pad or truncate to dim, as NewFlatI8 does. The result is
+ * the index fi8_index_create would build from NewFlatI8's own codes. No
+ * counterpart on the reference's device seam (its build is CPU-only). */
+int fi8_index_create_f32(fi8_ctx* ctx, const float* vecs, int64_t n, int32_t dim, int64_t id_base,
+                         fi8_index** out);
+
+/* Copy an index's rows back to the host: codes [n*dim] int8 and scales [n]
+ * (e.g. to fill FlatI8's bq and scales after a device build). */
+int fi8_index_read_rows(fi8_index* idx, int8_t* codes, float* scales);
+
 /* I8Index.Close (ann/backend.go:31; gpu/anncuda/backend.go:238-246). */
 int fi8_index_destroy(fi8_index* idx);
 
@@ -189,6 +202,24 @@ int fi8_bin_index_create(fi8_ctx* ctx, const uint64_t* codes, int32_t words, con
                          const int8_t* i8, const float* scales, int64_t n, int32_t dim, int32_t overquery,
                          int64_t id_base, fi8_bin** out);
 int fi8_bin_index_destroy(fi8_bin* b);
+
+/* newFlatBinaryI8 on the device (ann/flat_binary_i8.go:57-62): from f32 rows
+ * vecs [n*dim], the FlatI8 rows (quantized as fi8_index_create_f32) and the
+ * prefilter's sign codes. valid [n] (NULL = all) marks the rows of the
+ * reference's full dim; the others (ragged input) are left out of the centre
+ * and keep all-zero codes (prefilter.go:70-95). centered = 0 builds an
+ * uncentred prefilter. center (NULL = compute) supplies the centre, e.g. the
+ * whole corpus's for a row shard; computed, it is float32(float64 sum of the
+ * valid rows in row order / their count), bit-identical to the reference,
+ * and none when no row is valid. */
+int fi8_bin_index_create_f32(fi8_ctx* ctx, const float* vecs, const uint8_t* valid, int64_t n, int32_t dim,
+                             int32_t overquery, int32_t centered, const float* center, int64_t id_base,
+                             fi8_bin** out);
+
+/* The prefilter's centre [dim] (*has_center = 0 when uncentred) and its
+ * packed codes [n*words], copied back to the host. */
+int fi8_bin_center(fi8_bin* b, float* out, int32_t* has_center);
+int fi8_bin_read_codes(fi8_bin* b, uint64_t* codes);
 
 /* The FlatI8 index inside b (owned by b): for fi8_index_* options, timing and
  * launch counts. */
