@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 
 CUDA_SOURCES = ["fi8_api.cu", "fi8_scan.cu", "fi8_gemm.cu", "fi8_binary.cu", "fi8_build.cu"]
-CUDA_HEADERS = ["fi8_device.cuh", "fi8_scan.cuh", "fi8_select.cuh", "fi8_gemm.cuh", "fi8_binary.cuh", "fi8_build.cuh"]
+CUDA_HEADERS = ["fi8_device.cuh", "fi8_scan.cuh", "fi8_select.cuh", "fi8_gemm.cuh", "fi8_binary.cuh", "fi8_build.cuh", "fi8_stage.h"]
 SYNTH_SOURCES = ["synth.c"]
 
 NVCC = os.environ.get("NVCC", "nvcc")

@@ -24,6 +24,7 @@
 #include "fi8_device.cuh"
 #include "fi8_gemm.cuh"
 #include "fi8_scan.cuh"
+#include "fi8_stage.h"
 
 using namespace fi8;
 
@@ -345,8 +346,10 @@ static int index_finish(fi8_index* x) {
   return FI8_OK;
 }
 
-// Rows of float vectors per staged chunk of the device builds (~128 MB).
-static int64_t build_chunk_rows(int32_t dim) { return std::max<int64_t>(256, ((int64_t)128 << 20) / ((int64_t)dim * 4)); }
+// Rows of float vectors per chunk of the device builds: one pinned buffer.
+static int64_t build_chunk_rows(int32_t dim) {
+  return std::max<int64_t>(1, (int64_t)(PinnedStager::kBufBytes / ((size_t)dim * 4)));
+}
 
 extern "C" {
 
@@ -359,13 +362,11 @@ int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int
   int rc = index_alloc(ctx, n, dim, id_base, "fi8_index_create", &x);
   if (rc != FI8_OK) return rc;
   DeviceGuard g(x->device);
-  cudaError_t e;
-  if (x->dpad == dim)
-    e = cudaMemcpyAsync(x->d_codes, codes, (size_t)n * dim, cudaMemcpyHostToDevice, x->stream);
-  else
-    e = cudaMemcpy2DAsync(x->d_codes, x->dpad, codes, dim, dim, (size_t)n, cudaMemcpyHostToDevice, x->stream);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(x->d_scales, scales, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, x->stream);
+  PinnedStager stage;
+  cudaError_t e = stage.init();
+  if (e == cudaSuccess) e = stage.put_rows(x->d_codes, x->dpad, codes, dim, dim, n, x->stream);
+  if (e == cudaSuccess) e = stage.put_rows(x->d_scales, 4, scales, 4, 4, n, x->stream);
+  if (e == cudaSuccess) e = stage.finish();
   if (e != cudaSuccess || (rc = index_finish(x)) != FI8_OK) {
     if (e != cudaSuccess) rc = cuda_fail(e, "gpu: device upload failed");
     index_free(x);
@@ -386,15 +387,19 @@ int fi8_index_create_f32(fi8_ctx* ctx, const float* vecs, int64_t n, int32_t dim
   DeviceGuard g(x->device);
   const int64_t chunk = std::min<int64_t>(n, build_chunk_rows(dim));
   float* d_v = nullptr;
-  cudaError_t e = cudaMalloc(&d_v, (size_t)chunk * dim * sizeof(float));
+  PinnedStager stage;
+  cudaError_t e = stage.init();
+  if (e == cudaSuccess) e = cudaMalloc(&d_v, (size_t)chunk * dim * sizeof(float));
+  const size_t rb = (size_t)dim * sizeof(float);
   for (int64_t r0 = 0; e == cudaSuccess && r0 < n; r0 += chunk) {
     const int64_t rows = std::min(chunk, n - r0);
-    e = cudaMemcpyAsync(d_v, vecs + (size_t)r0 * dim, (size_t)rows * dim * sizeof(float), cudaMemcpyHostToDevice,
-                        x->stream);
+    // stream order keeps the next chunk's copy behind this chunk's kernel
+    e = stage.put_rows(d_v, rb, vecs + (size_t)r0 * dim, rb, rb, rows, x->stream);
     if (e == cudaSuccess)
       e = quantize_rows_launch(d_v, rows, dim, x->dpad, x->d_codes + (size_t)r0 * x->dpad, x->d_scales + r0,
                                x->stream);
   }
+  if (e == cudaSuccess) e = stage.finish();
   if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
   cudaFree(d_v);
   if (e != cudaSuccess || (rc = index_finish(x)) != FI8_OK) {
@@ -1127,11 +1132,12 @@ int fi8_bin_index_create(fi8_ctx* ctx, const uint64_t* codes, int32_t words, con
   b->over = overquery < 1 ? 1 : overquery;
   DeviceGuard g(ix->device);
   const size_t pitch = (size_t)wpad * 8;
-  cudaError_t e = cudaMalloc(&b->d_bits, (size_t)ix->n_alloc * pitch);
+  PinnedStager stage;
+  cudaError_t e = stage.init();
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_bits, (size_t)ix->n_alloc * pitch);
   if (e == cudaSuccess) e = cudaMemsetAsync(b->d_bits, 0, (size_t)ix->n_alloc * pitch, ix->stream);
-  if (e == cudaSuccess)
-    e = cudaMemcpy2DAsync(b->d_bits, pitch, codes, (size_t)words * 8, (size_t)words * 8, (size_t)n,
-                          cudaMemcpyHostToDevice, ix->stream);
+  if (e == cudaSuccess) e = stage.put_rows(b->d_bits, pitch, codes, (size_t)words * 8, (size_t)words * 8, n, ix->stream);
+  if (e == cudaSuccess) e = stage.finish();
   if (e == cudaSuccess && center) {
     e = cudaMalloc(&b->d_center, (size_t)dim * sizeof(float));
     if (e == cudaSuccess)
@@ -1175,7 +1181,9 @@ int fi8_bin_index_create_f32(fi8_ctx* ctx, const float* vecs, const uint8_t* val
   float* d_v = nullptr;
   uint8_t* d_valid = nullptr;
   double* d_acc = nullptr;
-  cudaError_t e = cudaMalloc(&b->d_bits, (size_t)ix->n_alloc * b->wpad * 8);
+  PinnedStager stage;
+  cudaError_t e = stage.init();
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_bits, (size_t)ix->n_alloc * b->wpad * 8);
   if (e == cudaSuccess) e = cudaMemsetAsync(b->d_bits, 0, (size_t)ix->n_alloc * b->wpad * 8, st);
   if (e == cudaSuccess) e = cudaMalloc(&d_v, (size_t)chunk * dim * sizeof(float));
   if (e == cudaSuccess && valid) e = cudaMalloc(&d_valid, (size_t)chunk);
@@ -1203,11 +1211,12 @@ int fi8_bin_index_create_f32(fi8_ctx* ctx, const float* vecs, const uint8_t* val
     const bool pack_now = (pass == 0) != (compute && used > 0);
     if (pass == 1 && !pack_now) break;
     if (pass == 1 && compute && used > 0) e = center_launch(d_acc, dim, used, b->d_center, st);
+    const size_t rb = (size_t)dim * sizeof(float);
     for (int64_t r0 = 0; e == cudaSuccess && r0 < n; r0 += chunk) {
       const int64_t rows = std::min(chunk, n - r0);
-      e = cudaMemcpyAsync(d_v, vecs + (size_t)r0 * dim, (size_t)rows * dim * sizeof(float), cudaMemcpyHostToDevice,
-                          st);
-      if (e == cudaSuccess && valid) e = cudaMemcpyAsync(d_valid, valid + r0, (size_t)rows, cudaMemcpyHostToDevice, st);
+      // stream order keeps the next chunk's copies behind this chunk's kernels
+      e = stage.put_rows(d_v, rb, vecs + (size_t)r0 * dim, rb, rb, rows, st);
+      if (e == cudaSuccess && valid) e = stage.put_rows(d_valid, 1, valid + r0, 1, 1, rows, st);
       if (e == cudaSuccess && pass == 0)
         e = quantize_rows_launch(d_v, rows, dim, ix->dpad, ix->d_codes + (size_t)r0 * ix->dpad, ix->d_scales + r0,
                                  st);
@@ -1216,10 +1225,10 @@ int fi8_bin_index_create_f32(fi8_ctx* ctx, const float* vecs, const uint8_t* val
       if (e == cudaSuccess && pack_now)
         e = pack_rows_launch(d_v, rows, dim, has_center ? b->d_center : nullptr, valid ? d_valid : nullptr, b->wpad,
                              b->d_bits + (size_t)r0 * b->wpad, st);
-      // the staging buffers are reused by the next chunk's copies
-      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     }
   }
+  if (e == cudaSuccess) e = stage.finish();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   cudaFree(d_v);
   cudaFree(d_valid);
   cudaFree(d_acc);

@@ -22,7 +22,7 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=100)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
-    ap.add_argument("--mode", choices=["topk", "score", "binary"], default="topk")
+    ap.add_argument("--mode", choices=["topk", "score", "binary", "build"], default="topk")
     ap.add_argument("--recipe", choices=["mixture", "ties", "unit"], default="mixture",
                     help="corpus: C2/C3 mixture, C5 ties (codes in {-2..2}, scale 1/127), or iid unit rows")
     ap.add_argument("--over", type=int, default=100, help="binary mode: overquery (cand = k * over)")
@@ -37,6 +37,8 @@ def main() -> None:
     be = B200Backend(0)
     if a.mode == "binary":
         return binary_case(a, be)
+    if a.mode == "build":
+        return build_case(a, be)
     if a.recipe == "ties":
         r = synth.Recipe(synth.TIES, a.dim, seed=20265)
     elif a.recipe == "unit":
@@ -137,6 +139,29 @@ def binary_case(a, be) -> None:
         warm = max(a.reps - 1, 1)
         out["kernels"] = {k: {"launches_per_rep": v["launches"] / warm, "us_per_rep": v["ms"] * 1e3 / warm}
                           for k, v in bix.kernel_times().items()}
+    print(json.dumps(out))
+
+
+def build_case(a, be) -> None:
+    """Device corpus builds from float rows: FlatI8 (quantize) and
+    FlatBinaryI8 (quantize, float64 centre, sign codes), timed end to end
+    from the host array (its upload included)."""
+    import time
+    from aikit_b200 import synth
+    r = synth.Recipe(synth.MIXTURE, a.dim, seed=20262, ncl=1000, sigma=0.3)
+    v = r.floats(a.rows)
+    gb = v.nbytes / 1e9
+    out = {"mode": "build", "rows": a.rows, "dim": a.dim, "float_gb": gb}
+    for name, fn in (("flat_i8", lambda: be.NewI8IndexFromFloats(v)),
+                     ("flat_binary_i8", lambda: be.NewBinaryI8IndexFromFloats(v))):
+        times = []
+        for _ in range(max(a.reps, 1)):
+            t0 = time.perf_counter()
+            ix = fn()
+            times.append(time.perf_counter() - t0)
+            ix.Close()
+        best = min(times[1:] if len(times) > 1 else times)
+        out[name] = {"s": times, "rows_per_s": a.rows / best, "float_gbs": gb / best}
     print(json.dumps(out))
 
 

@@ -224,7 +224,10 @@ def main():
     bq, bs = recipe.codes(hi - lo, row0=lo)
     gen_s = time.time() - t0
     be = B200Backend(local)
+    t0 = time.perf_counter()
     ix = be.NewI8Index(bq, bs, hi - lo, DIM, id_base=lo)
+    upload_s = time.perf_counter() - t0
+    upload_bytes = bq.nbytes + bs.nbytes
     del bq, bs
 
     nb = 8  # distinct query batches cycled through the steps
@@ -340,7 +343,9 @@ def main():
         "config": {"workload": WORKLOAD, "n_rows": n_total, "dim": DIM, "k": K, "batch": BATCH,
                    "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
                    "l2": "corpus 7.7 GB >> 126 MB L2: no flush needed",
-                   "corpus_gen_s": round(gen_s, 1)},
+                   "corpus_gen_s": round(gen_s, 1),
+                   "upload": {"s": round(upload_s, 3), "gbs": round(upload_bytes / upload_s / 1e9, 1),
+                              "api": "fi8_index_create from pageable host arrays (pinned double-buffer staging)"}},
         "roofline": roof64,
         "gpu_launches": launches + launches1,
         "e2e": e2e,
