@@ -440,11 +440,7 @@ bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g, bool bin
   if (binary && topk) return false;
   int cpl = 0;
   const int rpg = rows_per_group(dpad, binary, &cpl);
-  // Tile: one pass of 32*RPG rows, doubled (more passes) while it stays at or
-  // under 32 KB; at most 256 rows so it divides the allocation padding.
-  int R = 32 * rpg;
-  while (R < 256 && (size_t)(2 * R) * dpad <= 32 * 1024) R *= 2;
-  const size_t stage = (size_t)R * (dpad + (binary ? 0 : 4));
+  const size_t row_bytes = (size_t)dpad + (binary ? 0 : 4);
   int cap = 0, kp = 0;
   if (topk) {
     if (k <= 0) return false;
@@ -456,16 +452,41 @@ bool scan_geometry(int32_t dpad, int32_t k, bool topk, ScanGeometry* g, bool bin
   // query row, then the groups' candidate buffers (top-K) or the distance
   // histogram of dpad*8 + 1 bins (binary)
   const size_t fixed = (size_t)dpad + (size_t)kGroups * cap * 8 + (binary ? ((size_t)dpad * 8 + 1) * 4 : 0);
-  // Ring depth: an even count (stage s always belongs to consumer group s % 2;
-  // with an odd count the groups would share stages, and because bulk copies
-  // complete out of order a parity wait could then observe the wrong phase),
-  // at least two stages per group when they fit, and about 100-160 KB in
-  // flight per SM (B200 measurement: 3-4 x 32-48 KB sustain ~7.3 TB/s with one
-  // CTA per SM; 4 x 48 KB already drops).
-  int stages = 2;
-  while (stages + 2 <= kMaxStages && (stages + 2) * stage <= 160 * 1024 && fixed + (stages + 2) * stage <= kSmemBudget)
-    stages += 2;
-  if (fixed + stages * stage > kSmemBudget) return false;
+  // Tile (R rows, a power-of-two multiple of one pass of 32*RPG rows, at most
+  // 256 so it divides the allocation padding) and ring depth S (even: stage s
+  // always belongs to consumer group s % 2; with an odd count the groups would
+  // share stages, and because bulk copies complete out of order a parity wait
+  // could then observe the wrong phase). One CTA per SM moves a bounded number
+  // of copies per second, so tiles must be large; measured on B200 (C2-size
+  // corpora, 768-1024-byte and 256-384-byte rows): 32 KB x 4 and ~96 KB x 2
+  // sustain ~7.0 TB/s, 48-64 KB tiles 6.7-6.9, 24 KB x 6 only 6.2.
+  struct Choice {
+    int R, S;
+  } pick[3];
+  int np = 0;
+  for (int r = 32 * rpg; r <= 256; r *= 2)
+    if ((size_t)r * dpad == 32 * 1024) pick[np++] = {r, 4};
+  {
+    int r = 32 * rpg;
+    while (r < 256 && (size_t)(2 * r) * dpad <= 100 * 1024) r *= 2;
+    if ((size_t)r * dpad >= 48 * 1024) pick[np++] = {r, 2};
+  }
+  {
+    int r = 32 * rpg;  // small rows: the largest tile at or under 32 KB, deeper ring
+    while (r < 256 && (size_t)(2 * r) * dpad <= 32 * 1024) r *= 2;
+    int st = 2;
+    while (st + 2 <= kMaxStages && (size_t)(st + 2) * r * row_bytes <= 160 * 1024) st += 2;
+    pick[np++] = {r, st};
+  }
+  int R = 0, stages = 0;
+  for (int i = 0; i < np && !R; i++)
+    for (int st = pick[i].S; st >= 2 && !R; st -= 2)
+      if (fixed + (size_t)st * pick[i].R * row_bytes <= kSmemBudget) {
+        R = pick[i].R;
+        stages = st;
+      }
+  if (!R) return false;
+  const size_t stage = (size_t)R * row_bytes;
   g->rows_per_tile = R;
   g->stages = stages;
   g->cap = cap;

@@ -105,6 +105,7 @@ class ClockSampler:
 
     def __init__(self, device_index: int):
         self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.mem, self.temp, self.power = [], [], []
         self._stop = threading.Event()
         self._h = None
         try:
@@ -131,6 +132,9 @@ class ClockSampler:
         while not self._stop.is_set():
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.mem.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_MEM))
+                self.temp.append(nv.nvmlDeviceGetTemperature(self._h, nv.NVML_TEMPERATURE_GPU))
+                self.power.append(nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0)
                 mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
                 for name, bit in self.REASONS.items():
                     if mask & bit and name != "gpu_idle":
@@ -153,8 +157,12 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        out = {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        if self.mem:
+            out.update(mem_mhz=statistics.median(self.mem), temp_c_max=max(self.temp),
+                       power_w_median=round(statistics.median(self.power), 1))
+        return out
 
 
 # ----------------------------------------------------------------------------
