@@ -154,6 +154,7 @@ struct fi8_index {
   CUtensorMap tmA;       // over d_A, rebuilt when d_A moves
   const int8_t* tmA_base = nullptr;
   int64_t tmA_rows = 0;
+  int32_t tmA_box = 0;   // query tile rows the map's box was built for
   float* d_qscale = nullptr;
   size_t qscale_cap = 0;
   unsigned long long* d_thr = nullptr;
@@ -551,21 +552,25 @@ static int32_t pow2_ge_host(int64_t x) {
   return p;
 }
 
-// Row ranges [0,s1), [s1, s1*F1), ... rounded to 256-row tiles. A range
-// admits about k*F candidates per query. Every range costs a GEMM launch and a
-// select, so the growth factor starts at 16 (the first ranges are short and
-// latency-bound, and their candidates are dense per tile) and rises to 64
-// once ranges are long enough (from 16K rows) that the extra candidates
-// spread thinly over many tiles, within a quarter of the per-query buffer.
+// Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles. A range after
+// the first admits about k*F candidates per query. Every range costs a GEMM
+// launch and a select, so ranges are few: the first has no threshold and
+// takes every row as a candidate, up to a quarter of the per-query buffer
+// (16K rows at batch 64); then the growth factor is 64 (16 while ranges are
+// short), within a quarter of the buffer.
 static void plan_ranges(int64_t n, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
   const int64_t room = std::max<int64_t>(4, cap / (4 * (int64_t)k));
   const int64_t F1 = std::min<int64_t>(16, room);
   const int64_t F2 = std::min<int64_t>(64, room);
-  int64_t hi = std::max<int64_t>(k, 1024);
+  int64_t hi = std::max<int64_t>(std::max<int64_t>(k, 1024), std::min<int64_t>(16384, cap / 4));
   hi = (hi + kGemmBN - 1) / kGemmBN * kGemmBN;
   int64_t lo = 0;
   while (lo < n) {
-    const int64_t h = std::min<int64_t>(n, hi);
+    int64_t h = std::min<int64_t>(n, hi);
+    // a short tail after this range joins it when the joined range still
+    // admits few enough candidates (about k * (h - lo) / lo per query): one
+    // launch and one select fewer, which matters on small row shards
+    if (lo > 0 && h < n && n - h < (h - lo) / 2 && n - lo <= lo * room) h = n;
     out->push_back(GemmLevel{lo, h});
     lo = h;
     const int64_t F = lo >= 16 * 1024 ? F2 : F1;
@@ -578,7 +583,8 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
   if (k > select_max_k())
     return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d beyond the device top-K)", k);
   const int32_t kp = pow2_ge_host(k);
-  const int32_t Mpad = (M + kGemmBM - 1) / kGemmBM * kGemmBM;
+  const int32_t bm = M <= 64 ? 64 : kGemmBM;  // the MMA's M: a small batch is one 64-query tile
+  const int32_t Mpad = (M + bm - 1) / bm * bm;
   // per-query candidate capacity: ~256 MB of keys at most across the batch
   int32_t cap = pow2_ge_host(std::max<int64_t>(8192, std::min<int64_t>(65536, (1ll << 25) / M)));
   if (cap > 65536) cap = 65536;
@@ -590,15 +596,16 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
   if ((rc = ensure_device(&x->d_cand, &x->cand_cap, (size_t)M * cap, "gemm cand")) != FI8_OK) return rc;
   if ((rc = ensure_device(&x->d_topk, &x->topk_cap, (size_t)M * kp, "gemm topk")) != FI8_OK) return rc;
   const int64_t A_rows = (int64_t)(x->A_cap / x->dpad);
-  if (x->tmA_base != x->d_A || x->tmA_rows != A_rows) {
-    if (!make_tmap_i8(&x->tmA, x->d_A, (uint64_t)A_rows, (uint64_t)x->dpad, (uint32_t)kGemmBM))
+  if (x->tmA_base != x->d_A || x->tmA_rows != A_rows || x->tmA_box != bm) {
+    if (!make_tmap_i8(&x->tmA, x->d_A, (uint64_t)A_rows, (uint64_t)x->dpad, (uint32_t)bm))
       return fail(FI8_ERR_CUDA, "fi8: cuTensorMapEncodeTiled failed for the query tile map");
     x->tmA_base = x->d_A;
     x->tmA_rows = A_rows;
+    x->tmA_box = bm;
   }
   cudaEvent_t t0 = timer_begin(x, st);
   cudaError_t e = quantize_launch(d_q, M, Mpad, x->dim, x->dpad, x->d_A, x->d_qscale, x->d_thr, x->d_cnt,
-                                  x->d_topk, kp, st);
+                                  x->d_topk, kp, bm, st);
   if (e != cudaSuccess) return cuda_fail(e, "quantize_launch");
   timer_end(x, st, t0, FI8_KERNEL_QUANTIZE, (double)M * x->dim * 4 + (double)Mpad * x->dpad);
   x->last_launches++;
@@ -607,7 +614,7 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
   GemmParams p{};
   p.kchunks = (x->dpad + kGemmBK - 1) / kGemmBK;
   p.M = M;
-  p.qtiles = Mpad / kGemmBM;
+  p.qtiles = Mpad / bm;
   p.id_base = x->id_base;
   p.scales = x->d_scales;
   p.qscale = x->d_qscale;
@@ -626,7 +633,7 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
     const int64_t units = (int64_t)p.qtiles * p.rtiles;
     const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(x->sm_count, units));
     t0 = timer_begin(x, st);
-    e = gemm_launch(x->tmA, x->tmB, p, G, st);
+    e = gemm_launch(x->tmA, x->tmB, p, G, bm, st);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_launch");
     // the range's codes and scales, plus the int8 query tile
     timer_end(x, st, t0, FI8_KERNEL_GEMM,
@@ -634,7 +641,7 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
     const bool last = (i + 1 == ranges.size());
     t0 = timer_begin(x, st);
     e = select_launch(M, k, kp, x->d_topk, x->d_thr, x->d_cnt, x->d_cand, cap, last ? d_keys : nullptr,
-                      x->d_err, st);
+                      x->d_err, x->sm_count, st);
     if (e != cudaSuccess) return cuda_fail(e, "select_launch");
     timer_end(x, st, t0, FI8_KERNEL_SELECT, 0.0);
     x->last_launches += 2;

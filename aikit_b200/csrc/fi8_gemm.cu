@@ -36,22 +36,30 @@ namespace fi8 {
 
 namespace {
 
-constexpr int kStageA = kGemmBM * kGemmBK;  // 16 KB
-constexpr int kStageB = kGemmBN * kGemmBK;  // 32 KB
-constexpr int kStageBytes = kStageA + kStageB;
+// Query tiles of BM = 64 or 128 queries (the MMA's M). A batch of at most 64
+// queries uses M = 64: half the tensor work and half the query-tile traffic of
+// padding it to 128.
+template <int BM>
+__host__ __device__ constexpr int stage_a() { return BM * kGemmBK; }  // 8 / 16 KB
+constexpr int kStageB = kGemmBN * kGemmBK;                      // 32 KB
+template <int BM>
+__host__ __device__ constexpr int stage_bytes() { return stage_a<BM>() + kStageB; }
 constexpr int kStages = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kGemmThreads = 64 + kEpiThreads;
 constexpr int kTmemCols = 512;  // two 256-column accumulators
 constexpr int kStageKeys = 4;   // staged candidate keys per epilogue thread
-constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024;  // + alignment slack
+template <int BM>
+constexpr size_t gemm_smem() { return (size_t)kStages * stage_bytes<BM>() + 1024; }  // + alignment slack
 
 // tcgen05 instruction descriptor, kind::i8: D = s32 (c_format 2), A and B
-// signed 8-bit (format 1), both K-major, N = 256 (n_dim = N>>3), M = 128
+// signed 8-bit (format 1), both K-major, N = 256 (n_dim = N>>3), M = BM
 // (m_dim = M>>4).
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGemmBN >> 3) << 17) |
-                            ((uint32_t)(kGemmBM >> 4) << 24);
+template <int BM>
+__host__ __device__ constexpr uint32_t idesc() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGemmBN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
 
 // Shared-memory matrix descriptor for a K-major SWIZZLE_128B tile whose rows
 // are 128 bytes: start address >> 4, leading byte offset 1 (unused for
@@ -82,12 +90,13 @@ __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+template <int BM>
 __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "l"(adesc), "l"(bdesc), "r"(idesc<BM>()), "r"(accumulate)
       : "memory");
 }
 
@@ -111,18 +120,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Placement of a tile's queries in the A operand (= TMEM lanes). A tile with
-// at most 64 real queries spreads them 16 per 32-lane quarter, so all four
-// epilogue sub-partitions get work; a fuller tile is dense.
-__host__ __device__ __forceinline__ int tile_row_of(int j, int m_t) {
-  return m_t <= 64 ? ((j >> 4) << 5) + (j & 15) : j;
-}
-__device__ __forceinline__ int tile_query_of(int r, int m_t) {
-  if (m_t <= 64) {
+// Which query of a tile an A row holds, and which query a TMEM lane's
+// accumulators belong to (-1: none).
+//  * BM = 64: A rows are dense; the M = 64 accumulator puts rows 16i..16i+15
+//    in lanes 32i..32i+15, so every epilogue sub-partition gets 16 queries.
+//  * BM = 128: A row r is TMEM lane r. A tile with at most 64 real queries
+//    places them 16 per 32-lane quarter, for the same balance; a fuller tile
+//    is dense.
+template <int BM>
+__device__ __forceinline__ int arow_query(int r, int m_t) {
+  if (BM == 128 && m_t <= 64) {
     const int l = r & 31;
     return l < 16 ? ((r >> 5) << 4) + l : -1;
   }
   return r;
+}
+template <int BM>
+__device__ __forceinline__ int lane_query(int r, int m_t) {
+  if (BM == 64 || m_t <= 64) {
+    const int l = r & 31;
+    return l < 16 ? ((r >> 5) << 4) + l : -1;
+  }
+  return r;
+}
+// A row of query j of a tile
+template <int BM>
+__device__ __forceinline__ int query_arow(int j, int m_t) {
+  return (BM == 128 && m_t <= 64) ? ((j >> 4) << 5) + (j & 15) : j;
 }
 
 // Move a thread's staged candidate keys into its query's global list.
@@ -134,8 +158,11 @@ __device__ __forceinline__ void flush_staged(const GemmParams& p, int q, const u
     if (pos < (unsigned int)p.cap) dst[pos] = stage[j];
 }
 
+template <int BM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  constexpr int kStageA = stage_a<BM>();
+  constexpr int kStageBytes = stage_bytes<BM>();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ uint64_t s_full[kStages], s_empty[kStages], s_tfull[2], s_tempty[2], s_done;
   __shared__ uint32_t s_tmem;
@@ -198,7 +225,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           unsigned char* st = smem + (size_t)s * kStageBytes;
           mbar_arrive_expect_tx(&s_full[s], kStageBytes);
-          tma_load_2d(st, &tmA, kc * kGemmBK, qt * kGemmBM, &s_full[s]);
+          tma_load_2d(st, &tmA, kc * kGemmBK, qt * BM, &s_full[s]);
           tma_load_2d(st + kStageA, &tmB, kc * kGemmBK, row0, &s_full[s]);
         }
       }
@@ -232,7 +259,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kGemmBK / 32; k++) {
             // advance K by 32 bytes inside the swizzled 128-byte rows
-            umma_i8(d_tmem, sw128_desc(a_base) + (uint64_t)(2 * k), sw128_desc(b_base) + (uint64_t)(2 * k),
+            umma_i8<BM>(d_tmem, sw128_desc(a_base) + (uint64_t)(2 * k), sw128_desc(b_base) + (uint64_t)(2 * k),
                     (kc > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&s_empty[s]);
@@ -280,11 +307,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         flush_staged(p, q, my_stage, staged);  // staged keys belong to the previous tile's query
         staged = 0;
         cur_qt = qt;
-        const int m_t = min(kGemmBM, p.M - qt * kGemmBM);
-        const int j = tile_query_of(r, m_t);
+        const int m_t = min(BM, p.M - qt * BM);
+        const int j = lane_query<BM>(r, m_t);
         const bool valid_q = j >= 0 && j < m_t;
-        q = qt * kGemmBM + j;
-        qs = valid_q ? p.qscale[qt * kGemmBM + r] : 0.0f;
+        q = qt * BM + j;
+        qs = valid_q ? p.qscale[qt * BM + query_arow<BM>(j, m_t)] : 0.0f;
         T = valid_q ? p.thr[q] : ~0ull;
         // T is the k-th best key of rows below this range, and every row of
         // this range has a larger index, so a row scoring exactly T's score
@@ -397,24 +424,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // One CTA per A row (Mpad rows): quantize the query placed there
-// (quant.go:43-71, zero scale 0; see tile_row_of) or zero-fill an unused row,
+// (quant.go:43-71, zero scale 0; see arow_query) or zero-fill an unused row,
 // and reset that query's select state.
+template <int BM>
 __global__ void __launch_bounds__(256) quantize_kernel(const float* q, int M, int d, int dpad, int8_t* A,
                                                        float* qscale, unsigned long long* thr, unsigned int* cnt,
                                                        uint64_t* topk, int kp) {
   __shared__ float s_red[8];
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
-  const int qt = row / kGemmBM;
-  const int m_t = min(kGemmBM, M - qt * kGemmBM);
-  const int j = tile_query_of(row % kGemmBM, m_t);
+  const int qt = row / BM;
+  const int m_t = min(BM, M - qt * BM);
+  const int j = arow_query<BM>(row % BM, m_t);
   int8_t* dst = A + (size_t)row * dpad;
   if (j < 0 || j >= m_t) {  // no query at this row
     for (int i = tid; i < dpad; i += blockDim.x) dst[i] = 0;
     if (tid == 0) qscale[row] = 0.0f;
     return;
   }
-  const int qi = qt * kGemmBM + j;
+  const int qi = qt * BM + j;
   const float* src = q + (size_t)qi * d;
   float m = 0.0f;
   for (int i = tid; i < d; i += blockDim.x) m = absmax_step(m, src[i]);
@@ -467,8 +495,8 @@ __device__ __forceinline__ uint64_t union_key(const uint64_t* mine, int kp, cons
 }
 
 __global__ void __launch_bounds__(kSelThreads)
-    select_kernel(int k, int kp, uint64_t* topk, unsigned long long* thr, unsigned int* cnt, const uint64_t* cand,
-                  int cap, uint64_t* out, unsigned int* err) {
+    select_kernel(int k, int kp, int cap_s, uint64_t* topk, unsigned long long* thr, unsigned int* cnt,
+                  const uint64_t* cand, int cap, uint64_t* out, unsigned int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_count;
   __shared__ unsigned long long s_prefix, s_mask, s_min;
@@ -477,6 +505,7 @@ __global__ void __launch_bounds__(kSelThreads)
   __shared__ int s_rank, s_done;
   uint64_t* sel = reinterpret_cast<uint64_t*>(smem);  // [kp] the kept keys
   uint64_t* ranked = sel + kp;                          // [kp] their order (last range)
+  uint64_t* ubuf = ranked + kp;                         // [cap_s] the union, when staged
   const int qi = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -488,6 +517,24 @@ __global__ void __launch_bounds__(kSelThreads)
   const int n_c = (int)(c_all < (unsigned int)cap ? c_all : (unsigned int)cap);
   const uint64_t* src = cand + (size_t)qi * cap;
   const int n_all = kp + n_c;  // slots of the union; empty keys (0) are skipped
+  // A union that fits the shared buffer (one CTA per query in a single wave
+  // can afford a large one) is read from L2 once; otherwise every pass reads
+  // it from L2.
+  const bool staged = n_all <= cap_s;
+  if (staged) {
+    for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
+      uint64_t keys[kSelUnroll];
+#pragma unroll
+      for (int u = 0; u < kSelUnroll; u++) keys[u] = union_key(mine, kp, src, n_all, i0 + u * kSelThreads + tid);
+#pragma unroll
+      for (int u = 0; u < kSelUnroll; u++)
+        if (i0 + u * kSelThreads + tid < n_all) ubuf[i0 + u * kSelThreads + tid] = keys[u];
+    }
+  }
+  auto key_at = [&](int i) -> uint64_t {
+    if (staged) return i < n_all ? ubuf[i] : kEmptyKey;
+    return union_key(mine, kp, src, n_all, i);
+  };
   if (tid == 0) {
     s_prefix = 0ull;
     s_mask = 0ull;
@@ -505,7 +552,7 @@ __global__ void __launch_bounds__(kSelThreads)
     for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
       uint64_t keys[kSelUnroll];  // loads first, so their L2 latencies overlap
 #pragma unroll
-      for (int u = 0; u < kSelUnroll; u++) keys[u] = union_key(mine, kp, src, n_all, i0 + u * kSelThreads + tid);
+      for (int u = 0; u < kSelUnroll; u++) keys[u] = key_at(i0 + u * kSelThreads + tid);
 #pragma unroll
       for (int u = 0; u < kSelUnroll; u++) {
         const uint64_t key = keys[u];
@@ -565,7 +612,7 @@ __global__ void __launch_bounds__(kSelThreads)
   for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
     uint64_t keys[kSelUnroll];
 #pragma unroll
-    for (int u = 0; u < kSelUnroll; u++) keys[u] = union_key(mine, kp, src, n_all, i0 + u * kSelThreads + tid);
+    for (int u = 0; u < kSelUnroll; u++) keys[u] = key_at(i0 + u * kSelThreads + tid);
 #pragma unroll
     for (int u = 0; u < kSelUnroll; u++) {
       const uint64_t key = keys[u];
@@ -642,29 +689,43 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pi
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G,
+cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G, int32_t bm,
                         cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
+  if (bm == 64) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)gemm_smem<64>());
+    if (e != cudaSuccess) return e;
+    return launch_pdl(gemm_kernel<64>, dim3((unsigned)G), dim3(kGemmThreads), gemm_smem<64>(), stream, tmA, tmB, p);
+  }
+  if (bm != 128) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gemm_smem<128>());
   if (e != cudaSuccess) return e;
-  return launch_pdl(gemm_kernel, dim3((unsigned)G), dim3(kGemmThreads), kGemmSmem, stream, tmA, tmB, p);
+  return launch_pdl(gemm_kernel<128>, dim3((unsigned)G), dim3(kGemmThreads), gemm_smem<128>(), stream, tmA, tmB, p);
 }
 
 cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,
                             float* qscale, unsigned long long* thr, unsigned int* cnt, uint64_t* topk, int32_t kp,
-                            cudaStream_t stream) {
-  quantize_kernel<<<Mpad, 256, 0, stream>>>(q, M, d, dpad, A, qscale, thr, cnt, topk, kp);
+                            int32_t bm, cudaStream_t stream) {
+  if (bm == 64)
+    quantize_kernel<64><<<Mpad, 256, 0, stream>>>(q, M, d, dpad, A, qscale, thr, cnt, topk, kp);
+  else
+    quantize_kernel<128><<<Mpad, 256, 0, stream>>>(q, M, d, dpad, A, qscale, thr, cnt, topk, kp);
   return cudaGetLastError();
 }
 
 cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsigned long long* thr,
                           unsigned int* cnt, const uint64_t* cand, int32_t cap, uint64_t* out, unsigned int* err,
-                          cudaStream_t stream) {
+                          int32_t sm_count, cudaStream_t stream) {
   if (kp > 4096 || kp < k) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)2 * kp * 8;  // kept list + its order
-  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 4096 * 8);
+  // one wave of CTAs (a query each) stages its union in shared memory
+  const int cap_s = M <= sm_count ? 16384 : 0;
+  const size_t smem = (size_t)(2 * kp + cap_s) * 8;  // kept list + its order (+ the union)
+  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (2 * 4096 + 16384) * 8);
   if (e != cudaSuccess) return e;
-  return launch_pdl(select_kernel, dim3((unsigned)M), dim3(kSelThreads), smem, stream, k, kp, topk, thr, cnt, cand,
-                    cap, out, err);
+  return launch_pdl(select_kernel, dim3((unsigned)M), dim3(kSelThreads), smem, stream, k, kp, cap_s, topk, thr, cnt,
+                    cand, cap, out, err);
 }
 
 }  // namespace fi8

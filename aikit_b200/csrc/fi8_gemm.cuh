@@ -10,7 +10,7 @@
 
 namespace fi8 {
 
-constexpr int32_t kGemmBM = 128;  // queries per tile (TMEM lanes)
+constexpr int32_t kGemmBM = 128;  // largest query tile (TMEM lanes); 64 for batches of <= 64
 constexpr int32_t kGemmBN = 256;  // corpus rows per tile (MMA N)
 constexpr int32_t kGemmBK = 128;  // K bytes per pipeline stage (one 128B-swizzle row)
 
@@ -41,20 +41,21 @@ struct GemmParams {
 // (pitch a multiple of 16 bytes) with a {128 bytes, box_rows} box.
 bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pitch, uint32_t box_rows);
 
-cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G,
+// bm: the query tile (64 or 128); tmA's box must be bm rows.
+cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G, int32_t bm,
                         cudaStream_t stream);
 
 // Quantize M queries ([M][d] f32) into A ([Mpad][dpad] int8, zero padded) and
 // qscale ([Mpad]); also resets the per-query select state (thr, cnt, topk).
 cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,
                             float* qscale, unsigned long long* thr, unsigned int* cnt, uint64_t* topk, int32_t kp,
-                            cudaStream_t stream);
+                            int32_t bm, cudaStream_t stream);
 
 // Per query: top-k of (carried topk list [kp] U this range's candidates) ->
 // topk, thr = k-th best key (0 if fewer), cnt = 0; optionally out[q][k].
 cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsigned long long* thr,
                           unsigned int* cnt, const uint64_t* cand, int32_t cap, uint64_t* out, unsigned int* err,
-                          cudaStream_t stream);
+                          int32_t sm_count, cudaStream_t stream);
 
 int32_t select_max_k();
 
