@@ -57,9 +57,9 @@ def peaks():
 # dram__bytes_write.sum) next to that launch's algorithmic bytes; the ratio
 # scales the bench's average launch. Summaries: profiles/<kernel>_*.md.
 NCU_TRAFFIC = {
-    "gemm_kernel": {"dram_bytes": 1.341871e9 + 4.182016e6, "algorithmic_bytes": 1_737_856 * (DIM + 4) + 64 * DIM,
+    "gemm_kernel": {"dram_bytes": 734.708736e6 + 6.427392e6, "algorithmic_bytes": 951_424 * (DIM + 4) + 64 * DIM,
                     "profile": "profiles/gemm_kernel_c2_batch64.md"},
-    "scan_kernel": {"dram_bytes": 3.088212e9 + 4.358144e6, "algorithmic_bytes": 4_000_000 * (DIM + 4) + DIM * 4,
+    "scan_kernel": {"dram_bytes": 3.088071e9 + 3.871744e6, "algorithmic_bytes": 4_000_000 * (DIM + 4) + DIM * 4,
                     "profile": "profiles/scan_kernel_c2_batch1.md"},
     # binary (Hamming histogram) mode: 4M rows x 128-byte codes, plus the u16 distance written per row
     "scan_kernel_binary": {"dram_bytes": 512.031744e6 + 10.409216e6,
