@@ -501,7 +501,6 @@ __global__ void __launch_bounds__(kSelThreads)
   __shared__ int s_count;
   __shared__ unsigned long long s_prefix, s_mask, s_min;
   __shared__ unsigned int s_hist[kRadixBins];
-  __shared__ unsigned int s_total;
   __shared__ int s_rank, s_done;
   uint64_t* sel = reinterpret_cast<uint64_t*>(smem);  // [kp] the kept keys
   uint64_t* ranked = sel + kp;                          // [kp] their order (last range)
@@ -542,7 +541,6 @@ __global__ void __launch_bounds__(kSelThreads)
     s_rank = k;
     s_done = 0;
     s_count = 0;
-    s_total = 0;
   }
   __syncthreads();
   for (int shift = 56; shift >= 0; shift -= 8) {
@@ -580,7 +578,6 @@ __global__ void __launch_bounds__(kSelThreads)
       }
       const unsigned int total = __shfl_sync(0xffffffffu, incl, 31);
       const unsigned int rank = (unsigned int)s_rank;
-      if (shift == 56 && lane == 0) s_total = total;
       if (shift == 56 && total <= rank) {
         if (lane == 0) s_done = 2;  // k or fewer keys in all: keep them all
       } else {
@@ -649,12 +646,6 @@ __global__ void __launch_bounds__(kSelThreads)
     thr[qi] = nkept >= k ? s_min : 0ull;
     cnt[qi] = 0u;
   }
-}
-
-int pow2_ge(int x) {
-  int p = 1;
-  while (p < x) p <<= 1;
-  return p;
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
