@@ -30,6 +30,7 @@ SIGNATURES = {
     "fi8_ctx_create": (C.c_int, [C.c_int, _P]),
     "fi8_ctx_destroy": (C.c_int, [_P]),
     "fi8_ctx_sm_count": (C.c_int, [_P, _P]),
+    "fi8_probe_tensor_i8": (C.c_int, [_P, _I64, _P, _P]),
     "fi8_index_create": (C.c_int, [_P, _P, _P, _I64, _I32, _I64, _P]),
     "fi8_index_destroy": (C.c_int, [_P]),
     "fi8_index_info": (C.c_int, [_P, _P, _P]),

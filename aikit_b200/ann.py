@@ -74,6 +74,13 @@ class Context:
         check(lib().fi8_ctx_sm_count(self._h, C.byref(n)))
         return n.value
 
+    def probe_tensor_i8(self, iters: int = 20000) -> tuple[float, float]:
+        """The int8 tensor-pipe rate (ops/s) and the probe's ms (fi8_probe_tensor_i8)."""
+        ops = C.c_double(0.0)
+        ms = C.c_double(0.0)
+        check(lib().fi8_probe_tensor_i8(self._h, iters, C.byref(ops), C.byref(ms)))
+        return ops.value, ms.value
+
     def merge_keys_async(self, d_in: int, nsrc: int, M: int, k: int, d_out: int, stream: int = 0) -> None:
         """Top k per query of nsrc device key lists [nsrc][M][k] -> [M][k]."""
         check(lib().fi8_merge_keys_async(self._h, C.c_void_p(d_in), nsrc, M, k, C.c_void_p(d_out),

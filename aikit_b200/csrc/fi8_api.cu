@@ -259,6 +259,34 @@ int fi8_ctx_destroy(fi8_ctx* ctx) {
   return FI8_OK;
 }
 
+int fi8_probe_tensor_i8(fi8_ctx* ctx, int64_t iters, double* ops_per_s, double* ms) {
+  if (!ctx || !ops_per_s || !ms || iters <= 0) return fail(FI8_ERR_ARG, "fi8_probe_tensor_i8: bad arguments");
+  DeviceGuard g(ctx->device);
+  unsigned int* d_err = nullptr;
+  unsigned int h_err = 0;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaError_t e = cudaMalloc(&d_err, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(d_err, 0, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaEventCreate(&e0);
+  if (e == cudaSuccess) e = cudaEventCreate(&e1);
+  if (e == cudaSuccess) e = mma_probe_launch(ctx->sm_count, 1, d_err, nullptr);  // warm-up
+  if (e == cudaSuccess) e = cudaEventRecord(e0, nullptr);
+  if (e == cudaSuccess) e = mma_probe_launch(ctx->sm_count, iters, d_err, nullptr);
+  if (e == cudaSuccess) e = cudaEventRecord(e1, nullptr);
+  if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+  float dt = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&dt, e0, e1);
+  if (e == cudaSuccess) e = cudaMemcpy(&h_err, d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost);
+  cudaFree(d_err);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (e != cudaSuccess) return cuda_fail(e, "fi8_probe_tensor_i8");
+  if (h_err) return fail(FI8_ERR_DEVICE, "fi8_probe_tensor_i8: a bounded wait expired");
+  *ms = dt;
+  *ops_per_s = mma_probe_ops(ctx->sm_count, iters) / (dt * 1e-3);
+  return FI8_OK;
+}
+
 int fi8_ctx_sm_count(fi8_ctx* ctx, int* out) {
   if (!ctx || !out) return fail(FI8_ERR_ARG, "fi8_ctx_sm_count: null argument");
   *out = ctx->sm_count;

@@ -664,7 +664,70 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Tensor-pipe probe: back-to-back tcgen05.mma.kind::i8 (M=128, N=256, K=32)
+// on operands resident in shared memory (filled with a hash pattern, so the
+// multipliers toggle as on real data), accumulating into TMEM: no global
+// traffic, one issuing thread per SM. Each instruction is 2*128*256*32 ops.
+__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int64_t iters, unsigned int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t s_done;
+  __shared__ uint32_t s_tmem;
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x;
+  constexpr int kBytes = stage_bytes<128>();
+  for (int i = tid; i < kBytes / 4; i += blockDim.x) {
+    uint32_t h = (uint32_t)i * 0x9E3779B1u + blockIdx.x;
+    h ^= h >> 15;
+    h *= 0x85EBCA77u;
+    reinterpret_cast<uint32_t*>(smem)[i] = h ^ (h >> 13);
+  }
+  if (tid == 0) {
+    mbar_init(&s_done, 1);
+    fence_mbar_init();
+  }
+  if (tid < 32) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(256)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // the operands were written by ordinary stores; the tensor core reads them
+  // through the async proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  if (tid == 0) {
+    const uint32_t a_base = smem_u32(smem);
+    const uint32_t b_base = a_base + stage_a<128>();
+    for (int64_t i = 0; i < iters; i++) {
+#pragma unroll
+      for (int k = 0; k < kGemmBK / 32; k++)
+        umma_i8<128>(tmem, sw128_desc(a_base) + (uint64_t)(2 * k), sw128_desc(b_base) + (uint64_t)(2 * k),
+                     (i > 0 || k > 0) ? 1u : 0u);
+    }
+    umma_commit(&s_done);
+    if (!mbar_wait_bounded(&s_done, 0)) atomicOr(err, 1u);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid < 32) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+}
+
 }  // namespace
+
+cudaError_t mma_probe_launch(int32_t G, int64_t iters, unsigned int* err, cudaStream_t stream) {
+  const size_t smem = (size_t)stage_bytes<128>() + 1024;
+  cudaError_t e = cudaFuncSetAttribute(mma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  mma_probe_kernel<<<G, 128, smem, stream>>>(iters, err);
+  return cudaGetLastError();
+}
+
+double mma_probe_ops(int32_t G, int64_t iters) { return 2.0 * 128 * 256 * kGemmBK * (double)iters * G; }
 
 int32_t select_max_k() { return 4096; }  // kp <= 4096 keeps the select buffer at 64 KB
 

@@ -59,4 +59,9 @@ cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsi
 
 int32_t select_max_k();
 
+// Tensor-pipe probe: G CTAs (one per SM) issue iters x 4 back-to-back
+// kind::i8 MMAs (M=128, N=256, K=32) on shared-memory operands; ops done.
+cudaError_t mma_probe_launch(int32_t G, int64_t iters, unsigned int* err, cudaStream_t stream);
+double mma_probe_ops(int32_t G, int64_t iters);
+
 }  // namespace fi8

@@ -22,7 +22,7 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=100)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
-    ap.add_argument("--mode", choices=["topk", "score", "binary", "build"], default="topk")
+    ap.add_argument("--mode", choices=["topk", "score", "binary", "build", "probe"], default="topk")
     ap.add_argument("--recipe", choices=["mixture", "ties", "unit"], default="mixture",
                     help="corpus: C2/C3 mixture, C5 ties (codes in {-2..2}, scale 1/127), or iid unit rows")
     ap.add_argument("--over", type=int, default=100, help="binary mode: overquery (cand = k * over)")
@@ -39,6 +39,13 @@ def main() -> None:
         return binary_case(a, be)
     if a.mode == "build":
         return build_case(a, be)
+    if a.mode == "probe":
+        out = {"mode": "probe"}
+        for iters in (2000, 20000, 20000, 60000):
+            ops, ms = be.ctx.probe_tensor_i8(iters)
+            out.setdefault("runs", []).append({"iters": iters, "ms": round(ms, 3), "tops": round(ops / 1e12, 1)})
+        print(json.dumps(out))
+        return
     if a.recipe == "ties":
         r = synth.Recipe(synth.TIES, a.dim, seed=20265)
     elif a.recipe == "unit":

@@ -49,6 +49,13 @@ int fi8_ctx_destroy(fi8_ctx* ctx);
 /* Streaming-multiprocessor count of the context's device. */
 int fi8_ctx_sm_count(fi8_ctx* ctx, int* out);
 
+/* Measurement aid with no counterpart in the reference: the device's int8
+ * tensor-pipe rate. One CTA per SM issues iters x 4 back-to-back
+ * tcgen05.mma.kind::i8 (M=128, N=256, K=32) on shared-memory operands (no
+ * global traffic), timed with CUDA events: *ops_per_s (2 ops per
+ * multiply-add) and *ms. The roofline denominator for tensor-bound batches. */
+int fi8_probe_tensor_i8(fi8_ctx* ctx, int64_t iters, double* ops_per_s, double* ms);
+
 /* ann.Backend.NewI8Index (ann/backend.go:20; gpu/anncuda/backend.go:124-154).
  * Copies codes [n*dim] int8 row-major and scales [n] f32 to the device; the host
  * arrays are not retained (they may alias an mmap, ann/flat_i8_mmap.go:157-180).
