@@ -62,6 +62,7 @@ SIGNATURES = {
     "fi8_topk_batch_async_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _P]),
     "fi8_bin_query_topk_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _P]),
     "fi8_bin_prefilter_async_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _I32, _P]),
+    "fi8_bin_set_tensor_prefilter": (C.c_int, [_P, _I32]),
 }
 
 

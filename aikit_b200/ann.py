@@ -390,6 +390,13 @@ class BinaryI8Index:
         check(lib().fi8_index_read_rows(self._ih, _p(bq), _p(sc)))
         return bq, sc
 
+    def set_tensor_prefilter(self, min_batch: int) -> None:
+        """Prefilter batches of at least min_batch queries on the tensor cores
+        (the codes unpacked to +1/-1 int8 rows on the device, n x dim bytes
+        more HBM); 0 frees the rows and keeps every batch on the popcount
+        pass. The shortlist is the same either way."""
+        check(lib().fi8_bin_set_tensor_prefilter(self._h, int(min_batch)))
+
     def Query(self, q, k: int) -> list[Hit]:
         """FlatBinaryI8.Query (flat_binary_i8.go:78) for one query."""
         return self.QueryBatch([q], k)[0]

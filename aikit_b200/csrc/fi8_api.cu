@@ -606,8 +606,17 @@ static void plan_ranges(int64_t n, int32_t k, int32_t cap, std::vector<GemmLevel
   }
 }
 
-static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
-                            cudaStream_t st) {
+// The corpus side of a batched top-k GEMM: FlatI8's int8 rows scored W8A8, or
+// a binary index's sign rows (+1/-1 per code bit) scored by -Hamming distance.
+struct GemmCorpus {
+  const CUtensorMap* tmB;  // [n_alloc][dpad] int8 rows, 256-row boxes
+  const float* scales;     // W8A8: the row scales; null in Hamming mode
+  const float* center;     // Hamming mode: the prefilter's centre (null: none)
+  int32_t ham_dim;         // > 0: Hamming mode over this many bits
+};
+
+static int launch_topk_gemm(fi8_index* x, const GemmCorpus& corpus, const float* d_q, int32_t M, int32_t k,
+                            uint64_t* d_keys, cudaStream_t st) {
   if (k > select_max_k())
     return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d beyond the device top-K)", k);
   const int32_t kp = pow2_ge_host(k);
@@ -632,9 +641,12 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
     x->tmA_box = bm;
   }
   cudaEvent_t t0 = timer_begin(x, st);
-  cudaError_t e = quantize_launch(d_q, M, Mpad, x->dim, x->dpad, x->d_A, x->d_qscale, x->d_thr, x->d_cnt,
-                                  x->d_topk, kp, bm, st);
-  if (e != cudaSuccess) return cuda_fail(e, "quantize_launch");
+  const bool ham = corpus.ham_dim > 0;
+  cudaError_t e = ham ? sign_prep_launch(d_q, M, Mpad, x->dim, x->dpad, corpus.center, x->d_A, x->d_qscale,
+                                         x->d_thr, x->d_cnt, x->d_topk, kp, bm, st)
+                      : quantize_launch(d_q, M, Mpad, x->dim, x->dpad, x->d_A, x->d_qscale, x->d_thr, x->d_cnt,
+                                        x->d_topk, kp, bm, st);
+  if (e != cudaSuccess) return cuda_fail(e, ham ? "sign_prep_launch" : "quantize_launch");
   timer_end(x, st, t0, FI8_KERNEL_QUANTIZE, (double)M * x->dim * 4 + (double)Mpad * x->dpad);
   x->last_launches++;
   std::vector<GemmLevel> ranges;
@@ -644,7 +656,8 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
   p.M = M;
   p.qtiles = Mpad / bm;
   p.id_base = x->id_base;
-  p.scales = x->d_scales;
+  p.scales = corpus.scales;
+  p.ham_dim = corpus.ham_dim;
   p.qscale = x->d_qscale;
   p.thr = x->d_thr;
   p.cnt = x->d_cnt;
@@ -661,11 +674,11 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
     const int64_t units = (int64_t)p.qtiles * p.rtiles;
     const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(x->sm_count, units));
     t0 = timer_begin(x, st);
-    e = gemm_launch(x->tmA, x->tmB, p, G, bm, st);
+    e = gemm_launch(x->tmA, *corpus.tmB, p, G, bm, st);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_launch");
-    // the range's codes and scales, plus the int8 query tile
+    // the range's rows (and scales), plus the int8 query tile
     timer_end(x, st, t0, FI8_KERNEL_GEMM,
-              (double)(p.row_hi - p.row_lo) * (x->dim + 4) + (double)M * x->dim);
+              (double)(p.row_hi - p.row_lo) * (x->dim + (ham ? 0 : 4)) + (double)M * x->dim);
     const bool last = (i + 1 == ranges.size());
     t0 = timer_begin(x, st);
     e = select_launch(M, k, kp, x->d_topk, x->d_thr, x->d_cnt, x->d_cand, cap, last ? d_keys : nullptr,
@@ -680,7 +693,8 @@ static int launch_topk_gemm(fi8_index* x, const float* d_q, int32_t M, int32_t k
 static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
                        cudaStream_t st) {
   x->last_launches = 0;
-  if (M >= x->gemm_min_batch && x->has_tmB) return launch_topk_gemm(x, d_q, M, k, d_keys, st);
+  if (M >= x->gemm_min_batch && x->has_tmB)
+    return launch_topk_gemm(x, GemmCorpus{&x->tmB, x->d_scales, nullptr, 0}, d_q, M, k, d_keys, st);
   return launch_topk_scan(x, d_q, M, k, d_keys, st);
 }
 
@@ -1060,6 +1074,11 @@ struct fi8_bin {
   size_t parts_cap = 0;
   uint64_t* d_short = nullptr;  // [M][cand] shortlist keys (host entry point)
   size_t short_cap = 0;
+  // tensor-core prefilter (fi8_bin_set_tensor_prefilter): the codes unpacked
+  // to +1/-1 int8 rows, so a batch's Hamming distances are one kind::i8 GEMM
+  int8_t* d_sign = nullptr;     // [n_alloc][dpad]; 0 past dim and for rows >= n
+  CUtensorMap tmS;              // over d_sign, 256-row boxes
+  int32_t tensor_min_m = 0;     // batches of at least this many queries use it (0: off)
 };
 
 namespace {
@@ -1076,6 +1095,14 @@ constexpr int32_t kBinMaxM = 16;
 static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
                                 bool sorted, cudaStream_t st) {
   fi8_index* x = b->ix;
+  if (b->d_sign && b->tensor_min_m > 0 && M >= b->tensor_min_m) {
+    // The shortlist is the cand best rows under (distance asc, id asc); as
+    // packed keys (-distance, id) that is the exact top-cand the GEMM path
+    // selects, sorted descending (so it also serves a key merge).
+    if (cand > kBinMaxCand)
+      return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond %d)", cand, kBinMaxCand);
+    return launch_topk_gemm(x, GemmCorpus{&b->tmS, nullptr, b->d_center, x->dim}, d_q, M, cand, d_keys, st);
+  }
   const int32_t bpad = b->wpad * 8;
   const int32_t nbins = bpad * 8 + 1;
   ScanGeometry geo;
@@ -1312,9 +1339,39 @@ int fi8_bin_index_destroy(fi8_bin* b) {
     cudaFree(b->d_counts);
     cudaFree(b->d_parts);
     cudaFree(b->d_short);
+    cudaFree(b->d_sign);
     fi8_index_destroy(b->ix);
   }
   delete b;
+  return FI8_OK;
+}
+
+int fi8_bin_set_tensor_prefilter(fi8_bin* b, int32_t min_batch) {
+  if (!b || min_batch < 0) return fail(FI8_ERR_ARG, "fi8_bin_set_tensor_prefilter: bad arguments");
+  fi8_index* x = b->ix;
+  std::lock_guard<std::mutex> lk(x->mu);
+  DeviceGuard g(x->device);
+  FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+  if (min_batch == 0) {
+    cudaFree(b->d_sign);
+    b->d_sign = nullptr;
+    b->tensor_min_m = 0;
+    return FI8_OK;
+  }
+  if (!b->d_sign) {
+    FI8_CUDA(cudaMalloc(&b->d_sign, (size_t)x->n_alloc * x->dpad), "gpu: sign rows allocation");
+    cudaError_t e = sign_rows_launch(b->d_bits, x->n, x->n_alloc, b->wpad, x->dim, x->dpad, b->d_sign, x->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
+    if (e == cudaSuccess && !make_tmap_i8(&b->tmS, b->d_sign, (uint64_t)x->n_alloc, (uint64_t)x->dpad,
+                                          (uint32_t)kGemmBN))
+      e = cudaErrorInvalidValue;
+    if (e != cudaSuccess) {
+      cudaFree(b->d_sign);
+      b->d_sign = nullptr;
+      return cuda_fail(e, "gpu: sign rows build failed");
+    }
+  }
+  b->tensor_min_m = min_batch;
   return FI8_OK;
 }
 

@@ -274,6 +274,31 @@ __global__ void __launch_bounds__(kSegThreads) shortlist_emit_kernel(const uint1
   }
 }
 
+// The sign rows of the tensor-core prefilter: a thread per 16 output bytes
+// (16 code bits), one 16-byte store each.
+__global__ void __launch_bounds__(256) sign_rows_kernel(const uint64_t* bits, int64_t n, int64_t n_alloc, int wpad,
+                                                        int d, int dpad, int8_t* rows) {
+  const int chunks = dpad >> 4;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n_alloc * chunks) return;
+  const int64_t r = t / chunks;
+  const int i0 = (int)(t % chunks) << 4;
+  const uint32_t w = r < n ? (uint32_t)(bits[(size_t)r * wpad + (i0 >> 6)] >> (i0 & 63)) & 0xFFFFu : 0u;
+  uint32_t o[4];
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+      const int i = i0 + 4 * g + b;
+      const uint32_t byte = (r < n && i < d) ? (((w >> (4 * g + b)) & 1u) ? 0x01u : 0xFFu) : 0u;
+      v |= byte << (8 * b);
+    }
+    o[g] = v;
+  }
+  reinterpret_cast<uint4*>(rows + (size_t)r * dpad)[i0 >> 4] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // One CTA per query: sort its cand keys descending (for the cross-shard merge).
 __global__ void __launch_bounds__(1024) sort_keys_kernel(uint64_t* keys, int cand, int candp) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -408,6 +433,15 @@ cudaError_t shortlist_launch(const uint16_t* dist, int64_t n, int64_t dstride, i
   e = cudaFuncSetAttribute(sort_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRerankMaxCand * 8);
   if (e != cudaSuccess) return e;
   return launch_pdl(sort_keys_kernel, dim3((unsigned)M), dim3(1024), (size_t)candp * 8, stream, out, cand, candp);
+}
+
+cudaError_t sign_rows_launch(const uint64_t* bits, int64_t n, int64_t n_alloc, int32_t wpad, int32_t d, int32_t dpad,
+                             int8_t* rows, cudaStream_t stream) {
+  if (dpad % 16 != 0 || dpad > wpad * 64 || n > n_alloc) return cudaErrorInvalidValue;
+  const int64_t threads = n_alloc * (dpad / 16);
+  if (threads == 0) return cudaSuccess;
+  sign_rows_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(bits, n, n_alloc, wpad, d, dpad, rows);
+  return cudaGetLastError();
 }
 
 int32_t rerank_parts(int32_t cand) { return (cand + kRerankRowsPerCta - 1) / kRerankRowsPerCta; }

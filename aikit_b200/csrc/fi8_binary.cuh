@@ -41,6 +41,12 @@ cudaError_t rerank_launch(const float* q, int32_t M, int32_t d, int32_t dpad, co
                           const float* scales, int64_t n, uint32_t id_base, const uint64_t* shortlist,
                           int32_t cand, int32_t k, uint64_t* parts, uint64_t* out, cudaStream_t stream);
 
+// The codes unpacked for the tensor-core prefilter: rows[r][i] = +1 where bit
+// i of row r's code is set, -1 where it is clear (i < d), 0 for i >= d and
+// for rows r >= n (n_alloc rows of dpad bytes; dpad a multiple of 16).
+cudaError_t sign_rows_launch(const uint64_t* bits, int64_t n, int64_t n_alloc, int32_t wpad, int32_t d, int32_t dpad,
+                             int8_t* rows, cudaStream_t stream);
+
 // Largest shortlist (cand) the shortlist sort and the rerank support.
 constexpr int32_t kRerankMaxCand = 4096;
 

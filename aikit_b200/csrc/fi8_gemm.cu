@@ -158,7 +158,7 @@ __device__ __forceinline__ void flush_staged(const GemmParams& p, int q, const u
     if (pos < (unsigned int)p.cap) dst[pos] = stage[j];
 }
 
-template <int BM>
+template <int BM, bool HAM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
   constexpr int kStageA = stage_a<BM>();
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int cq = ew >> 2;
     const int r = quarter * 32 + lane;  // A row / TMEM lane of this thread
     float* const my_scale = &s_scale[ew][0][0];
-    if (my_units > 0) {
+    if (!HAM && my_units > 0) {
       const int64_t row0 = p.row_lo + ((int64_t)blockIdx.x / p.qtiles) * kGemmBN;
       cp_async8(my_scale + 2 * lane, p.scales + row0 + cq * 64 + 2 * lane);
     }
@@ -296,6 +296,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* const my_stage = s_stage[ew * 32 + lane];
     int staged = 0;  // candidates held in my_stage, not yet in the global list
     float qs = 0.0f, Tscore = INFINITY;
+    // Hamming mode: the filter in accumulator units -- a row passes iff its
+    // dot >= hthr (always inside [-ham_dim, ham_dim + 1], so hthr - 1 - dot
+    // cannot overflow)
+    int32_t hthr = 0;
     unsigned long long T = ~0ull;
     for (int64_t u = 0; u < my_units; u++) {
       const int64_t unit = blockIdx.x + u * G;
@@ -319,13 +323,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // above pass, i.e. scores >= the next float up. With no threshold
         // yet (T == 0) every non-NaN score passes, -inf included.
         Tscore = !valid_q ? INFINITY : (T == 0ull) ? -INFINITY : nextafterf(key_score(T), INFINITY);
+        // scores are the integers (dot - ham_dim) / 2: score > T's score s
+        // <=> dot >= ham_dim + 2 (s + 1)
+        if (HAM)
+          hthr = !valid_q ? p.ham_dim + 1
+                 : (T == 0ull) ? -p.ham_dim
+                               : p.ham_dim + 2 * ((int32_t)key_score(T) + 1);
       }
       if (s_abort) break;
       // this unit's scales (copied during the previous unit) have landed;
       // start the copy of the next unit's into the other slot
       cp_async_wait_all();
       __syncwarp();
-      if (u + 1 < my_units) {
+      if (!HAM && u + 1 < my_units) {
         const int64_t nrow0 = p.row_lo + ((unit + G) / p.qtiles) * kGemmBN;
         cp_async8(my_scale + (b ^ 1) * 64 + 2 * lane, p.scales + nrow0 + cq * 64 + 2 * lane);
       }
@@ -347,20 +357,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // semantics) score whenever it is not NaN, and NaN never passes. The
         // score replaces the accumulator in v for the append below.
         uint32_t mask = 0;
-        const float4* s4 = reinterpret_cast<const float4*>(scl);
+        if (HAM) {
+          // Hamming mode: A and B hold +1/-1 per sign bit (0 past dim), so
+          // the dot is dim - 2h. The filter is an integer compare: the sign
+          // bit of hthr - 1 - dot, shifted into the mask (one funnel shift);
+          // v keeps the dots and survivors get their scores when appended.
+          const int32_t tm1 = hthr - 1;
 #pragma unroll
-        for (int i4 = 0; i4 < 8; i4++) {
-          const float4 rs = s4[i4];
-          const float rsv[4] = {rs.x, rs.y, rs.z, rs.w};
+          for (int i = 31; i >= 0; i--) mask = __funnelshift_l((uint32_t)(tm1 - (int32_t)v[i]), mask, 1);
+        } else {
+          const float4* s4 = reinterpret_cast<const float4*>(scl);
 #pragma unroll
-          for (int t = 0; t < 4; t++) {
-            const int i = i4 * 4 + t;
-            const float sc = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), rsv[t]);
-            v[i] = __float_as_uint(sc);
-            mask |= (sc >= Tscore ? 1u : 0u) << i;
+          for (int i4 = 0; i4 < 8; i4++) {
+            const float4 rs = s4[i4];
+            const float rsv[4] = {rs.x, rs.y, rs.z, rs.w};
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+              const int i = i4 * 4 + t;
+              const float sc = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), rsv[t]);
+              v[i] = __float_as_uint(sc);
+              mask |= (sc >= Tscore ? 1u : 0u) << i;
+            }
           }
         }
-        if (qs == 0.0f) {  // an all-zero query scores exactly 0
+        if (!HAM && qs == 0.0f) {  // an all-zero query scores exactly 0
           mask = (0.0f >= Tscore) ? 0xFFFFFFFFu : 0u;
 #pragma unroll
           for (int i = 0; i < 32; i++) v[i] = 0u;
@@ -399,8 +419,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               for (int t = 0; t < 4; t++) {
                 if ((nib >> t) & 1u) {
                   const int i = 4 * g + t;
-                  const uint64_t key = make_key(__uint_as_float(v[i]), id0 + (uint32_t)i);
-                  if (pos < room) dst[pos] = key > T ? key : kEmptyKey;
+                  const float sc = HAM ? __int2float_rn(((int32_t)v[i] - p.ham_dim) >> 1) : __uint_as_float(v[i]);
+                  const uint64_t key = make_key(sc, id0 + (uint32_t)i);
+                  // (Hamming survivors score above T's score, so their keys
+                  // always beat T)
+                  if (pos < room) dst[pos] = (HAM || key > T) ? key : kEmptyKey;
                   pos++;
                 }
               }
@@ -473,6 +496,42 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* q, int M, in
   for (int i = tid; i < kp; i += blockDim.x) topk[(size_t)qi * kp + i] = kEmptyKey;
 }
 
+// One CTA per A row, as quantize_kernel: the query's sign row for the
+// Hamming mode (the packing rule of binary_prep_kernel, as +1/-1 bytes).
+template <int BM>
+__global__ void __launch_bounds__(256) sign_prep_kernel(const float* q, int M, int d, int dpad, const float* center,
+                                                        int8_t* A, float* qscale, unsigned long long* thr,
+                                                        unsigned int* cnt, uint64_t* topk, int kp) {
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int qt = row / BM;
+  const int m_t = min(BM, M - qt * BM);
+  const int j = arow_query<BM>(row % BM, m_t);
+  int8_t* dst = A + (size_t)row * dpad;
+  if (j < 0 || j >= m_t) {  // no query at this row
+    for (int i = tid; i < dpad; i += blockDim.x) dst[i] = 0;
+    if (tid == 0) qscale[row] = 0.0f;
+    return;
+  }
+  const int qi = qt * BM + j;
+  const float* src = q + (size_t)qi * d;
+  for (int i = tid; i < dpad; i += blockDim.x) {
+    int8_t sgn = 0;
+    if (i < d) {
+      float x = src[i];
+      if (center) x = __fsub_rn(x, center[i]);
+      sgn = x >= 0.0f ? (int8_t)1 : (int8_t)-1;  // NaN compares false: -1
+    }
+    dst[i] = sgn;
+  }
+  if (tid == 0) {
+    qscale[row] = 1.0f;
+    thr[qi] = 0ull;
+    cnt[qi] = 0u;
+  }
+  for (int i = tid; i < kp; i += blockDim.x) topk[(size_t)qi * kp + i] = kEmptyKey;
+}
+
 // One CTA of 512 threads per query: fold this range's candidates into the
 // running top-k. The carried list holds keys of earlier ranges (all above the
 // threshold the candidates passed), so top-k of the union is exact.
@@ -485,7 +544,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* q, int M, in
 // many queries' CTAs share an SM and a large batch selects in one wave. Only
 // the last range's select orders its keys (its output is the answer).
 constexpr int kSelThreads = 512;
-constexpr int kSelUnroll = 4;
+constexpr int kSelUnroll = 8;
 constexpr int kRadixBins = 256;
 
 // Slot i of a query's union: its carried list, then this range's candidates.
@@ -499,7 +558,7 @@ __global__ void __launch_bounds__(kSelThreads)
                   const uint64_t* cand, int cap, uint64_t* out, unsigned int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_count;
-  __shared__ unsigned long long s_prefix, s_mask, s_min;
+  __shared__ unsigned long long s_prefix, s_mask, s_min, s_and, s_or;
   __shared__ unsigned int s_hist[kRadixBins];
   __shared__ int s_rank, s_done;
   uint64_t* sel = reinterpret_cast<uint64_t*>(smem);  // [kp] the kept keys
@@ -538,15 +597,30 @@ __global__ void __launch_bounds__(kSelThreads)
     s_prefix = 0ull;
     s_mask = 0ull;
     s_min = ~0ull;
+    s_and = ~0ull;
+    s_or = 0ull;
     s_rank = k;
     s_done = 0;
     s_count = 0;
   }
   __syncthreads();
+  // The first pass also ANDs and ORs every key: a later digit that all keys
+  // share is appended to the prefix without a pass (score images and row ids
+  // leave several bytes constant across a union).
   for (int shift = 56; shift >= 0; shift -= 8) {
+    if (shift < 56 && (unsigned int)((s_and ^ s_or) >> shift & 0xFFull) == 0u) {
+      __syncthreads();  // every thread has read s_and / s_or
+      if (tid == 0) {
+        s_prefix |= s_and & (0xFFull << shift);
+        s_mask |= 0xFFull << shift;
+      }
+      __syncthreads();
+      continue;
+    }
     if (tid < kRadixBins) s_hist[tid] = 0u;
     __syncthreads();
     const unsigned long long prefix = s_prefix, mask = s_mask;
+    unsigned long long k_and = ~0ull, k_or = 0ull;
     for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
       uint64_t keys[kSelUnroll];  // loads first, so their L2 latencies overlap
 #pragma unroll
@@ -558,6 +632,20 @@ __global__ void __launch_bounds__(kSelThreads)
         const unsigned int bin = live ? (unsigned int)(key >> shift) & 0xFFu : 0x100u;
         const unsigned int same = __match_any_sync(0xffffffffu, bin);
         if (live && lane == __ffs(same) - 1) atomicAdd(&s_hist[bin], (unsigned int)__popc(same));
+        if (shift == 56 && live) {
+          k_and &= key;
+          k_or |= key;
+        }
+      }
+    }
+    if (shift == 56) {
+      const unsigned int a_lo = __reduce_and_sync(0xffffffffu, (unsigned int)k_and);
+      const unsigned int a_hi = __reduce_and_sync(0xffffffffu, (unsigned int)(k_and >> 32));
+      const unsigned int o_lo = __reduce_or_sync(0xffffffffu, (unsigned int)k_or);
+      const unsigned int o_hi = __reduce_or_sync(0xffffffffu, (unsigned int)(k_or >> 32));
+      if (lane == 0) {
+        atomicAnd(&s_and, ((unsigned long long)a_hi << 32) | a_lo);
+        atomicOr(&s_or, ((unsigned long long)o_hi << 32) | o_lo);
       }
     }
     __syncthreads();
@@ -606,6 +694,7 @@ __global__ void __launch_bounds__(kSelThreads)
   // keep every non-empty key at or above the prefix (exactly min(total, k))
   const unsigned long long prefix = s_done == 2 ? 0ull : s_prefix;
   const unsigned long long mask = s_done == 2 ? 0ull : s_mask;
+  unsigned long long my_min = ~0ull;
   for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
     uint64_t keys[kSelUnroll];
 #pragma unroll
@@ -614,10 +703,16 @@ __global__ void __launch_bounds__(kSelThreads)
     for (int u = 0; u < kSelUnroll; u++) {
       const uint64_t key = keys[u];
       const bool take = key != kEmptyKey && (key & mask) >= prefix;
-      if (take) atomicMin(&s_min, (unsigned long long)key);
+      if (take && key < my_min) my_min = key;
       warp_append(take, key, sel, &s_count);
     }
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, my_min, off);
+    if (o < my_min) my_min = o;
+  }
+  if (lane == 0 && my_min != ~0ull) atomicMin(&s_min, my_min);
   __syncthreads();
   const int nkept = s_count;
   const uint64_t* kept = sel;
@@ -743,19 +838,22 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pi
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <int BM, bool HAM>
+static cudaError_t gemm_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G,
+                                 cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BM, HAM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gemm_smem<BM>());
+  if (e != cudaSuccess) return e;
+  return launch_pdl(gemm_kernel<BM, HAM>, dim3((unsigned)G), dim3(kGemmThreads), gemm_smem<BM>(), stream, tmA, tmB,
+                    p);
+}
+
 cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G, int32_t bm,
                         cudaStream_t stream) {
-  if (bm == 64) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gemm_smem<64>());
-    if (e != cudaSuccess) return e;
-    return launch_pdl(gemm_kernel<64>, dim3((unsigned)G), dim3(kGemmThreads), gemm_smem<64>(), stream, tmA, tmB, p);
-  }
+  const bool ham = p.ham_dim > 0;
+  if (bm == 64) return ham ? gemm_launch_t<64, true>(tmA, tmB, p, G, stream) : gemm_launch_t<64, false>(tmA, tmB, p, G, stream);
   if (bm != 128) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)gemm_smem<128>());
-  if (e != cudaSuccess) return e;
-  return launch_pdl(gemm_kernel<128>, dim3((unsigned)G), dim3(kGemmThreads), gemm_smem<128>(), stream, tmA, tmB, p);
+  return ham ? gemm_launch_t<128, true>(tmA, tmB, p, G, stream) : gemm_launch_t<128, false>(tmA, tmB, p, G, stream);
 }
 
 cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,
@@ -765,6 +863,16 @@ cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, 
     quantize_kernel<64><<<Mpad, 256, 0, stream>>>(q, M, d, dpad, A, qscale, thr, cnt, topk, kp);
   else
     quantize_kernel<128><<<Mpad, 256, 0, stream>>>(q, M, d, dpad, A, qscale, thr, cnt, topk, kp);
+  return cudaGetLastError();
+}
+
+cudaError_t sign_prep_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, const float* center,
+                             int8_t* A, float* qscale, unsigned long long* thr, unsigned int* cnt, uint64_t* topk,
+                             int32_t kp, int32_t bm, cudaStream_t stream) {
+  if (bm == 64)
+    sign_prep_kernel<64><<<Mpad, 256, 0, stream>>>(q, M, d, dpad, center, A, qscale, thr, cnt, topk, kp);
+  else
+    sign_prep_kernel<128><<<Mpad, 256, 0, stream>>>(q, M, d, dpad, center, A, qscale, thr, cnt, topk, kp);
   return cudaGetLastError();
 }
 

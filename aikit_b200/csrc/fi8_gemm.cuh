@@ -25,7 +25,10 @@ struct GemmParams {
   int32_t qtiles;        // ceil(M / 128)
   int64_t rtiles;        // 256-row tiles in [row_lo, row_hi)
   uint32_t id_base;      // global id of corpus row 0
-  const float* scales;   // [n_alloc] row scales
+  const float* scales;   // [n_alloc] row scales (W8A8 mode)
+  int32_t ham_dim;       // > 0: Hamming mode -- A and B are +1/-1 sign rows
+                         // (0 past ham_dim) and a row's score is -(Hamming
+                         // distance) = (dot - ham_dim) / 2; 0: W8A8 scores
   const float* qscale;   // [Mpad] query scales
   const unsigned long long* thr;  // [M] per-query threshold key (0 = none)
   unsigned int* cnt;     // [M] candidates appended this range
@@ -50,6 +53,13 @@ cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Ge
 cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,
                             float* qscale, unsigned long long* thr, unsigned int* cnt, uint64_t* topk, int32_t kp,
                             int32_t bm, cudaStream_t stream);
+
+// The Hamming mode's A: query j's sign row, +1 where q[j][i] - center[i] >= 0
+// in float32 (center may be null), -1 elsewhere (NaN included), 0 past d;
+// qscale 1 (0 for rows without a query); the select state reset as above.
+cudaError_t sign_prep_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, const float* center,
+                             int8_t* A, float* qscale, unsigned long long* thr, unsigned int* cnt, uint64_t* topk,
+                             int32_t kp, int32_t bm, cudaStream_t stream);
 
 // Per query: top-k of (carried topk list [kp] U this range's candidates) ->
 // topk, thr = k-th best key (0 if fewer), cnt = 0; optionally out[q][k].

@@ -26,6 +26,8 @@ def main() -> None:
     ap.add_argument("--recipe", choices=["mixture", "ties", "unit"], default="mixture",
                     help="corpus: C2/C3 mixture, C5 ties (codes in {-2..2}, scale 1/127), or iid unit rows")
     ap.add_argument("--over", type=int, default=100, help="binary mode: overquery (cand = k * over)")
+    ap.add_argument("--tensor", type=int, default=0,
+                    help="binary mode: prefilter batches of at least this many queries on the tensor cores")
     ap.add_argument("--trace", action="store_true",
                     help="also report per-kernel device time (torch.profiler / CUPTI) over the reps")
     a = ap.parse_args()
@@ -120,6 +122,9 @@ def binary_case(a, be) -> None:
     ctr = r.center(a.rows)
     bits, q8, sc = r.binary(a.rows, ctr)
     bix = be.NewBinaryI8Index(bits, bits.shape[1], ctr, q8, sc, a.rows, a.dim, a.over)
+    del q8, sc
+    if a.tensor:
+        bix.set_tensor_prefilter(a.tensor)
     cand = a.k * a.over
     Q = torch.from_numpy(r.queries(a.batch)).cuda()
     short = torch.zeros((a.batch, cand), dtype=torch.int64, device="cuda")
@@ -141,7 +146,8 @@ def binary_case(a, be) -> None:
     bix.sync()
     gbs = [a.batch * a.rows * bits.shape[1] * 8 / (t * 1e-3) / 1e9 for t in times]
     out = {"mode": "binary", "rows": a.rows, "dim": a.dim, "k": a.k, "cand": cand, "batch": a.batch,
-           "ms": times, "codes_gbs_per_pass": gbs}
+           "tensor_min_batch": a.tensor, "ms": times, "codes_gbs_per_pass": gbs,
+           "queries_per_s": [a.batch / (t * 1e-3) for t in times]}
     if a.trace:  # per kernel class, from the library's CUDA events
         warm = max(a.reps - 1, 1)
         out["kernels"] = {k: {"launches_per_rep": v["launches"] / warm, "us_per_rep": v["ms"] * 1e3 / warm}

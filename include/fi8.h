@@ -232,6 +232,16 @@ int fi8_bin_read_codes(fi8_bin* b, uint64_t* codes);
  * launch counts. */
 int fi8_bin_index_handle(fi8_bin* b, fi8_index** out);
 
+/* Tensor-core prefilter for query batches (no reference counterpart; the
+ * result is the same shortlist). min_batch > 0 unpacks the codes on the
+ * device into +1/-1 int8 rows (n x dim bytes, rounded up to 16, held until
+ * min_batch = 0 or destroy; built once) and sends every prefilter of at least
+ * min_batch queries through the tcgen05 kind::i8 GEMM: the dot of two sign
+ * rows is dim - 2 * distance, so the batch's distances are one matrix
+ * product, and the epilogue selects each query's cand nearest rows under
+ * (distance, id) exactly. Smaller batches keep the popcount pass. */
+int fi8_bin_set_tensor_prefilter(fi8_bin* b, int32_t min_batch);
+
 /* FlatBinaryI8.Query for M queries (ann/flat_binary_i8.go:86-109): q [M*dim]
  * host f32; out_idx/out_score [M*k], as fi8_topk_batch. With cand = k *
  * overquery: when cand >= n this is FlatI8's exact top-k (:95-97); otherwise
