@@ -377,6 +377,8 @@ BIN_ROWS = 4_000_000   # sample of C4's 25M-row per-GPU shard (C4: 2e8 rows over
 BIN_DIM = 1024
 BIN_K = 10
 BIN_OVER = 100         # cand = K * over = 1000, BASELINE's shortlist
+BIN_BATCH = 512        # C4's batch form
+BIN_TENSOR_MIN = 16    # batches of at least this many queries prefilter on the tensor cores
 
 
 def binary_leg(be, args, stream, pk, pk_kind, local):
@@ -455,8 +457,93 @@ def binary_leg(be, args, stream, pk, pk_kind, local):
         "clocks": clk.summary(),
         "cpu_baseline": binary_cpu_baseline(bits, ctr, Qh, r),
     }
+    out["batch512"] = binary_batch_leg(be, bix, r, args, stream, local)
     bix.Close()
     return out
+
+
+def binary_batch_leg(be, bix, r, args, stream, local):
+    """C4's batch form on the same shard: 512 queries per step, the prefilter
+    as one tcgen05 kind::i8 GEMM over the codes unpacked to +1/-1 int8 rows
+    (dot = dim - 2 * distance), then the rerank. Tensor-bound: the roofline is
+    the GEMM's int8 ops against our own tcgen05 probe's measured peak."""
+    import torch
+    from aikit_b200.ann import unpack_keys
+    M, cand = BIN_BATCH, BIN_K * BIN_OVER
+    peak_ops, probe_ms = be.ctx.probe_tensor_i8(60000)
+    t0 = time.perf_counter()
+    bix.set_tensor_prefilter(BIN_TENSOR_MIN)
+    sign_s = time.perf_counter() - t0
+    nb = 2
+    Qh = r.queries(nb * M, row0=4096).reshape(nb, M, BIN_DIM)
+    Qd = torch.from_numpy(Qh).cuda()
+    short = torch.zeros((M, cand), dtype=torch.int64, device="cuda")
+    keys = torch.zeros((M, BIN_K), dtype=torch.int64, device="cuda")
+    st = stream.cuda_stream
+
+    def step(i):
+        bix.prefilter_async(Qd[i % nb].data_ptr(), M, cand, short.data_ptr(), st, sorted_keys=False)
+        n = bix.last_launch_count()
+        bix.rerank_async(Qd[i % nb].data_ptr(), M, short.data_ptr(), cand, BIN_K, keys.data_ptr(), st)
+        return n + bix.last_launch_count()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    bix.sync()
+
+    def timed(kernel_events):
+        bix.kernel_times(reset=True)
+        bix.set_kernel_timing(kernel_events)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        n_launch = 0
+        for i in range(args.steps):
+            n_launch += step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        bix.set_kernel_timing(False)
+        return ev0.elapsed_time(ev1), n_launch, bix.kernel_times(reset=True)
+
+    with ClockSampler(local) as clk:
+        ms, launches, _ = timed(False)
+        ms_ev, _, kt = timed(True)
+    bix.sync()
+    gidx, _ = unpack_keys(keys.cpu().numpy().view(np.uint64))
+    assert (gidx >= 0).all(), "binary batch top-K came back short"
+    # e2e: the host entry point (fi8_bin_query_topk) with a pinned batch
+    Qpin = torch.from_numpy(Qh.copy()).pin_memory().numpy()
+    bix.topk_arrays(Qpin[0], BIN_K)
+    t1 = time.perf_counter()
+    for i in range(args.steps):
+        bix.topk_arrays(Qpin[i % nb], BIN_K)
+    e2e_s = time.perf_counter() - t1
+    gemm = kt["gemm_kernel"]
+    gemm_ms = gemm["ms"] / args.steps
+    ops = 2.0 * M * BIN_ROWS * BIN_DIM  # every row once per step, over the ranges
+    achieved = ops / (gemm_ms / 1e3)
+    return {
+        "metric": "FlatBinaryI8 top-K queries/sec, batch 512", "value": M * args.steps / (ms / 1e3),
+        "unit": "queries/s", "ms_per_step": ms / args.steps,
+        "dtype": "int8 +1/-1 sign rows (int32 accumulate) + int8 rerank",
+        "config": {"workload": f"C4 batch form: {M} queries per step, d={BIN_DIM}, K={BIN_K}, cand {cand}, "
+                               f"{BIN_ROWS:,} rows; prefilter batches of >= {BIN_TENSOR_MIN} on the tensor cores",
+                   "sign_rows_bytes": BIN_ROWS * BIN_DIM, "sign_rows_build_s": round(sign_s, 3)},
+        "roofline": {"bound": "tensor", "achieved": achieved / 1e12, "peak": peak_ops / 1e12, "unit": "TOPS",
+                     "frac": achieved / peak_ops, "traffic": None, "kernel": "gemm_kernel (Hamming mode)",
+                     "launches": gemm["launches"], "ms_per_step": gemm_ms,
+                     "algorithmic_ops_per_step": ops,
+                     "hbm_view_gbs": BIN_ROWS * BIN_DIM / (gemm_ms / 1e3) / 1e9,
+                     "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
+                     "peak_source": f"fi8_probe_tensor_i8 measured live ({probe_ms:.1f} ms of back-to-back "
+                                    "kind::i8 MMAs on all SMs); MEASURED_PEAKS.json has no int8 figure"},
+        "gpu_launches": launches,
+        "e2e": {"value": M * args.steps / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": M * BIN_DIM * 4,
+                "d2h_bytes_per_step": M * BIN_K * 8, "api": "fi8_bin_query_topk (include/fi8.h), pinned host batch"},
+        "clocks": clk.summary(),
+    }
 
 
 def binary_cpu_baseline(bits, ctr, Qh, r, budget_s: float = 6.0):
