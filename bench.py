@@ -65,6 +65,10 @@ NCU_TRAFFIC = {
     "scan_kernel_binary": {"dram_bytes": 512.031744e6 + 10.409216e6,
                            "algorithmic_bytes": 4_000_000 * 128 + 128 + 2 * 4_000_000,
                            "profile": "profiles/scan_kernel_binary_c4.md"},
+    # Hamming-mode GEMM (tensor-core prefilter), batch 512: 737,856 sign rows of 1024 B, plus the query tile
+    "gemm_kernel_ham": {"dram_bytes": 756.334080e6 + 11.297024e6,
+                        "algorithmic_bytes": 737_856 * 1024 + 512 * 1024,
+                        "profile": "profiles/gemm_kernel_ham_c4_batch512.md"},
 }
 
 
@@ -524,6 +528,9 @@ def binary_batch_leg(be, bix, r, args, stream, local):
     gemm_ms = gemm["ms"] / args.steps
     ops = 2.0 * M * BIN_ROWS * BIN_DIM  # every row once per step, over the ranges
     achieved = ops / (gemm_ms / 1e3)
+    ncu = NCU_TRAFFIC["gemm_kernel_ham"]
+    step_bytes = BIN_ROWS * BIN_DIM + M * BIN_DIM
+    traffic = step_bytes * ncu["dram_bytes"] / ncu["algorithmic_bytes"]
     return {
         "metric": "FlatBinaryI8 top-K queries/sec, batch 512", "value": M * args.steps / (ms / 1e3),
         "unit": "queries/s", "ms_per_step": ms / args.steps,
@@ -532,7 +539,10 @@ def binary_batch_leg(be, bix, r, args, stream, local):
                                f"{BIN_ROWS:,} rows; prefilter batches of >= {BIN_TENSOR_MIN} on the tensor cores",
                    "sign_rows_bytes": BIN_ROWS * BIN_DIM, "sign_rows_build_s": round(sign_s, 3)},
         "roofline": {"bound": "tensor", "achieved": achieved / 1e12, "peak": peak_ops / 1e12, "unit": "TOPS",
-                     "frac": achieved / peak_ops, "traffic": None, "kernel": "gemm_kernel (Hamming mode)",
+                     "frac": achieved / peak_ops, "traffic": traffic, "traffic_unit": "bytes per step",
+                     "traffic_source": f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
+                                       "times this step's sign-row bytes",
+                     "kernel": "gemm_kernel (Hamming mode)",
                      "launches": gemm["launches"], "ms_per_step": gemm_ms,
                      "algorithmic_ops_per_step": ops,
                      "hbm_view_gbs": BIN_ROWS * BIN_DIM / (gemm_ms / 1e3) / 1e9,
