@@ -317,6 +317,12 @@ class I8Index:
         from ._ffi import FI8_OPT_GEMM_MIN_BATCH
         check(lib().fi8_index_set_option(self._h, FI8_OPT_GEMM_MIN_BATCH, m))
 
+    def set_gemm_ctas(self, ctas: int) -> None:
+        """Cap the batched GEMM's persistent CTAs (0: one per SM), leaving SMs
+        free for work that overlaps it (an NCCL collective of another batch)."""
+        from ._ffi import FI8_OPT_GEMM_CTAS
+        check(lib().fi8_index_set_option(self._h, FI8_OPT_GEMM_CTAS, ctas))
+
     def _queries(self, queries) -> np.ndarray:
         if isinstance(queries, np.ndarray) and queries.ndim == 2:
             Q = _f32(queries)

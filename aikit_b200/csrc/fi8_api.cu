@@ -166,6 +166,7 @@ struct fi8_index {
   uint64_t* d_topk = nullptr;
   size_t topk_cap = 0;
   int32_t gemm_min_batch = 2;  // batches of at least this many queries use the GEMM path
+  int32_t gemm_ctas = 0;       // cap on the GEMM's persistent CTAs (0: one per SM)
   int32_t last_launches = 0;   // kernels launched by the last query call
 
   // keep filter of the call in progress (QueryFilter), null when none
@@ -682,7 +683,8 @@ static int launch_topk_gemm(fi8_index* x, const GemmCorpus& corpus, const float*
     p.rtiles = (p.row_hi - p.row_lo + kGemmBN - 1) / kGemmBN;
     p.producer_waits = i == 0 ? 1 : 0;  // the first range follows the quantize kernel
     const int64_t units = (int64_t)p.qtiles * p.rtiles;
-    const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(x->sm_count, units));
+    const int32_t ctas = x->gemm_ctas > 0 ? std::min(x->gemm_ctas, x->sm_count) : x->sm_count;
+    const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(ctas, units));
     t0 = timer_begin(x, st);
     e = gemm_launch(x->tmA, *corpus.tmB, p, G, bm, st);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_launch");
@@ -881,6 +883,10 @@ int fi8_index_set_option(fi8_index* idx, int option, int64_t value) {
     case FI8_OPT_KERNEL_TIMING:
       if (value != 0 && value != 1) return fail(FI8_ERR_ARG, "fi8_index_set_option: KERNEL_TIMING is 0 or 1");
       idx->timing = value != 0;
+      return FI8_OK;
+    case FI8_OPT_GEMM_CTAS:
+      if (value < 0) return fail(FI8_ERR_ARG, "fi8_index_set_option: GEMM_CTAS must be >= 0");
+      idx->gemm_ctas = (int32_t)std::min<int64_t>(value, 1 << 30);
       return FI8_OK;
     default:
       return fail(FI8_ERR_ARG, "fi8_index_set_option: unknown option %d", option);

@@ -31,16 +31,30 @@ def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
 
 class ShardedTopK:
     """TopKBatch over a row-sharded FlatI8: this rank's I8Index (built with
-    id_base = its first global row) plus the cross-rank merge."""
+    id_base = its first global row) plus the cross-rank merge.
 
-    def __init__(self, index, ctx, world: int, stream, group=None):
+    overlap=True pipelines consecutive batches: the all-gather and merge of a
+    batch run on a second (communication) stream while the next batch's scan
+    runs on `stream`. The GEMM then leaves `free_sms` SMs to the collective's
+    kernel (FI8_OPT_GEMM_CTAS), and two buffer slots alternate, so a result
+    stays valid until the call after next. `wait()` orders `stream` after
+    all communication issued so far."""
+
+    def __init__(self, index, ctx, world: int, stream, group=None, overlap: bool = False, free_sms: int = 2):
         import torch
         self.ix, self.ctx, self.world, self.stream, self.group = index, ctx, world, stream, group
         self._torch = torch
         self._bufs = {}
+        self.overlap = overlap and world > 1
+        self.comm = None
+        self._slot = 0
+        self._done = [None, None]  # per slot: the event after its last all-gather and merge
+        if self.overlap:
+            self.comm = torch.cuda.Stream()
+            index.set_gemm_ctas(max(1, ctx.sm_count() - free_sms))
 
-    def _buffers(self, M: int, k: int):
-        key = (M, k)
+    def _buffers(self, M: int, k: int, slot: int = 0):
+        key = (M, k, slot)
         if key not in self._bufs:
             t = self._torch
             self._bufs[key] = (t.zeros((M, k), dtype=t.int64, device="cuda"),
@@ -49,9 +63,13 @@ class ShardedTopK:
         return self._bufs[key]
 
     def topk_async(self, d_q: int, M: int, k: int):
-        """Device keys [M][k] of the global top-k (stream-ordered, no sync).
-        Every rank must call it with the same M and k."""
+        """Device keys [M][k] of the global top-k (stream-ordered, no sync;
+        with overlap, ordered on the communication stream: call wait() before
+        reading them on `stream`). Every rank must call it with the same M
+        and k."""
         import torch.distributed as dist
+        if self.overlap:
+            return self._topk_overlapped(d_q, M, k)
         local, gathered, merged = self._buffers(M, k)
         st = self.stream.cuda_stream
         self.ix.topk_async(d_q, M, k, local.data_ptr(), st)
@@ -61,6 +79,32 @@ class ShardedTopK:
             dist.all_gather_into_tensor(gathered.view(-1), local.view(-1), group=self.group)
         self.ctx.merge_keys_async(gathered.data_ptr(), self.world, M, k, merged.data_ptr(), st)
         return merged
+
+    def _topk_overlapped(self, d_q: int, M: int, k: int):
+        import torch.distributed as dist
+        t = self._torch
+        slot = self._slot
+        self._slot ^= 1
+        local, gathered, merged = self._buffers(M, k, slot)
+        if self._done[slot] is not None:
+            # this slot's previous all-gather has read `local` before the scan rewrites it
+            self.stream.wait_event(self._done[slot])
+        self.ix.topk_async(d_q, M, k, local.data_ptr(), self.stream.cuda_stream)
+        scanned = t.cuda.Event()
+        scanned.record(self.stream)
+        self.comm.wait_event(scanned)
+        with t.cuda.stream(self.comm):
+            dist.all_gather_into_tensor(gathered.view(-1), local.view(-1), group=self.group)
+        self.ctx.merge_keys_async(gathered.data_ptr(), self.world, M, k, merged.data_ptr(), self.comm.cuda_stream)
+        done = t.cuda.Event()
+        done.record(self.comm)
+        self._done[slot] = done
+        return merged
+
+    def wait(self) -> None:
+        """Order `stream` after every all-gather and merge issued so far."""
+        if self.comm is not None:
+            self.stream.wait_stream(self.comm)
 
 
 class ShardedBinary:

@@ -138,6 +138,12 @@ int fi8_topk_batch_async_keep(fi8_index* idx, const float* d_q, int32_t M, int32
  * 0 (default) records nothing. A measurement aid with no counterpart in the
  * reference. */
 #define FI8_OPT_KERNEL_TIMING 2
+/* FI8_OPT_GEMM_CTAS: the batched GEMM's persistent grid uses at most this many
+ * CTAs, one per SM (0, the default: every SM). No counterpart in the
+ * reference. A multi-GPU caller that overlaps the NCCL all-gather of one batch
+ * with the next batch's GEMM leaves a few SMs free for the collective's
+ * kernel; results are identical. */
+#define FI8_OPT_GEMM_CTAS 3
 int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
 
 /* Kernel classes reported by fi8_index_kernel_times. */

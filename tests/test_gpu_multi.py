@@ -58,6 +58,24 @@ def _worker(rank, world, port, results):
                 for m in range(M):
                     i, s = oracle.flat_i8_query(bq, bs, Q[m], k)
                     ok &= gi[m].tolist() == list(i) and gs[m].tobytes() == np.asarray(s, np.float32).tobytes()
+        # pipelined batches: each all-gather + merge on a second stream beside
+        # the next batch's scan, two result slots alternating
+        sho = ShardedTopK(ix, be.ctx, world, stream, overlap=True)
+        M = 24
+        Qs = [r.queries(M, row0=100 + 50 * b) for b in range(3)]
+        outs = []
+        for b in range(3):
+            qd = torch.from_numpy(Qs[b]).cuda()
+            outs.append((qd, sho.topk_async(qd.data_ptr(), M, k)))
+        sho.wait()
+        stream.synchronize()
+        ix.sync()
+        for b in (1, 2):  # batch 0's slot was reused by batch 2
+            gi, gs = unpack_keys(outs[b][1].cpu().numpy().view(np.uint64))
+            if rank == 0:
+                for m in range(0, M, 5):
+                    i, s = oracle.flat_i8_query(bq, bs, Qs[b][m], k)
+                    ok &= gi[m].tolist() == list(i) and gs[m].tobytes() == np.asarray(s, np.float32).tobytes()
         ix.Close()
         # FlatBinaryI8 with the global shortlist
         d, n, k, over = 512, 40000, 10, 30
