@@ -880,9 +880,8 @@ cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsi
                           unsigned int* cnt, const uint64_t* cand, int32_t cap, uint64_t* out, unsigned int* err,
                           int32_t sm_count, cudaStream_t stream) {
   if (kp > 4096 || kp < k) return cudaErrorInvalidValue;
-  // one wave of CTAs (a query each) stages its union in shared memory: room
-  // for a 16K-row first range (every row a candidate) plus the carried list
-  const int cap_s = M <= sm_count ? 16384 + (kp <= 1024 ? kp : 0) : 0;
+  // one wave of CTAs (a query each) stages its union in shared memory
+  const int cap_s = M <= sm_count ? 16384 : 0;
   const size_t smem = (size_t)(2 * kp + cap_s) * 8;  // kept list + its order (+ the union)
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (2 * 4096 + 16384) * 8);
