@@ -64,6 +64,9 @@ SIGNATURES = {
     "fi8_bin_query_topk_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _P]),
     "fi8_bin_prefilter_async_keep": (C.c_int, [_P, _P, _I32, _I32, _P, _I64, _P, _I32, _P]),
     "fi8_bin_set_tensor_prefilter": (C.c_int, [_P, _I32]),
+    "fi8_index_create_empty": (C.c_int, [_P, _I64, _I32, _I64, _P]),
+    "fi8_index_upload_rows": (C.c_int, [_P, _I64, _P, _P, _I64]),
+    "fi8_index_upload_finish": (C.c_int, [_P]),
 }
 
 

@@ -128,6 +128,14 @@ class B200Backend:
         check(lib().fi8_index_create_f32(self.ctx.handle, _p(v), v.shape[0], v.shape[1], id_base, C.byref(h)))
         return I8Index._adopt(self.ctx, h, v.shape[0], v.shape[1], id_base)
 
+    def NewI8IndexEmpty(self, n: int, dim: int, id_base: int = 0) -> "I8Index":
+        """An index of n all-zero rows to fill with I8Index.upload_rows
+        (fi8_index_create_empty): the device path of a paged or streamed
+        corpus, which never has to be resident on the host as a whole."""
+        h = C.c_void_p()
+        check(lib().fi8_index_create_empty(self.ctx.handle, n, dim, id_base, C.byref(h)))
+        return I8Index._adopt(self.ctx, h, n, dim, id_base)
+
     def NewBinaryI8IndexFromFloats(self, vecs, overquery: int = 16, centered: bool = True, center=None,
                                    valid=None, id_base: int = 0) -> "BinaryI8Index":
         """newFlatBinaryI8 on the device (fi8_bin_index_create_f32): the FlatI8
@@ -193,6 +201,20 @@ class I8Index:
         sc = np.empty(self.n, np.float32)
         check(lib().fi8_index_read_rows(self._h, _p(bq), _p(sc)))
         return bq, sc
+
+    def upload_rows(self, row0: int, codes, scales) -> None:
+        """Copy rows [row0, row0 + len(scales)) to the device
+        (fi8_index_upload_rows); the host arrays may be dropped on return."""
+        c = np.ascontiguousarray(codes, dtype=np.int8).reshape(-1)
+        s = _f32(scales).reshape(-1)
+        rows = s.shape[0]
+        if c.shape[0] != rows * self.dim:
+            raise Fi8Error(1, f"fi8_index_upload_rows: {c.shape[0]} codes for {rows} rows of dim {self.dim}")
+        check(lib().fi8_index_upload_rows(self._h, row0, _p(c), _p(s), rows))
+
+    def upload_finish(self) -> None:
+        """Wait for every upload_rows copy and free the staging buffers."""
+        check(lib().fi8_index_upload_finish(self._h))
 
     # -- I8Index ---------------------------------------------------------
     def Score(self, q: Sequence[float], dst: np.ndarray) -> None:

@@ -169,6 +169,10 @@ struct fi8_index {
   int32_t gemm_ctas = 0;       // cap on the GEMM's persistent CTAs (0: one per SM)
   int32_t last_launches = 0;   // kernels launched by the last query call
 
+  // incremental uploads (fi8_index_upload_rows): the pinned double buffer,
+  // held from the first upload until fi8_index_upload_finish or destroy
+  PinnedStager* up_stage = nullptr;
+
   // keep filter of the call in progress (QueryFilter), null when none
   const uint64_t* cur_keep = nullptr;
   int64_t cur_keep_nbits = 0;
@@ -297,6 +301,7 @@ int fi8_ctx_sm_count(fi8_ctx* ctx, int* out) {
 static void index_free(fi8_index* x) {
   DeviceGuard g(x->device);
   if (x->stream) cudaStreamSynchronize(x->stream);
+  delete x->up_stage;  // waits for its last copies, frees the pinned buffers
   cudaFree(x->d_codes);
   cudaFree(x->d_scales);
   cudaFree(x->d_gthr);
@@ -438,6 +443,62 @@ int fi8_index_create_f32(fi8_ctx* ctx, const float* vecs, int64_t n, int32_t dim
     return rc;
   }
   *out = x;
+  return FI8_OK;
+}
+
+int fi8_index_create_empty(fi8_ctx* ctx, int64_t n, int32_t dim, int64_t id_base, fi8_index** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_index_create_empty: null out");
+  *out = nullptr;
+  fi8_index* x = nullptr;
+  int rc = index_alloc(ctx, n, dim, id_base, "fi8_index_create_empty", &x);
+  if (rc != FI8_OK) return rc;
+  if ((rc = index_finish(x)) != FI8_OK) {
+    index_free(x);
+    return rc;
+  }
+  *out = x;
+  return FI8_OK;
+}
+
+int fi8_index_upload_rows(fi8_index* idx, int64_t row0, const int8_t* codes, const float* scales, int64_t rows) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_index_upload_rows: null index");
+  if (rows == 0) return FI8_OK;
+  if (rows < 0 || row0 < 0 || row0 + rows > idx->n || !codes || !scales)
+    return fail(FI8_ERR_ARG, "fi8_index_upload_rows: rows [%lld, %lld) outside [0, %lld) or null data",
+                (long long)row0, (long long)(row0 + rows), (long long)idx->n);
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  if (!idx->up_stage) {
+    idx->up_stage = new (std::nothrow) PinnedStager;
+    if (!idx->up_stage) return fail(FI8_ERR_OOM, "fi8_index_upload_rows: host allocation");
+    cudaError_t e = idx->up_stage->init();
+    if (e != cudaSuccess) {
+      delete idx->up_stage;
+      idx->up_stage = nullptr;
+      return cuda_fail(e, "gpu: pinned staging buffers");
+    }
+  }
+  // put_rows has read the host rows when it returns (they are copied into
+  // the pinned buffers); the DMA from those buffers drains on the stream
+  cudaError_t e = idx->up_stage->put_rows(idx->d_codes + (size_t)row0 * idx->dpad, idx->dpad, codes, idx->dim,
+                                          idx->dim, rows, idx->stream);
+  if (e == cudaSuccess)
+    e = idx->up_stage->put_rows(idx->d_scales + row0, 4, scales, 4, 4, rows, idx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "gpu: device upload failed");
+  return FI8_OK;
+}
+
+int fi8_index_upload_finish(fi8_index* idx) {
+  if (!idx) return fail(FI8_ERR_ARG, "fi8_index_upload_finish: null index");
+  std::lock_guard<std::mutex> lk(idx->mu);
+  DeviceGuard g(idx->device);
+  if (idx->up_stage) {
+    cudaError_t e = idx->up_stage->finish();
+    delete idx->up_stage;
+    idx->up_stage = nullptr;
+    if (e != cudaSuccess) return cuda_fail(e, "gpu: device upload failed");
+  }
+  FI8_CUDA(cudaStreamSynchronize(idx->stream), "gpu: device upload failed");
   return FI8_OK;
 }
 

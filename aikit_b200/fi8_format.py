@@ -73,6 +73,53 @@ def load_mmap(path: str):
     return load(mm)
 
 
+# Rows per paging block: about 1 MiB of codes (pagedBlockRows,
+# ann/flat_i8_mmap.go:46-56).
+PAGED_BLOCK_BYTES = 1 << 20
+
+
+def paged_block_rows(dim: int) -> int:
+    return max(PAGED_BLOCK_BYTES // dim, 1) if dim > 0 else 1
+
+
+def upload_paged(backend, path: str, block_rows: int = 0, id_base: int = 0):
+    """EnableGPU for a paged index (LoadFlatI8MmapPaged, ann/flat_i8_mmap.go:
+    75-102): map the blob read-only and walk its blocks in order, uploading
+    each block's rows (fi8_index_upload_rows) and then releasing its pages
+    from the process (MADV_DONTNEED on the clean, file-backed mapping), so a
+    corpus larger than host RAM reaches the device with about one block
+    resident at a time. Returns the device index (an aikit_b200.ann.I8Index)."""
+    with open(path, "rb") as fh:
+        if os.fstat(fh.fileno()).st_size == 0:
+            raise FormatError("ann: FlatI8 blob: truncated reading magic")
+        mm = mmap.mmap(fh.fileno(), 0, access=mmap.ACCESS_READ)
+    try:
+        dim, n, at = layout(mm)
+        if n == 0:
+            raise FormatError("ann: FlatI8 blob holds no rows")
+        rows = block_rows if block_rows > 0 else paged_block_rows(dim)
+        codes = np.frombuffer(mm, dtype=np.int8, count=n * dim, offset=at)
+        scales = np.frombuffer(mm, dtype="<f4", count=n, offset=at + n * dim)
+        ix = backend.NewI8IndexEmpty(n, dim, id_base=id_base)
+        page = mmap.PAGESIZE
+        for r0 in range(0, n, rows):
+            r1 = min(r0 + rows, n)
+            ix.upload_rows(r0, codes[r0 * dim:r1 * dim], scales[r0:r1].astype(np.float32))
+            # the block's whole pages are no longer needed on the host
+            lo = -(-(at + r0 * dim) // page) * page
+            hi = (at + r1 * dim) // page * page
+            if hasattr(mmap, "MADV_DONTNEED") and hi > lo:
+                mm.madvise(mmap.MADV_DONTNEED, lo, hi - lo)
+        ix.upload_finish()
+        del codes, scales
+        return ix
+    finally:
+        try:
+            mm.close()
+        except BufferError:  # a view is still alive; the mapping closes with it
+            pass
+
+
 def dumps(codes: np.ndarray, scales: np.ndarray) -> bytes:
     """MarshalBinary (ann/flat_i8_persist.go:48-72)."""
     codes = np.ascontiguousarray(codes, dtype=np.int8)

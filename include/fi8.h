@@ -74,6 +74,27 @@ int fi8_index_create(fi8_ctx* ctx, const int8_t* codes, const float* scales, int
 int fi8_index_create_f32(fi8_ctx* ctx, const float* vecs, int64_t n, int32_t dim, int64_t id_base,
                          fi8_index** out);
 
+/* Paged and streamed sources: the device path of a paged FlatI8
+ * (LoadFlatI8MmapPaged, ann/flat_i8_mmap.go:75-102), whose codes may exceed
+ * host RAM and which the reference refuses to put on a device
+ * (ann/backend.go:162, errPagedGPU at :366). The adapter creates an empty
+ * index, then walks the pager's blocks in order -- Touch a block, upload its
+ * rows, let the pager evict it -- so only a block or two is resident on the
+ * host at a time, and the device ends up holding the whole corpus.
+ * fi8_index_create_empty: n rows of dim, all zero (a row not yet uploaded
+ * scores 0). fi8_index_upload_rows: rows [row0, row0 + rows) from host codes
+ * [rows*dim] and scales [rows]; the host memory may be released as soon as the
+ * call returns (the rows are already in pinned staging buffers), and the copies
+ * drain on the index's stream, overlapping the caller's next block.
+ * fi8_index_upload_finish: wait for every upload and free the staging buffers
+ * (two 64 MB pinned buffers, allocated by the first upload_rows). Call it
+ * before device-resident queries on other streams; the host-pointer entry
+ * points are ordered after the uploads anyway. Uploading every row gives the
+ * index fi8_index_create would build from the same rows. */
+int fi8_index_create_empty(fi8_ctx* ctx, int64_t n, int32_t dim, int64_t id_base, fi8_index** out);
+int fi8_index_upload_rows(fi8_index* idx, int64_t row0, const int8_t* codes, const float* scales, int64_t rows);
+int fi8_index_upload_finish(fi8_index* idx);
+
 /* Copy an index's rows back to the host: codes [n*dim] int8 and scales [n]
  * (e.g. to fill FlatI8's bq and scales after a device build). */
 int fi8_index_read_rows(fi8_index* idx, int8_t* codes, float* scales);

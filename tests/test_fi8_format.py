@@ -90,3 +90,12 @@ def test_embedded_corpus_fixture():
         assert idx[0] <= row and q[idx[0]].tobytes() == q[row].tobytes()
         if idx[0] != row:
             assert row in idx.tolist() and sc[idx.tolist().index(row)] == sc[0]
+
+
+def test_paged_block_rows_follow_the_reference():
+    """pagedBlockRows (ann/flat_i8_mmap.go:46-56): about 1 MiB of codes per
+    block, at least one row."""
+    assert fi8_format.paged_block_rows(1024) == 1024
+    assert fi8_format.paged_block_rows(768) == (1 << 20) // 768
+    assert fi8_format.paged_block_rows(1 << 21) == 1
+    assert fi8_format.paged_block_rows(0) == 1
