@@ -373,10 +373,88 @@ def main():
         out["batch1"] = {"value": 1e3 / per1, "unit": "queries/s", "ms_per_query": per1,
                          "roofline": kernel_roofline(kt1, "scan_kernel", pk, pk_kind, ms1_ev)}
     if world == 1:
-        out["flat_binary"] = binary_leg(be, args, stream, pk, pk_kind, local)
+        peak_ops, probe_ms = be.ctx.probe_tensor_i8(60000)  # the int8 tensor roofline, measured live
+        tensor_peak = (peak_ops, probe_ms)
+        out["c3_sample"] = c3_leg(be, args, stream, local, tensor_peak)
+        out["flat_binary"] = binary_leg(be, args, stream, pk, pk_kind, local, tensor_peak)
         out["cpu_baseline"] = cpu_baseline()
     print(json.dumps(out))
     return 0
+
+
+# ----------------------------------------------------------------------------
+# C3 row shape, tensor-bound batch: a row sample of the 50M-row corpus
+# ----------------------------------------------------------------------------
+C3_ROWS = 4_000_000   # a sample of C3's 50M rows (6.25M per GPU at 8)
+C3_DIM = 1024
+C3_K = 100
+C3_BATCH = 4096
+
+
+def c3_leg(be, args, stream, local, tensor_peak):
+    """TopKBatch of 4096 queries (C3's large batch) over a 4M-row sample of
+    the C3 corpus recipe (10,000 clusters, sigma 0.25, d = 1024, K = 100). The
+    GEMM is tensor-bound here: the roofline is its int8 ops against our own
+    tcgen05 probe's measured peak."""
+    import torch
+    from aikit_b200 import synth
+    from aikit_b200.ann import unpack_keys
+    r = synth.Recipe(synth.MIXTURE, C3_DIM, seed=SEED + 3, ncl=10000, sigma=0.25)
+    bq, bs = r.codes(C3_ROWS)
+    ix = be.NewI8Index(bq, bs, C3_ROWS, C3_DIM)
+    del bq, bs
+    Q = torch.from_numpy(r.queries(C3_BATCH)).cuda()
+    keys = torch.zeros((C3_BATCH, C3_K), dtype=torch.int64, device="cuda")
+    st = stream.cuda_stream
+    steps = max(3, min(args.steps, 5))  # each step is ~15 ms of tensor work
+
+    def step():
+        ix.topk_async(Q.data_ptr(), C3_BATCH, C3_K, keys.data_ptr(), st)
+        return ix.last_launch_count()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ix.sync()
+
+    def timed(kernel_events):
+        ix.kernel_times(reset=True)
+        ix.set_kernel_timing(kernel_events)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        n_launch = sum(step() for _ in range(steps))
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ix.set_kernel_timing(False)
+        return ev0.elapsed_time(ev1), n_launch, ix.kernel_times(reset=True)
+
+    with ClockSampler(local) as clk:
+        ms, launches, _ = timed(False)
+        _, _, kt = timed(True)
+    ix.sync()
+    gidx, _ = unpack_keys(keys.cpu().numpy().view(np.uint64))
+    assert (gidx >= 0).all(), "C3 top-K came back short"
+    ix.Close()
+    peak_ops, probe_ms = tensor_peak
+    gemm_ms = kt["gemm_kernel"]["ms"] / steps
+    ops = 2.0 * C3_BATCH * C3_ROWS * C3_DIM
+    achieved = ops / (gemm_ms / 1e3)
+    return {
+        "metric": "FlatI8 exact top-K queries/sec, batch 4096", "value": C3_BATCH * steps / (ms / 1e3),
+        "unit": "queries/s", "ms_per_step": ms / steps, "steps": steps,
+        "config": {"workload": f"C3 row shape: {C3_ROWS:,}-row sample of the 50M-row mixture (10,000 clusters, "
+                               f"sigma 0.25), d={C3_DIM}, K={C3_K}, batch {C3_BATCH}",
+                   "l2": "codes 4.1 GB > 126 MB L2"},
+        "roofline": {"bound": "tensor", "achieved": achieved / 1e12, "peak": peak_ops / 1e12, "unit": "TOPS",
+                     "frac": achieved / peak_ops, "traffic": None, "kernel": "gemm_kernel (W8A8)",
+                     "gemm_ms_per_step": gemm_ms, "algorithmic_ops_per_step": ops,
+                     "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
+                     "peak_source": f"fi8_probe_tensor_i8 measured live ({probe_ms:.1f} ms)"},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
 
 
 # ----------------------------------------------------------------------------
@@ -390,7 +468,7 @@ BIN_BATCH = 512        # C4's batch form
 BIN_TENSOR_MIN = 16    # batches of at least this many queries prefilter on the tensor cores
 
 
-def binary_leg(be, args, stream, pk, pk_kind, local):
+def binary_leg(be, args, stream, pk, pk_kind, local, tensor_peak):
     """Batch-1 FlatBinaryI8 queries on a C4-shaped shard: device-resident
     prefilter + rerank timed on the device, then the host entry point."""
     import torch
@@ -466,12 +544,12 @@ def binary_leg(be, args, stream, pk, pk_kind, local):
         "clocks": clk.summary(),
         "cpu_baseline": binary_cpu_baseline(bits, ctr, Qh, r),
     }
-    out["batch512"] = binary_batch_leg(be, bix, r, args, stream, local)
+    out["batch512"] = binary_batch_leg(be, bix, r, args, stream, local, tensor_peak)
     bix.Close()
     return out
 
 
-def binary_batch_leg(be, bix, r, args, stream, local):
+def binary_batch_leg(be, bix, r, args, stream, local, tensor_peak):
     """C4's batch form on the same shard: 512 queries per step, the prefilter
     as one tcgen05 kind::i8 GEMM over the codes unpacked to +1/-1 int8 rows
     (dot = dim - 2 * distance), then the rerank. Tensor-bound: the roofline is
@@ -479,7 +557,7 @@ def binary_batch_leg(be, bix, r, args, stream, local):
     import torch
     from aikit_b200.ann import unpack_keys
     M, cand = BIN_BATCH, BIN_K * BIN_OVER
-    peak_ops, probe_ms = be.ctx.probe_tensor_i8(60000)
+    peak_ops, probe_ms = tensor_peak
     t0 = time.perf_counter()
     bix.set_tensor_prefilter(BIN_TENSOR_MIN)
     sign_s = time.perf_counter() - t0
