@@ -460,7 +460,7 @@ def c3_leg(be, args, stream, local, tensor_peak):
 # ----------------------------------------------------------------------------
 # FlatBinaryI8 (C4 row shape): sign-bit Hamming prefilter + int8 rerank
 # ----------------------------------------------------------------------------
-BIN_ROWS = 4_000_000   # sample of C4's 25M-row per-GPU shard (C4: 2e8 rows over 8 GPUs)
+BIN_ROWS = 25_000_000  # C4's per-GPU shard (C4: 2e8 rows over 8 GPUs)
 BIN_DIM = 1024
 BIN_K = 10
 BIN_OVER = 100         # cand = K * over = 1000, BASELINE's shortlist
@@ -469,7 +469,7 @@ BIN_TENSOR_MIN = 16    # batches of at least this many queries prefilter on the 
 
 
 def binary_leg(be, args, stream, pk, pk_kind, local, tensor_peak):
-    """Batch-1 FlatBinaryI8 queries on a C4-shaped shard: device-resident
+    """Batch-1 FlatBinaryI8 queries on C4's per-GPU shard: device-resident
     prefilter + rerank timed on the device, then the host entry point."""
     import torch
     from aikit_b200 import synth
@@ -533,8 +533,9 @@ def binary_leg(be, args, stream, pk, pk_kind, local, tensor_peak):
         "ms_per_query": ms / args.steps, "dtype": "u64 popcount + int8 rerank",
         "config": {"workload": f"C4 row shape: d={BIN_DIM} sign codes (128 B) of centred N(0,1) rows + int8 "
                                f"copies, K={BIN_K}, overquery {BIN_OVER} (cand {cand}), batch 1, "
-                               f"{BIN_ROWS:,} rows (a sample of C4's 25M-row per-GPU shard)",
-                   "n_rows": BIN_ROWS, "codes_bytes": int(bits.nbytes), "l2": "codes 512 MB > 126 MB L2",
+                               f"{BIN_ROWS:,} rows (C4's per-GPU shard of 200M rows over 8 GPUs)",
+                   "n_rows": BIN_ROWS, "codes_bytes": int(bits.nbytes),
+                   "l2": f"codes {bits.nbytes / 1e9:.1f} GB > 126 MB L2",
                    "corpus_gen_s": round(gen_s, 1)},
         "roofline": dict(kernel_roofline(kt, "scan_kernel", pk, pk_kind, ms_ev, ncu_key="scan_kernel_binary"),
                          kernel_events_pass_ms_per_query=ms_ev / args.steps),
