@@ -293,6 +293,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // per-query state of the current query tile (constant within a launch)
     // (a lane without a query gets qs = 0 and Tscore = +inf: it never passes)
     int cur_qt = -1, q = 0;
+    // Whether this lane holds a query of the current tile. With 64-query
+    // tiles the M = 64 MMA writes TMEM lanes 0-15 of each sub-partition only,
+    // so the other lanes read stale accumulators: their mask must be empty
+    // whatever those values are (their q is not a query index).
+    bool lane_valid = false;
     uint64_t* const my_stage = s_stage[ew * 32 + lane];
     int staged = 0;  // candidates held in my_stage, not yet in the global list
     float qs = 0.0f, Tscore = INFINITY;
@@ -314,6 +319,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int m_t = min(BM, p.M - qt * BM);
         const int j = lane_query<BM>(r, m_t);
         const bool valid_q = j >= 0 && j < m_t;
+        lane_valid = valid_q;
         q = qt * BM + j;
         qs = valid_q ? p.qscale[qt * BM + query_arow<BM>(j, m_t)] : 0.0f;
         T = valid_q ? p.thr[q] : ~0ull;
@@ -385,6 +391,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; i++) v[i] = 0u;
         }
+        if (!lane_valid) mask = 0u;
         if (col0 + 32 > lim) mask &= (col0 >= lim) ? 0u : ((1u << (uint32_t)(lim - col0)) - 1u);
         if (p.keep && mask) mask &= keep_bits32(p.keep, p.keep_nbits, (uint64_t)p.id_base + row0 + col0);
         if (mask) {

@@ -193,3 +193,24 @@ def test_tensor_prefilter_row_shards(backend):
     assert_answers(gidx[:4], gsc[:4], *oracle_answers(codes, ctr, bq, bs, over, Q[:4], k), "shards")
     for b in shards:
         b.Close()
+
+
+@pytest.mark.parametrize("M", [64, 17])
+def test_tensor_prefilter_after_stale_tmem(backend, M):
+    """A batch of at most 64 queries runs 64-query MMA tiles, which write TMEM
+    lanes 0-15 of each 32-lane sub-partition only; the epilogue reads the other
+    lanes too. Whatever stale accumulators those lanes hold, they hold no query
+    and must yield no candidate. The tensor-pipe probe first leaves large
+    accumulators in every SM's TMEM."""
+    d, n, k, over = 1024, 30000, 10, 40
+    r = synth.Recipe(synth.MIXTURE, d, seed=M + 1, ncl=20, sigma=0.35)
+    v, ctr, codes, bq, bs = build(r, n)
+    bix = backend.NewBinaryI8Index(codes, codes.shape[1], ctr, bq, bs, n, d, over)
+    Q = r.queries(M)
+    cand = k * over
+    want = shortlist(bix, Q, cand)
+    bix.set_tensor_prefilter(1)
+    for _ in range(2):
+        backend.ctx.probe_tensor_i8(500)
+        assert shortlist(bix, Q, cand).tobytes() == want.tobytes()
+    bix.Close()
