@@ -645,24 +645,25 @@ static int32_t pow2_ge_host(int64_t x) {
 // Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles. A range after
 // the first admits about k*F candidates per query; every range costs a GEMM
 // launch and a select. Two regimes:
+// The first range takes every row as a candidate: max(k, 4096) rows. Its
+// select is the most expensive one (a 4096-key union per query); a 16K-row
+// first range cost a row shard of 1.25M rows (C2 over 8 GPUs) 10 % more per
+// batch on B200, and 10M rows no less. Then two regimes:
 //  * batches of up to 64 queries stream the corpus at the HBM rate and the
-//    epilogue hides under the loads, so ranges are few: the first takes every
-//    row as a candidate, up to a quarter of the per-query buffer (16K rows at
-//    batch 64); then the growth factor is 64 (16 while ranges are short);
+//    epilogue hides under the loads, so ranges are few: the growth factor is
+//    64 (16 while ranges are short);
 //  * larger batches are bound by the tensor pipe and the epilogue, where
-//    every candidate costs epilogue and select work, so ranges are more and
-//    finer: the first takes max(k, 4096) rows, then the growth factor is 8
-//    (4 when k >= 512). On B200 this took a batch of 512 at k = 1000 from
-//    2.73 to 2.37 ms (4M rows) and a batch of 1024 at k = 1000 from 4.04 to
-//    3.67 ms, with batch 4096 at k = 100 unchanged.
+//    every candidate costs epilogue and select work, so ranges are finer: the
+//    growth factor is 8 (4 when k >= 512). On B200 this took a batch of 512
+//    at k = 1000 from 2.73 to 2.37 ms (4M rows) and a batch of 1024 at
+//    k = 1000 from 4.04 to 3.67 ms, with batch 4096 at k = 100 unchanged.
 // All factors stay within a quarter of the per-query buffer.
 static void plan_ranges(int64_t n, int32_t M, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
   const int64_t room = std::max<int64_t>(4, cap / (4 * (int64_t)k));
   const bool fine = M > 64;
   const int64_t F1 = std::min<int64_t>(fine ? (k >= 512 ? 4 : 8) : 16, room);
   const int64_t F2 = fine ? F1 : std::min<int64_t>(64, room);
-  int64_t hi = fine ? std::max<int64_t>(k, 4096)
-                    : std::max<int64_t>(std::max<int64_t>(k, 1024), std::min<int64_t>(16384, cap / 4));
+  int64_t hi = std::max<int64_t>(k, 4096);
   hi = (hi + kGemmBN - 1) / kGemmBN * kGemmBN;
   int64_t lo = 0;
   while (lo < n) {
