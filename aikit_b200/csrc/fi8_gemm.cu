@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(256) sign_prep_kernel(const float* q, int M, i
   for (int i = tid; i < kp; i += blockDim.x) topk[(size_t)qi * kp + i] = kEmptyKey;
 }
 
-// One CTA of 512 threads per query: fold this range's candidates into the
+// One CTA per query (1024 or 512 threads): fold this range's candidates into the
 // running top-k. The carried list holds keys of earlier ranges (all above the
 // threshold the candidates passed), so top-k of the union is exact.
 //
@@ -550,8 +550,11 @@ __global__ void __launch_bounds__(256) sign_prep_kernel(const float* q, int M, i
 // those keys. Shared memory holds only the histogram and the kept list, so
 // many queries' CTAs share an SM and a large batch selects in one wave. Only
 // the last range's select orders its keys (its output is the answer).
-constexpr int kSelThreads = 512;
-constexpr int kSelUnroll = 8;
+// Threads and unrolled loads per CTA: a one-wave launch stages its union in
+// shared memory (one CTA per SM) and spreads it over 1024 threads; a larger
+// batch streams unions from L2 with several 512-thread CTAs per SM.
+constexpr int kSelThreadsStaged = 1024, kSelUnrollStaged = 4;
+constexpr int kSelThreads = 512, kSelUnroll = 8;
 constexpr int kRadixBins = 256;
 
 // Slot i of a query's union: its carried list, then this range's candidates.
@@ -560,7 +563,8 @@ __device__ __forceinline__ uint64_t union_key(const uint64_t* mine, int kp, cons
   return i < kp ? __ldcg(mine + i) : __ldcg(src + (i - kp));
 }
 
-__global__ void __launch_bounds__(kSelThreads)
+template <int NT, int UNROLL>
+__global__ void __launch_bounds__(NT)
     select_kernel(int k, int kp, int cap_s, uint64_t* topk, unsigned long long* thr, unsigned int* cnt,
                   const uint64_t* cand, int cap, uint64_t* out, unsigned int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -587,13 +591,13 @@ __global__ void __launch_bounds__(kSelThreads)
   // it from L2.
   const bool staged = n_all <= cap_s;
   if (staged) {
-    for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
-      uint64_t keys[kSelUnroll];
+    for (int i0 = 0; i0 < n_all; i0 += NT * UNROLL) {
+      uint64_t keys[UNROLL];
 #pragma unroll
-      for (int u = 0; u < kSelUnroll; u++) keys[u] = union_key(mine, kp, src, n_all, i0 + u * kSelThreads + tid);
+      for (int u = 0; u < UNROLL; u++) keys[u] = union_key(mine, kp, src, n_all, i0 + u * NT + tid);
 #pragma unroll
-      for (int u = 0; u < kSelUnroll; u++)
-        if (i0 + u * kSelThreads + tid < n_all) ubuf[i0 + u * kSelThreads + tid] = keys[u];
+      for (int u = 0; u < UNROLL; u++)
+        if (i0 + u * NT + tid < n_all) ubuf[i0 + u * NT + tid] = keys[u];
     }
   }
   auto key_at = [&](int i) -> uint64_t {
@@ -628,12 +632,12 @@ __global__ void __launch_bounds__(kSelThreads)
     __syncthreads();
     const unsigned long long prefix = s_prefix, mask = s_mask;
     unsigned long long k_and = ~0ull, k_or = 0ull;
-    for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
-      uint64_t keys[kSelUnroll];  // loads first, so their L2 latencies overlap
+    for (int i0 = 0; i0 < n_all; i0 += NT * UNROLL) {
+      uint64_t keys[UNROLL];  // loads first, so their L2 latencies overlap
 #pragma unroll
-      for (int u = 0; u < kSelUnroll; u++) keys[u] = key_at(i0 + u * kSelThreads + tid);
+      for (int u = 0; u < UNROLL; u++) keys[u] = key_at(i0 + u * NT + tid);
 #pragma unroll
-      for (int u = 0; u < kSelUnroll; u++) {
+      for (int u = 0; u < UNROLL; u++) {
         const uint64_t key = keys[u];
         const bool live = key != kEmptyKey && (key & mask) == prefix;
         const unsigned int bin = live ? (unsigned int)(key >> shift) & 0xFFu : 0x100u;
@@ -702,12 +706,12 @@ __global__ void __launch_bounds__(kSelThreads)
   const unsigned long long prefix = s_done == 2 ? 0ull : s_prefix;
   const unsigned long long mask = s_done == 2 ? 0ull : s_mask;
   unsigned long long my_min = ~0ull;
-  for (int i0 = 0; i0 < n_all; i0 += kSelThreads * kSelUnroll) {
-    uint64_t keys[kSelUnroll];
+  for (int i0 = 0; i0 < n_all; i0 += NT * UNROLL) {
+    uint64_t keys[UNROLL];
 #pragma unroll
-    for (int u = 0; u < kSelUnroll; u++) keys[u] = key_at(i0 + u * kSelThreads + tid);
+    for (int u = 0; u < UNROLL; u++) keys[u] = key_at(i0 + u * NT + tid);
 #pragma unroll
-    for (int u = 0; u < kSelUnroll; u++) {
+    for (int u = 0; u < UNROLL; u++) {
       const uint64_t key = keys[u];
       const bool take = key != kEmptyKey && (key & mask) >= prefix;
       if (take && key < my_min) my_min = key;
@@ -727,23 +731,23 @@ __global__ void __launch_bounds__(kSelThreads)
     if (nkept <= 512) {
       // rank placement: a kept key's position is the number of kept keys
       // above it (keys are distinct); a sorting network beyond that
-      for (int i = tid; i < nkept; i += kSelThreads) {
+      for (int i = tid; i < nkept; i += NT) {
         const uint64_t key = sel[i];
         int rank = 0;
         for (int j = 0; j < nkept; j++) rank += sel[j] > key;
         ranked[rank] = key;
       }
     } else {
-      for (int i = tid; i < kp; i += kSelThreads) ranked[i] = i < nkept ? sel[i] : kEmptyKey;
-      named_sync(1, kSelThreads);
-      group_sort_desc<kSelThreads>(ranked, kp, tid, 1);
+      for (int i = tid; i < kp; i += NT) ranked[i] = i < nkept ? sel[i] : kEmptyKey;
+      named_sync(1, NT);
+      group_sort_desc<NT>(ranked, kp, tid, 1);
     }
     __syncthreads();
     kept = ranked;
   }
-  for (int i = tid; i < kp; i += kSelThreads) mine[i] = i < nkept ? kept[i] : kEmptyKey;
+  for (int i = tid; i < kp; i += NT) mine[i] = i < nkept ? kept[i] : kEmptyKey;
   if (out)
-    for (int i = tid; i < k; i += kSelThreads) out[(size_t)qi * k + i] = i < nkept ? kept[i] : kEmptyKey;
+    for (int i = tid; i < k; i += NT) out[(size_t)qi * k + i] = i < nkept ? kept[i] : kEmptyKey;
   if (tid == 0) {
     thr[qi] = nkept >= k ? s_min : 0ull;
     cnt[qi] = 0u;
@@ -890,11 +894,11 @@ cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsi
   // one wave of CTAs (a query each) stages its union in shared memory
   const int cap_s = M <= sm_count ? 16384 : 0;
   const size_t smem = (size_t)(2 * kp + cap_s) * 8;  // kept list + its order (+ the union)
-  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (2 * 4096 + 16384) * 8);
+  auto kern = cap_s ? select_kernel<kSelThreadsStaged, kSelUnrollStaged> : select_kernel<kSelThreads, kSelUnroll>;
+  const int nt = cap_s ? kSelThreadsStaged : kSelThreads;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (2 * 4096 + 16384) * 8);
   if (e != cudaSuccess) return e;
-  return launch_pdl(select_kernel, dim3((unsigned)M), dim3(kSelThreads), smem, stream, k, kp, cap_s, topk, thr, cnt,
-                    cand, cap, out, err);
+  return launch_pdl(kern, dim3((unsigned)M), dim3(nt), smem, stream, k, kp, cap_s, topk, thr, cnt, cand, cap, out, err);
 }
 
 }  // namespace fi8
