@@ -107,3 +107,28 @@ def test_batch_row_shard_ids(backend):
     widx, wsc = oracle_topk(bq[10_000:], bs[10_000:], Q, 25)
     assert_same(gidx.astype(np.int64), gsc, widx + 10_000, wsc, "shard")
     ix.Close()
+
+
+@pytest.mark.parametrize("share", [0.5, 0.97])
+def test_cpu_gpu_shard_split(backend, share):
+    """EnableGPUShardSplit / queryBatchSharded (ann/backend.go:207-346): the
+    device index holds the first int(share * n) rows (built from a prefix of
+    the corpus, as the reference's NewI8Index call does), the CPU scores the
+    rest, and the two shard-local top-k lists merge by (score desc, index asc)
+    into exactly the whole corpus's answer."""
+    n, d, k = 40_000, 256, 50
+    r = synth.Recipe(synth.MIXTURE, d, seed=21, ncl=20, sigma=0.3)
+    bq, bs = r.codes(n)
+    rows = min(max(int(share * n), 1), n - 1)
+    ix = backend.NewI8Index(bq[:rows], bs[:rows], rows, d)
+    Q = r.queries(12)
+    gidx, gsc = ix.topk_arrays(Q, k)  # the device shard, one batch
+    for m, q in enumerate(Q):
+        ci, cs = oracle.flat_i8_query(bq[rows:], bs[rows:], q, k)  # the CPU shard
+        dev = [(int(i), float(s)) for i, s in zip(gidx[m], gsc[m]) if i >= 0]
+        mi, ms = oracle.merge_hits([([i for i, _ in dev], [s for _, s in dev]),
+                                    (np.asarray(ci, np.int64) + rows, np.asarray(cs))], k)
+        wi, ws = oracle.flat_i8_query(bq, bs, q, k)
+        assert mi.tolist() == list(wi)
+        assert np.asarray(ms, np.float32).tobytes() == np.asarray(ws, np.float32).tobytes()
+    ix.Close()
