@@ -398,19 +398,55 @@ void or_hamming_rows(const uint64_t* q, const uint64_t* codes, int64_t words,
   }
 }
 
-int64_t or_prefilter_hist(const uint64_t* qc, const uint64_t* codes, int64_t n,
-                          int64_t dim, int64_t cand, int32_t* ids_out) {
+typedef struct {
+  const uint64_t* qc;
+  const uint64_t* codes;
+  int64_t words, lo, hi, nb;
+  uint16_t* dists;
+  int64_t* hist;
+} hist_job;
+
+/* scanHist (prefilter.go:207-216) over rows [lo, hi) in 1024-row blocks. */
+static void hist_span(const hist_job* j) {
+  for (int64_t base = j->lo; base < j->hi; base += 1024) {
+    int64_t end = base + 1024 < j->hi ? base + 1024 : j->hi;
+    or_hamming_rows(j->qc, j->codes + base * j->words, j->words, end - base, j->dists + base);
+    for (int64_t i = base; i < end; i++) j->hist[j->dists[i]]++;
+  }
+}
+
+static void* hist_thread(void* arg) {
+  hist_span((const hist_job*)arg);
+  return NULL;
+}
+
+int64_t or_prefilter_hist_mt(const uint64_t* qc, const uint64_t* codes, int64_t n,
+                             int64_t dim, int64_t cand, int32_t* ids_out, int nthreads) {
   int64_t words = (dim + 63) / 64;
   int64_t nb = dim + 1;
   uint16_t* dists = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(n > 0 ? n : 1));
-  int64_t* hist = (int64_t*)calloc((size_t)nb, sizeof(int64_t));
-  /* scanHist (prefilter.go:207-216) in 1024-row blocks; the worker split of
-   * prefilter.go:152-178 only partitions rows and sums histograms. */
-  for (int64_t base = 0; base < n; base += 1024) {
-    int64_t end = base + 1024 < n ? base + 1024 : n;
-    or_hamming_rows(qc, codes + base * words, words, end - base, dists + base);
-    for (int64_t i = base; i < end; i++) hist[dists[i]]++;
+  /* the worker split of prefilter.go:147-178: binQueryWorkers (:328-335,
+   * one worker below 2^17 scanned words, else one per CPU) workers, each
+   * scanning a contiguous row range into its own histogram; the histograms
+   * are summed. Results do not depend on the split. */
+  int64_t workers = (nthreads < 1 || n < 2 || n * words < (1 << 17)) ? 1 : (nthreads < n ? nthreads : n);
+  int64_t per = (n + workers - 1) / workers;
+  int64_t* hist = (int64_t*)calloc((size_t)(nb * workers), sizeof(int64_t));
+  hist_job* jobs = (hist_job*)malloc(sizeof(hist_job) * (size_t)workers);
+  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)workers);
+  for (int64_t w = 0; w < workers; w++) {
+    int64_t lo = w * per, hi = lo + per < n ? lo + per : n;
+    hist_job jb = {qc, codes, words, lo < n ? lo : n, hi, nb, dists, hist + w * nb};
+    jobs[w] = jb;
+    if (workers > 1) pthread_create(&th[w], NULL, hist_thread, &jobs[w]);
   }
+  if (workers == 1) hist_span(&jobs[0]);
+  else
+    for (int64_t w = 0; w < workers; w++) pthread_join(th[w], NULL);
+  for (int64_t w = 1; w < workers; w++)
+    for (int64_t b = 0; b < nb; b++) hist[b] += hist[w * nb + b];
+  free(jobs);
+  free(th);
   int64_t cum = 0, t = 0; /* prefilter.go:182-189 */
   for (; t < nb; t++) {
     if (cum + hist[t] >= cand) break;
@@ -429,6 +465,11 @@ int64_t or_prefilter_hist(const uint64_t* qc, const uint64_t* codes, int64_t n,
   free(dists);
   free(hist);
   return c;
+}
+
+int64_t or_prefilter_hist(const uint64_t* qc, const uint64_t* codes, int64_t n,
+                          int64_t dim, int64_t cand, int32_t* ids_out) {
+  return or_prefilter_hist_mt(qc, codes, n, dim, cand, ids_out, 1);
 }
 
 static int cmp_i32(const void* a, const void* b) {
@@ -493,7 +534,7 @@ int64_t or_flat_binary_i8_query(const uint64_t* codes, const float* center,
   or_pack_row(q, center, d, qc); /* :101-103 */
   int32_t* ids = (int32_t*)malloc(sizeof(int32_t) * (size_t)cand);
   int64_t nid = keep ? or_prefilter_heap(qc, codes, n, d, cand, keep, 1, ids)
-                     : or_prefilter_hist(qc, codes, n, d, cand, ids);
+                     : or_prefilter_hist_mt(qc, codes, n, d, cand, ids, nthreads);
   /* rerank (:122-153): gather in id order, one W8A8 call, topk in id order. */
   int8_t* g = (int8_t*)malloc((size_t)(nid * d > 0 ? nid * d : 1));
   float* gs = (float*)malloc(sizeof(float) * (size_t)(nid > 0 ? nid : 1));

@@ -90,6 +90,10 @@ void or_hamming_rows(const uint64_t* q, const uint64_t* codes, int64_t words,
  * Returns the id count. */
 int64_t or_prefilter_hist(const uint64_t* qc, const uint64_t* codes, int64_t n,
                           int64_t dim, int64_t cand, int32_t* ids_out);
+/* or_prefilter_hist with the reference's worker split over nthreads host
+ * threads (identical results). */
+int64_t or_prefilter_hist_mt(const uint64_t* qc, const uint64_t* codes, int64_t n,
+                             int64_t dim, int64_t cand, int32_t* ids_out, int nthreads);
 
 /* prefilterHeap/scanShard/finishCandidates (ann/flat_binary_prefilter.go:
  * 227-313) with nshards shards (binQueryWorkers' fan-out, :330-335). */

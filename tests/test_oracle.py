@@ -370,3 +370,17 @@ def test_synth_binary_corpus_matches_oracle():
     assert bits.tobytes() == oracle.pack_codes(v, ctr).tobytes()
     bq, bs = oracle.quantize_rows(v)
     assert q.tobytes() == bq.tobytes() and s.tobytes() == bs.tobytes()
+
+
+def test_binary_query_worker_split_is_result_identical():
+    """prefilterHist's worker split (flat_binary_prefilter.go:147-178) only
+    partitions rows and sums histograms: the threaded oracle returns exactly
+    the single-threaded answer."""
+    r = synth.Recipe(synth.UNIT, 256, seed=12)
+    n = 150_000  # n * words = 600K >= 2^17: the split engages
+    ctr = r.center(n)
+    bits, q8, sc = r.binary(n, ctr)
+    for m, q in enumerate(r.queries(3)):
+        a = oracle.flat_binary_i8_query(bits, ctr, q8, sc, 50, q, 10, nthreads=1)
+        b = oracle.flat_binary_i8_query(bits, ctr, q8, sc, 50, q, 10, nthreads=7)
+        assert a[0].tolist() == b[0].tolist() and a[1].tobytes() == b[1].tobytes(), m
