@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
     for (int g = 0; g < kGroups; g++) {
       s_count[g] = 0;
       s_local_thr[g] = 0;
-      s_thr[g] = TOPK ? ld_relaxed_u64(p.gthr + y) : 0ull;
+      s_thr[g] = 0ull;  // read from gthr after the wait below
     }
   }
   __syncthreads();
@@ -146,8 +146,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
     uint64_t* buf = bufs + (TOPK ? (size_t)g * p.cap : 0);
 
     // the query (and, binary, the zeroed histogram) may come from the kernel
-    // just before this one; the producer streams the corpus meanwhile
+    // just before this one; the producer streams the corpus meanwhile. So
+    // does the per-query threshold: the previous scan on this stream resets
+    // it in its very last CTA, after this launch's CTAs may have started on
+    // SMs that scan has freed, so it is read only after the wait.
     pdl_wait_prior();
+    if (TOPK && gtid == 0) s_thr[g] = ld_relaxed_u64(p.gthr + y);
     if (BIN) {
       // the query's packed sign bits, prepared by the caller
       const int8_t* qb = reinterpret_cast<const int8_t*>(p.qbits) + (size_t)y * dpad;

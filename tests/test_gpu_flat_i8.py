@@ -272,3 +272,34 @@ def test_large_c2_shape_sampled(backend):
     widx, wsc = oracle_topk(bq, bs, Q, 100)
     assert_same(gidx.astype(np.int64), gsc, widx, wsc, "C2-sample")
     ix.Close()
+
+
+def test_back_to_back_async_queries(backend):
+    """Batch-1 queries launched back to back on one stream with no host sync:
+    each scan may start on SMs the previous scan frees while that scan's last
+    CTA is still merging, so it must not take the previous query's threshold.
+    Queries alternate between full-scale and 1/100-scale vectors, so a stale
+    threshold from the previous query would be far above every score of the
+    next one."""
+    import torch
+    from aikit_b200.ann import unpack_keys
+    n, d, k, M = 300_000, 256, 50, 24
+    r = synth.Recipe(synth.MIXTURE, d, seed=11, ncl=40, sigma=0.3)
+    bq, bs = r.codes(n)
+    ix = backend.NewI8Index(bq, bs, n, d)
+    Q = r.queries(M)
+    Q[1::2] *= np.float32(0.01)
+    qd = torch.from_numpy(Q).cuda()
+    keys = torch.zeros((M, k), dtype=torch.int64, device="cuda")
+    st = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    for m in range(M):
+        ix.topk_async(qd[m].data_ptr(), 1, k, keys[m].data_ptr(), st.cuda_stream)
+    st.synchronize()
+    ix.sync()
+    gi, gs = unpack_keys(keys.cpu().numpy().view(np.uint64))
+    for m in range(M):
+        i, s = oracle.flat_i8_query(bq, bs, Q[m], k)
+        assert gi[m].tolist() == list(i), m
+        assert gs[m].tobytes() == np.asarray(s, np.float32).tobytes(), m
+    ix.Close()
