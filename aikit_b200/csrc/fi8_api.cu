@@ -796,6 +796,13 @@ static int check_device_error(fi8_index* x) {
     const unsigned v = *x->h_err;
     *x->h_err = 0;
     cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream);
+    if (v & 1u) {
+      // a launch gave up on a wait: return the scan's cross-CTA state to zero
+      // in case it stopped before its last CTA reset it
+      if (x->d_gthr) cudaMemsetAsync(x->d_gthr, 0, x->gthr_cap * sizeof(unsigned long long), x->stream);
+      if (x->d_counter) cudaMemsetAsync(x->d_counter, 0, x->counter_cap * sizeof(unsigned int), x->stream);
+      if (x->d_counter2) cudaMemsetAsync(x->d_counter2, 0, x->counter2_cap * sizeof(unsigned int), x->stream);
+    }
     cudaStreamSynchronize(x->stream);
     return fail(FI8_ERR_DEVICE, "fi8: kernel reported device error flags 0x%x (%s)", v,
                 (v & 1u) ? "a bounded wait expired" : "a candidate buffer overflowed");
