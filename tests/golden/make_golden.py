@@ -1,8 +1,8 @@
 """Regenerate the committed golden fixtures under tests/golden/.
 
-Run in a checkout that has the reference mounted (its path is the first
-argument, default /root/reference); the outputs are committed so the tests
-never read the reference at run time.
+Run where the reference tree is available, with its path as the only
+argument; the outputs are committed so the tests never read the reference at
+run time.
 
 1. embedded_corpus_head.fi8 -- the first 512 rows of the reference's real
    Model2Vec FI8 v1 blob (examples/embedded-corpus/assets/index.bin, d=256,
@@ -90,4 +90,6 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference tree>")
+    main(sys.argv[1])
