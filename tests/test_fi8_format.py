@@ -99,3 +99,58 @@ def test_paged_block_rows_follow_the_reference():
     assert fi8_format.paged_block_rows(768) == (1 << 20) // 768
     assert fi8_format.paged_block_rows(1 << 21) == 1
     assert fi8_format.paged_block_rows(0) == 1
+
+
+class _FakeIndex:
+    def __init__(self, n, dim):
+        self.n, self.dim, self.rows, self.finished = n, dim, [], False
+        self.codes = np.zeros((n, dim), np.int8)
+        self.scales = np.zeros(n, np.float32)
+
+    def upload_rows(self, row0, codes, scales):
+        c = np.asarray(codes, np.int8).reshape(-1, self.dim)
+        self.codes[row0:row0 + len(c)] = c
+        self.scales[row0:row0 + len(c)] = scales
+        self.rows.append((row0, len(c)))
+
+    def upload_finish(self):
+        self.finished = True
+
+
+class _FakeBackend:
+    def NewI8IndexEmpty(self, n, dim, id_base=0):
+        self.ix = _FakeIndex(n, dim)
+        return self.ix
+
+
+@pytest.mark.parametrize("n,dim,block", [(1000, 300, 77), (4096, 256, 0), (5, 1, 2)])
+def test_upload_paged_walks_blocks_in_order(tmp_path, n, dim, block):
+    """upload_paged (the paged-index device path): every row once, in blocks
+    of block_rows (pagedBlockRows when 0) in ascending order, a ragged last
+    block, then the finish call; the uploaded rows equal the blob's."""
+    rng = np.random.default_rng(n)
+    bq = rng.integers(-127, 128, size=(n, dim), dtype=np.int8)
+    bs = rng.random(n).astype(np.float32)
+    path = tmp_path / "c.fi8"
+    path.write_bytes(fi8_format.dumps(bq, bs))
+    be = _FakeBackend()
+    ix = fi8_format.upload_paged(be, str(path), block_rows=block)
+    rows = block or fi8_format.paged_block_rows(dim)
+    want = [(r0, min(rows, n - r0)) for r0 in range(0, n, rows)]
+    assert ix.rows == want and ix.finished
+    assert ix.codes.tobytes() == bq.tobytes() and ix.scales.tobytes() == bs.tobytes()
+
+
+def test_upload_paged_rejects_bad_blobs(tmp_path):
+    empty = tmp_path / "empty.fi8"
+    empty.write_bytes(b"")
+    with pytest.raises(fi8_format.FormatError):
+        fi8_format.upload_paged(_FakeBackend(), str(empty))
+    zero = tmp_path / "zero.fi8"
+    zero.write_bytes(fi8_format.dumps(np.zeros((0, 0), np.int8), np.zeros(0, np.float32)))
+    with pytest.raises(fi8_format.FormatError):
+        fi8_format.upload_paged(_FakeBackend(), str(zero))
+    bad = tmp_path / "bad.fi8"
+    bad.write_bytes(b"\x00" * 20)
+    with pytest.raises(fi8_format.FormatError):
+        fi8_format.upload_paged(_FakeBackend(), str(bad))
