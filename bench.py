@@ -68,6 +68,9 @@ NCU_TRAFFIC = {
                            "algorithmic_bytes": 4_000_000 * 128 + 128 + 2 * 4_000_000,
                            "profile": "profiles/scan_kernel_binary_c4.md"},
     # Hamming-mode GEMM (tensor-core prefilter), batch 512: 737,856 sign rows of 1024 B, plus the query tile
+    # W8A8 GEMM at batch 4096 (C3 row shape): 737,856 rows of 1024 codes + scales, plus the query tile
+    "gemm_kernel_c3": {"dram_bytes": 763.026176e6 + 12.11648e6, "algorithmic_bytes": 737_856 * 1028 + 4096 * 1024,
+                       "profile": "profiles/gemm_kernel_c3_batch4096.md"},
     "gemm_kernel_ham": {"dram_bytes": 756.334080e6 + 11.297024e6,
                         "algorithmic_bytes": 737_856 * 1024 + 512 * 1024,
                         "profile": "profiles/gemm_kernel_ham_c4_batch512.md"},
@@ -441,6 +444,8 @@ def c3_leg(be, args, stream, local, tensor_peak):
     gemm_ms = kt["gemm_kernel"]["ms"] / steps
     ops = 2.0 * C3_BATCH * C3_ROWS * C3_DIM
     achieved = ops / (gemm_ms / 1e3)
+    ncu = NCU_TRAFFIC["gemm_kernel_c3"]
+    traffic = (C3_ROWS * (C3_DIM + 4) + C3_BATCH * C3_DIM) * ncu["dram_bytes"] / ncu["algorithmic_bytes"]
     return {
         "metric": "FlatI8 exact top-K queries/sec, batch 4096", "value": C3_BATCH * steps / (ms / 1e3),
         "unit": "queries/s", "ms_per_step": ms / steps, "steps": steps,
@@ -448,7 +453,10 @@ def c3_leg(be, args, stream, local, tensor_peak):
                                f"sigma 0.25), d={C3_DIM}, K={C3_K}, batch {C3_BATCH}",
                    "l2": "codes 4.1 GB > 126 MB L2"},
         "roofline": {"bound": "tensor", "achieved": achieved / 1e12, "peak": peak_ops / 1e12, "unit": "TOPS",
-                     "frac": achieved / peak_ops, "traffic": None, "kernel": "gemm_kernel (W8A8)",
+                     "frac": achieved / peak_ops, "traffic": traffic, "traffic_unit": "bytes per step",
+                     "traffic_source": f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
+                                       "times this step's corpus bytes",
+                     "kernel": "gemm_kernel (W8A8)",
                      "gemm_ms_per_step": gemm_ms, "algorithmic_ops_per_step": ops,
                      "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
                      "peak_source": f"fi8_probe_tensor_i8 measured live ({probe_ms:.1f} ms)"},
