@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import oracle
-from aikit_b200 import synth
+from aikit_b200 import DeclinedError, synth
 
 from parity_util import assert_same, oracle_topk
 
@@ -76,6 +76,30 @@ def test_batch_all_identical_rows(backend):
     gidx, gsc = ix.topk_arrays(Q, 300)
     for m in range(3):
         assert gidx[m].tolist() == list(range(300))
+    ix.Close()
+
+
+@pytest.mark.parametrize("M", [8, 160])
+def test_batch_at_the_top_k_limit(backend, M):
+    """k = 4096, the largest k the batched select takes, on tied scores: the
+    kept list goes through the shared-memory sort, not the rank placement.
+    M = 8 stages each query's union in shared memory; M = 160, more queries
+    than SMs, streams the unions from L2. One more k is declined, not
+    approximated; a single query takes the scan's own limit."""
+    r = synth.Recipe(synth.TIES, 128, seed=M)
+    n = 60_000
+    bq, bs = r.codes(n)
+    Q = r.queries(M)
+    ix = backend.NewI8Index(bq, bs, n, 128)
+    gidx, gsc = ix.topk_arrays(Q, 4096)
+    widx, wsc = oracle_topk(bq, bs, Q, 4096)
+    assert_same(gidx.astype(np.int64), gsc, widx, wsc, f"k=4096 M={M}")
+    with pytest.raises(DeclinedError):
+        ix.topk_arrays(Q, 4097)
+    k1 = ix.max_k()
+    gidx, gsc = ix.topk_arrays(Q[:1], k1)
+    widx, wsc = oracle_topk(bq, bs, Q[:1], k1)
+    assert_same(gidx.astype(np.int64), gsc, widx, wsc, f"batch 1 k={k1}")
     ix.Close()
 
 
