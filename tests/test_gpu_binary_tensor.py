@@ -214,3 +214,29 @@ def test_tensor_prefilter_after_stale_tmem(backend, M):
         backend.ctx.probe_tensor_i8(500)
         assert shortlist(bix, Q, cand).tobytes() == want.tobytes()
     bix.Close()
+
+
+def test_prefilter_at_the_cand_limit(backend):
+    """cand = 2048, the largest shortlist the device takes (k = 16, overquery
+    128), on 64-bit codes where hundreds of rows tie at the cut: the GEMM's
+    shortlist equals the popcount pass's and the answers equal the oracle's.
+    One more k makes cand 2176, which both prefilters decline."""
+    from aikit_b200 import DeclinedError
+    d, n, k, over = 64, 40000, 16, 128
+    r = synth.Recipe(synth.MIXTURE, d, seed=31, ncl=30, sigma=0.35)
+    v, ctr, codes, bq, bs = build(r, n)
+    bix = backend.NewBinaryI8Index(codes, codes.shape[1], ctr, bq, bs, n, d, over)
+    Q = r.queries(24)
+    cand = k * over
+    want = shortlist(bix, Q, cand)
+    base = bix.topk_arrays(Q, k)
+    with pytest.raises(DeclinedError):
+        bix.topk_arrays(Q, k + 1)
+    bix.set_tensor_prefilter(1)
+    assert shortlist(bix, Q, cand).tobytes() == want.tobytes()
+    got = bix.topk_arrays(Q, k)
+    assert got[0].tolist() == base[0].tolist() and got[1].tobytes() == base[1].tobytes()
+    assert_answers(got[0][:3], got[1][:3], *oracle_answers(codes, ctr, bq, bs, over, Q[:3], k), "cand 2048")
+    with pytest.raises(DeclinedError):
+        bix.topk_arrays(Q, k + 1)
+    bix.Close()
