@@ -117,7 +117,9 @@ int fi8_score_batch(fi8_index* idx, const float* q, int32_t M, float* dst);
  * q [M*dim] host f32; out_idx [M*k] int32 global indices, out_score [M*k] f32,
  * each row sorted (score desc, index asc), padded with index -1 when fewer than
  * k rows have a non-NaN score. Declines (FI8_ERR_DECLINED) when k <= 0 or
- * k >= n, like the reference; also when k exceeds fi8_topk_max_k(). */
+ * k >= n, like the reference; also when k is beyond the device top-K: above
+ * fi8_topk_max_k() for a batch that runs the scan (M below
+ * FI8_OPT_GEMM_MIN_BATCH), above 4096 for one that runs the GEMM. */
 int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t* out_idx,
                    float* out_score);
 
@@ -131,7 +133,8 @@ int fi8_topk_batch(fi8_index* idx, const float* q, int32_t M, int32_t k, int32_t
 int fi8_topk_batch_keep(fi8_index* idx, const float* q, int32_t M, int32_t k, const uint64_t* keep,
                         int64_t nbits, int32_t* out_idx, float* out_score);
 
-/* Largest k the device top-K answers for this index. */
+/* Largest k the scan path answers for this index (single queries and
+ * batches below FI8_OPT_GEMM_MIN_BATCH); batches on the GEMM take k <= 4096. */
 int fi8_topk_max_k(fi8_index* idx, int32_t* out);
 
 /* Stream-ordered, device-resident form of fi8_topk_batch for callers that keep
