@@ -158,6 +158,25 @@ __device__ __forceinline__ void flush_staged(const GemmParams& p, int q, const u
     if (pos < (unsigned int)p.cap) dst[pos] = stage[j];
 }
 
+// The units of one persistent CTA: unit blockIdx.x + u*G is query tile
+// unit % qtiles of row tile unit / qtiles. Stepping u adds G = dq + dr*qtiles,
+// so the walk advances both with an add and a compare instead of two 64-bit
+// divisions per unit.
+struct UnitWalk {
+  int qt, dq, qtiles;
+  int64_t rt, dr;
+  __device__ UnitWalk(int first, int G, int qtiles_)
+      : qt(first % qtiles_), dq(G % qtiles_), qtiles(qtiles_), rt(first / qtiles_), dr(G / qtiles_) {}
+  __device__ __forceinline__ void next() {
+    qt += dq;
+    rt += dr;
+    if (qt >= qtiles) {
+      qt -= qtiles;
+      rt++;
+    }
+  }
+};
+
 template <int BM, bool HAM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
@@ -211,11 +230,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       if (p.producer_waits) pdl_wait_prior();
       int64_t step = 0;
-      for (int64_t u = 0; u < my_units && !s_abort; u++) {
-        const int64_t unit = blockIdx.x + u * G;
-        const int qt = (int)(unit % p.qtiles);
-        const int64_t rt = unit / p.qtiles;
-        const int32_t row0 = (int32_t)(p.row_lo + rt * kGemmBN);
+      UnitWalk w(blockIdx.x, G, p.qtiles);
+      for (int64_t u = 0; u < my_units && !s_abort; u++, w.next()) {
+        const int qt = w.qt;
+        const int32_t row0 = (int32_t)(p.row_lo + w.rt * kGemmBN);
         for (int kc = 0; kc < p.kchunks; kc++, step++) {
           const int s = (int)(step % kStages);
           if (step >= kStages && !mbar_wait_bounded(&s_empty[s], (uint32_t)(((step / kStages) - 1) & 1))) {
@@ -306,11 +324,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // cannot overflow)
     int32_t hthr = 0;
     unsigned long long T = ~0ull;
+    UnitWalk w(blockIdx.x, G, p.qtiles);
     for (int64_t u = 0; u < my_units; u++) {
-      const int64_t unit = blockIdx.x + u * G;
-      const int qt = (int)(unit % p.qtiles);
-      const int64_t rt = unit / p.qtiles;
-      const int64_t row0 = p.row_lo + rt * kGemmBN;
+      const int qt = w.qt;
+      const int64_t row0 = p.row_lo + w.rt * kGemmBN;
+      w.next();  // from here on, the next unit's tiles
       const int b = (int)(u & 1);
       if (qt != cur_qt) {
         flush_staged(p, q, my_stage, staged);  // staged keys belong to the previous tile's query
@@ -342,7 +360,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       cp_async_wait_all();
       __syncwarp();
       if (!HAM && u + 1 < my_units) {
-        const int64_t nrow0 = p.row_lo + ((unit + G) / p.qtiles) * kGemmBN;
+        const int64_t nrow0 = p.row_lo + w.rt * kGemmBN;
         cp_async8(my_scale + (b ^ 1) * 64 + 2 * lane, p.scales + nrow0 + cq * 64 + 2 * lane);
       }
       cp_async_commit();
