@@ -324,11 +324,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // cannot overflow)
     int32_t hthr = 0;
     unsigned long long T = ~0ull;
+    // The scale and threshold of this lane's query in the next unit's tile
+    // are loaded one unit ahead (the tile changes from unit to unit when G is
+    // not a multiple of qtiles), so their latency overlaps this unit's work.
+    float qs_next = 0.0f;
+    unsigned long long T_next = ~0ull;
+    auto fetch_tile_state = [&](int qt_f) {
+      const int m_t = min(BM, p.M - qt_f * BM);
+      const int j = lane_query<BM>(r, m_t);
+      const bool valid = j >= 0 && j < m_t;
+      qs_next = valid ? p.qscale[qt_f * BM + query_arow<BM>(j, m_t)] : 0.0f;
+      T_next = valid ? p.thr[qt_f * BM + j] : ~0ull;
+    };
     UnitWalk w(blockIdx.x, G, p.qtiles);
+    if (my_units > 0) fetch_tile_state(w.qt);
     for (int64_t u = 0; u < my_units; u++) {
       const int qt = w.qt;
       const int64_t row0 = p.row_lo + w.rt * kGemmBN;
-      w.next();  // from here on, the next unit's tiles
       const int b = (int)(u & 1);
       if (qt != cur_qt) {
         flush_staged(p, q, my_stage, staged);  // staged keys belong to the previous tile's query
@@ -339,8 +351,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool valid_q = j >= 0 && j < m_t;
         lane_valid = valid_q;
         q = qt * BM + j;
-        qs = valid_q ? p.qscale[qt * BM + query_arow<BM>(j, m_t)] : 0.0f;
-        T = valid_q ? p.thr[q] : ~0ull;
+        qs = qs_next;  // fetched for this tile
+        T = T_next;
         // T is the k-th best key of rows below this range, and every row of
         // this range has a larger index, so a row scoring exactly T's score
         // loses the (score desc, index asc) comparison: only scores strictly
@@ -354,6 +366,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                  : (T == 0ull) ? -p.ham_dim
                                : p.ham_dim + 2 * ((int32_t)key_score(T) + 1);
       }
+      w.next();  // from here on, the next unit's tiles
+      if (u + 1 < my_units && w.qt != qt) fetch_tile_state(w.qt);
       if (s_abort) break;
       // this unit's scales (copied during the previous unit) have landed;
       // start the copy of the next unit's into the other slot
