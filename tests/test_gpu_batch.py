@@ -103,6 +103,25 @@ def test_batch_at_the_top_k_limit(backend, M):
     ix.Close()
 
 
+@pytest.mark.parametrize("ctas", [1, 5, 7, 146])
+def test_gemm_grid_sizes(backend, ctas):
+    """The answer does not depend on the GEMM's persistent grid (the multi-GPU
+    path runs it on all SMs but two). With G CTAs, CTA c takes units c, c+G,
+    ..., and a unit's query tile changes from one unit to the next unless G
+    is a multiple of the tile count: here 3 tiles of a 300-query batch, the
+    last one holding 44 queries."""
+    r = synth.Recipe(synth.MIXTURE, 256, seed=ctas, ncl=30, sigma=0.3)
+    n = 30_000
+    bq, bs = r.codes(n)
+    Q = r.queries(300)
+    ix = backend.NewI8Index(bq, bs, n, 256)
+    ix.set_gemm_ctas(ctas)
+    gidx, gsc = ix.topk_arrays(Q, 50)
+    widx, wsc = oracle_topk(bq, bs, Q, 50)
+    assert_same(gidx.astype(np.int64), gsc, widx, wsc, f"ctas={ctas}")
+    ix.Close()
+
+
 def test_batch_overflow_falls_back_exactly(backend):
     """A corpus ordered against the query (every later row beats every earlier
     one) makes a row range admit more candidates than its buffer holds; the

@@ -240,3 +240,23 @@ def test_prefilter_at_the_cand_limit(backend):
     with pytest.raises(DeclinedError):
         bix.topk_arrays(Q, k + 1)
     bix.Close()
+
+
+@pytest.mark.parametrize("ctas", [1, 7, 146])
+def test_tensor_prefilter_grid_sizes(backend, ctas):
+    """The Hamming-mode GEMM on a capped persistent grid: 200 queries make two
+    128-query tiles (the second with 72), so with an odd G each CTA's query
+    tile alternates from unit to unit. The shortlist stays the popcount
+    pass's."""
+    from aikit_b200._ffi import FI8_OPT_GEMM_CTAS, check, lib
+    d, n, k, over = 512, 30000, 10, 20
+    r = synth.Recipe(synth.MIXTURE, d, seed=40 + ctas, ncl=20, sigma=0.35)
+    v, ctr, codes, bq, bs = build(r, n)
+    bix = backend.NewBinaryI8Index(codes, codes.shape[1], ctr, bq, bs, n, d, over)
+    Q = r.queries(200)
+    cand = k * over
+    want = shortlist(bix, Q, cand)
+    bix.set_tensor_prefilter(1)
+    check(lib().fi8_index_set_option(bix._ih, FI8_OPT_GEMM_CTAS, ctas))
+    assert shortlist(bix, Q, cand).tobytes() == want.tobytes()
+    bix.Close()
