@@ -39,6 +39,7 @@ SIGNATURES = {
     "fi8_score_batch": (C.c_int, [_P, _P, _I32, _P]),
     "fi8_topk_batch": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
     "fi8_topk_max_k": (C.c_int, [_P, _P]),
+    "fi8_gemm_plan": (C.c_int, [_I64, C.c_int32, C.c_int32, _P, C.c_int32, _P]),
     "fi8_topk_batch_async": (C.c_int, [_P, _P, _I32, _I32, _P, _P]),
     "fi8_index_set_option": (C.c_int, [_P, C.c_int, _I64]),
     "fi8_index_last_launch_count": (C.c_int, [_P, _P]),

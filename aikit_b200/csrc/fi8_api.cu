@@ -644,7 +644,7 @@ static int32_t pow2_ge_host(int64_t x) {
 
 // Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles. A range after
 // the first admits about k*F candidates per query; every range costs a GEMM
-// launch and a select. Two regimes:
+// launch and a select.
 // The first range takes every row as a candidate: max(k, 4096) rows. Its
 // select is the most expensive one (a 4096-key union per query); a 16K-row
 // first range cost a row shard of 1.25M rows (C2 over 8 GPUs) 10 % more per
@@ -658,6 +658,13 @@ static int32_t pow2_ge_host(int64_t x) {
 //    at k = 1000 from 2.73 to 2.37 ms (4M rows) and a batch of 1024 at
 //    k = 1000 from 4.04 to 3.67 ms, with batch 4096 at k = 100 unchanged.
 // All factors stay within a quarter of the per-query buffer.
+// Per-query candidate capacity of a batch of M: ~256 MB of keys at most
+// across the batch, 8K to 64K keys per query.
+static int32_t gemm_cap(int32_t M) {
+  const int32_t cap = pow2_ge_host(std::max<int64_t>(8192, std::min<int64_t>(65536, (1ll << 25) / M)));
+  return std::min<int32_t>(cap, 65536);
+}
+
 static void plan_ranges(int64_t n, int32_t M, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
   const int64_t room = std::max<int64_t>(4, cap / (4 * (int64_t)k));
   const bool fine = M > 64;
@@ -695,9 +702,7 @@ static int launch_topk_gemm(fi8_index* x, const GemmCorpus& corpus, const float*
   const int32_t kp = pow2_ge_host(k);
   const int32_t bm = M <= 64 ? 64 : kGemmBM;  // the MMA's M: a small batch is one 64-query tile
   const int32_t Mpad = (M + bm - 1) / bm * bm;
-  // per-query candidate capacity: ~256 MB of keys at most across the batch
-  int32_t cap = pow2_ge_host(std::max<int64_t>(8192, std::min<int64_t>(65536, (1ll << 25) / M)));
-  if (cap > 65536) cap = 65536;
+  const int32_t cap = gemm_cap(M);
   int rc;
   if ((rc = ensure_device(&x->d_A, &x->A_cap, (size_t)Mpad * x->dpad, "gemm A")) != FI8_OK) return rc;
   if ((rc = ensure_device(&x->d_qscale, &x->qscale_cap, (size_t)Mpad, "gemm qscale")) != FI8_OK) return rc;
@@ -1547,3 +1552,17 @@ int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t
 }
 
 }  // extern "C"
+
+extern "C" int fi8_gemm_plan(int64_t n, int32_t M, int32_t k, int64_t* out_bounds, int32_t max_bounds,
+                             int32_t* count) {
+  if (n <= 0 || M <= 0 || k <= 0 || !out_bounds || !count || max_bounds < 2)
+    return fail(FI8_ERR_ARG, "fi8_gemm_plan: bad arguments");
+  std::vector<GemmLevel> ranges;
+  plan_ranges(n, M, k, gemm_cap(M), &ranges);
+  *count = (int32_t)ranges.size();
+  if ((int64_t)ranges.size() + 1 > max_bounds)
+    return fail(FI8_ERR_ARG, "fi8_gemm_plan: %zu ranges need %zu bounds", ranges.size(), ranges.size() + 1);
+  for (size_t i = 0; i < ranges.size(); i++) out_bounds[i] = ranges[i].row_lo;
+  out_bounds[ranges.size()] = ranges.back().row_hi;
+  return FI8_OK;
+}

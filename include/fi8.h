@@ -137,6 +137,13 @@ int fi8_topk_batch_keep(fi8_index* idx, const float* q, int32_t M, int32_t k, co
  * batches below FI8_OPT_GEMM_MIN_BATCH); batches on the GEMM take k <= 4096. */
 int fi8_topk_max_k(fi8_index* idx, int32_t* out);
 
+/* The row ranges a batched top-k of M queries at k over n rows runs as (one
+ * GEMM launch and one select each; plan_ranges in fi8_api.cu): *count ranges,
+ * written as count + 1 ascending row offsets to out_bounds, 0 first and n
+ * last. Host-only, no device work; FI8_ERR_ARG (with *count set) when
+ * max_bounds < count + 1. No counterpart in the reference. */
+int fi8_gemm_plan(int64_t n, int32_t M, int32_t k, int64_t* out_bounds, int32_t max_bounds, int32_t* count);
+
 /* Stream-ordered, device-resident form of fi8_topk_batch for callers that keep
  * queries and results in HBM (multi-GPU merge, benchmarks): d_q [M*dim] f32 and
  * d_keys [M*k] packed uint64 keys (decode with fi8_keys_unpack), both device
