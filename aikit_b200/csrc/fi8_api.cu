@@ -642,6 +642,13 @@ static int32_t pow2_ge_host(int64_t x) {
   return p;
 }
 
+// Per-query candidate capacity of a batch of M: ~256 MB of keys at most
+// across the batch, 8K to 64K keys per query.
+static int32_t gemm_cap(int32_t M) {
+  const int32_t cap = pow2_ge_host(std::max<int64_t>(8192, std::min<int64_t>(65536, (1ll << 25) / M)));
+  return std::min<int32_t>(cap, 65536);
+}
+
 // Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles. A range after
 // the first admits about k*F candidates per query; every range costs a GEMM
 // launch and a select.
@@ -658,13 +665,6 @@ static int32_t pow2_ge_host(int64_t x) {
 //    at k = 1000 from 2.73 to 2.37 ms (4M rows) and a batch of 1024 at
 //    k = 1000 from 4.04 to 3.67 ms, with batch 4096 at k = 100 unchanged.
 // All factors stay within a quarter of the per-query buffer.
-// Per-query candidate capacity of a batch of M: ~256 MB of keys at most
-// across the batch, 8K to 64K keys per query.
-static int32_t gemm_cap(int32_t M) {
-  const int32_t cap = pow2_ge_host(std::max<int64_t>(8192, std::min<int64_t>(65536, (1ll << 25) / M)));
-  return std::min<int32_t>(cap, 65536);
-}
-
 static void plan_ranges(int64_t n, int32_t M, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
   const int64_t room = std::max<int64_t>(4, cap / (4 * (int64_t)k));
   const bool fine = M > 64;
