@@ -1182,10 +1182,12 @@ constexpr int32_t kBinMaxM = 16;
 // The prefilter (packing, the distance pass with its histogram, the cut and
 // the shortlist) for M queries. sorted: each query's keys sorted descending,
 // as a cross-shard key merge needs. Caller holds b->ix->mu and the device.
+// allow_tensor = false keeps a batch on the popcount pass whatever the
+// tensor-prefilter setting (the exact redo after a GEMM candidate overflow).
 static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
-                                bool sorted, cudaStream_t st) {
+                                bool sorted, cudaStream_t st, bool allow_tensor = true) {
   fi8_index* x = b->ix;
-  if (b->d_sign && b->tensor_min_m > 0 && M >= b->tensor_min_m) {
+  if (allow_tensor && b->d_sign && b->tensor_min_m > 0 && M >= b->tensor_min_m) {
     // The shortlist is the cand best rows under (distance asc, id asc); as
     // packed keys (-distance, id) that is the exact top-cand the GEMM path
     // selects, sorted descending (so it also serves a key merge).
@@ -1508,14 +1510,26 @@ int fi8_bin_query_topk_keep(fi8_bin* b, const float* q, int32_t M, int32_t k, co
   if ((rc = ensure_host(&x->h_keys, &x->h_keys_cap, nk, "pinned keys")) != FI8_OK) return rc;
   if (cand > kBinMaxCand)
     return fail(FI8_ERR_DECLINED, "gpu: binary TopK declined (cand=%lld beyond %d)", (long long)cand, kBinMaxCand);
-  if ((rc = launch_bin_prefilter(b, x->d_q, M, (int32_t)cand, b->d_short, false, x->stream)) != FI8_OK) return rc;
-  if ((rc = launch_bin_rerank(b, x->d_q, M, b->d_short, (int32_t)cand, k, x->d_keys, x->stream)) != FI8_OK)
-    return rc;
-  FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
-           "D2H keys");
-  FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
-           "D2H err");
-  FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+  for (int pass = 0; pass < 2; pass++) {
+    // pass 1 runs only after the tensor-core prefilter dropped candidates (a
+    // row range admitted more than its per-query buffer holds, e.g. on a
+    // corpus ordered against the queries): its shortlist is incomplete, so
+    // the popcount pass, which has no such limit, redoes it exactly
+    if ((rc = launch_bin_prefilter(b, x->d_q, M, (int32_t)cand, b->d_short, false, x->stream, pass == 0)) !=
+        FI8_OK)
+      return rc;
+    if ((rc = launch_bin_rerank(b, x->d_q, M, b->d_short, (int32_t)cand, k, x->d_keys, x->stream)) != FI8_OK)
+      return rc;
+    FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
+             "D2H keys");
+    FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
+             "D2H err");
+    FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
+    // only the GEMM's select sets the overflow flag (2) alone
+    if (*x->h_err != 2u || pass == 1) break;
+    *x->h_err = 0;
+    FI8_CUDA(cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream), "memset err");
+  }
   if ((rc = check_device_error(x)) != FI8_OK) return rc;
   return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
 }

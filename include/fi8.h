@@ -149,8 +149,9 @@ int fi8_gemm_plan(int64_t n, int32_t M, int32_t k, int64_t* out_bounds, int32_t 
  * d_keys [M*k] packed uint64 keys (decode with fi8_keys_unpack), both device
  * pointers; stream is a cudaStream_t (NULL = the legacy default stream, as in
  * CUDA). Does not synchronize; device-side errors surface at the next
- * fi8_index_sync. Unlike
- * fi8_topk_batch it accepts k >= n (a row shard smaller than k yields all of its
+ * fi8_index_sync, a dropped-candidate overflow among them (fi8_topk_batch
+ * redoes such a batch on the scan instead). Unlike fi8_topk_batch it accepts
+ * k >= n (a row shard smaller than k yields all of its
  * rows, then empty keys). Calls on one index must not overlap on the GPU (they
  * share the index's scratch); issue them on one stream. */
 int fi8_topk_batch_async(fi8_index* idx, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
@@ -285,7 +286,10 @@ int fi8_bin_set_tensor_prefilter(fi8_bin* b, int32_t min_batch);
  * the cand rows nearest the centred query's sign bits in Hamming distance,
  * ties by ascending id (prefilterHist, prefilter.go:145-216), reranked by
  * W8A8 score (rerank, :122-153). Declines k <= 0 and k >= n (the reference
- * returns the whole corpus there), and cand above the device limit (2048). */
+ * returns the whole corpus there), and cand above the device limit (2048).
+ * A batch on the tensor-core prefilter whose row range admits more candidates
+ * than its buffer holds is redone with the popcount pass, so the answer stays
+ * exact. */
 int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score);
 
 /* FlatBinaryI8.QueryFilter (flat_binary_i8.go:83): the keep filter applies in

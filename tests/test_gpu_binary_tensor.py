@@ -260,3 +260,26 @@ def test_tensor_prefilter_grid_sizes(backend, ctas):
     check(lib().fi8_index_set_option(bix._ih, FI8_OPT_GEMM_CTAS, ctas))
     assert shortlist(bix, Q, cand).tobytes() == want.tobytes()
     bix.Close()
+
+
+def test_tensor_prefilter_overflow_is_redone_exactly(backend):
+    """A corpus ordered against the first query (every later row nearer to
+    it) makes the last row range admit about 324K candidates for that query,
+    beyond its 64K-key buffer, so the tensor-core shortlist comes back
+    incomplete. The query call notices and redoes the batch with the popcount
+    pass: the answers are exact, as the reference's CPU FlatBinaryI8 (which
+    has no such buffer) gives them."""
+    d, n, k, over = 64, 400_000, 10, 10
+    r = synth.Recipe(synth.UNIT, d, seed=12)
+    v, ctr, codes, bq, bs = build(r, n)
+    Q = r.queries(2)
+    dist = oracle.hamming_rows(oracle.pack_row(Q[0], ctr), codes).astype(np.int64)
+    order = np.argsort(-dist, kind="stable")  # the nearest rows last
+    codes, bq, bs = (np.ascontiguousarray(a[order]) for a in (codes, bq, bs))
+    bix = backend.NewBinaryI8Index(codes, codes.shape[1], ctr, bq, bs, n, d, over)
+    want = bix.topk_arrays(Q, k)  # the popcount pass
+    bix.set_tensor_prefilter(1)
+    got = bix.topk_arrays(Q, k)   # the GEMM overflows; the call redoes it
+    assert got[0].tolist() == want[0].tolist() and got[1].tobytes() == want[1].tobytes()
+    assert_answers(got[0], got[1], *oracle_answers(codes, ctr, bq, bs, over, Q, k), "overflow")
+    bix.Close()
