@@ -18,7 +18,8 @@ FI8_OPT_GEMM_MIN_BATCH = 1
 FI8_OPT_KERNEL_TIMING = 2
 FI8_OPT_GEMM_CTAS = 3
 # kernel classes of fi8_index_kernel_times, in index order
-KERNEL_KINDS = ("scan_kernel", "gemm_kernel", "select_kernel", "quantize_kernel", "rerank_kernel")
+KERNEL_KINDS = ("scan_kernel", "gemm_kernel", "select_kernel", "quantize_kernel", "rerank_kernel",
+                "redo_gated")
 
 _P = C.c_void_p
 _I32 = C.c_int32
@@ -68,6 +69,9 @@ SIGNATURES = {
     "fi8_index_create_empty": (C.c_int, [_P, _I64, _I32, _I64, _P]),
     "fi8_index_upload_rows": (C.c_int, [_P, _I64, _P, _P, _I64]),
     "fi8_index_upload_finish": (C.c_int, [_P]),
+    "fi8_bin_index_create_empty": (C.c_int, [_P, _I64, _I32, _I32, _P, _I32, _I64, _P]),
+    "fi8_bin_upload_rows": (C.c_int, [_P, _I64, _P, _P, _P, _I64]),
+    "fi8_bin_upload_finish": (C.c_int, [_P]),
 }
 
 

@@ -157,6 +157,21 @@ class B200Backend:
                                              id_base, C.byref(h)))
         return BinaryI8Index._adopt(self.ctx, h, n, dim, (dim + 63) // 64, overquery, id_base)
 
+    def NewBinaryI8IndexEmpty(self, n: int, dim: int, center, overquery: int = 16,
+                              id_base: int = 0) -> "BinaryI8Index":
+        """A FlatBinaryI8 shard of n all-zero rows to fill with
+        BinaryI8Index.upload_rows (fi8_bin_index_create_empty): a corpus that
+        is generated or read block by block never sits on the host whole.
+        center: the prefilter's centre [dim] (None: uncentred)."""
+        ctr = None if center is None else _f32(center).reshape(-1)
+        if ctr is not None and ctr.shape[0] != dim:
+            raise Fi8Error(1, f"gpu: center len {ctr.shape[0]} != dim {dim}")
+        words = (dim + 63) // 64
+        h = C.c_void_p()
+        check(lib().fi8_bin_index_create_empty(self.ctx.handle, n, dim, words, _p(ctr) if ctr is not None else None,
+                                               overquery, id_base, C.byref(h)))
+        return BinaryI8Index._adopt(self.ctx, h, n, dim, words, overquery, id_base)
+
     def NewBinaryI8Index(self, codes, words: int, center, bq, scales, n: int, dim: int,
                          overquery: int = 16, id_base: int = 0) -> "BinaryI8Index":
         """A device FlatBinaryI8 shard from the prefilter's packed codes
@@ -397,6 +412,20 @@ class BinaryI8Index:
         self.overquery = max(int(overquery), 1)
         self.id_base = id_base
         return self
+
+    def upload_rows(self, row0: int, codes, bq, scales) -> None:
+        """Rows [row0, row0 + len(scales)): packed codes [rows, words] uint64,
+        int8 rows [rows, dim] and scales (fi8_bin_upload_rows)."""
+        codes = np.ascontiguousarray(codes, dtype=np.uint64)
+        bq = np.ascontiguousarray(bq, dtype=np.int8)
+        scales = _f32(scales).reshape(-1)
+        rows = scales.shape[0]
+        if codes.size != rows * self.words or bq.size != rows * self.dim:
+            raise Fi8Error(1, "gpu: binary upload shape mismatch")
+        check(lib().fi8_bin_upload_rows(self._h, row0, _p(codes), _p(bq), _p(scales), rows))
+
+    def upload_finish(self) -> None:
+        check(lib().fi8_bin_upload_finish(self._h))
 
     def center(self):
         """The prefilter's centre (float32 [dim]), or None when uncentred."""

@@ -135,6 +135,9 @@ struct fi8_index {
   size_t lvl2_cap = 0;
   unsigned int* d_err = nullptr;
   unsigned int* h_err = nullptr;
+  // the batched path's redo gate: set (on the device) when a batch's select
+  // dropped candidates, which opens the gated exact redo launched after it
+  unsigned int* d_redo = nullptr;
 
   // staging for the host-pointer entry points
   float* d_q = nullptr;
@@ -310,6 +313,7 @@ static void index_free(fi8_index* x) {
   cudaFree(x->d_lvl1);
   cudaFree(x->d_lvl2);
   cudaFree(x->d_err);
+  cudaFree(x->d_redo);
   cudaFree(x->d_q);
   cudaFree(x->d_keys);
   cudaFree(x->d_scores);
@@ -359,10 +363,12 @@ static int index_alloc(fi8_ctx* ctx, int64_t n, int32_t dim, int64_t id_base, co
   if (e == cudaSuccess) e = cudaMalloc(&x->d_codes, (size_t)x->n_alloc * dpad);
   if (e == cudaSuccess) e = cudaMalloc(&x->d_scales, (size_t)x->n_alloc * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&x->d_err, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMalloc(&x->d_redo, sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaMallocHost(&x->h_err, sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaMemsetAsync(x->d_codes, 0, (size_t)x->n_alloc * dpad, x->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(x->d_scales, 0, (size_t)x->n_alloc * sizeof(float), x->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(x->d_redo, 0, sizeof(unsigned int), x->stream);
   if (e != cudaSuccess) {
     const int rc = cuda_fail(e, "gpu: device allocation failed");
     index_free(x);
@@ -601,14 +607,24 @@ static int32_t grid_ctas(fi8_index* x, const ScanParams& p) {
   return (int32_t)std::max<int64_t>(G, 1);
 }
 
+// gate: null for a plain launch; otherwise the launches are the batched
+// path's exact redo and run only when *gate is set (timed as FI8_KERNEL_REDO).
 static int launch_topk_scan(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
-                            cudaStream_t st) {
+                            cudaStream_t st, const unsigned int* gate = nullptr) {
   ScanGeometry geo;
   if (!scan_geometry(x->dpad, k, true, &geo))
     return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d beyond the device top-K)", k);
   ScanParams p = base_params(x, geo);
-  const int32_t G = grid_ctas(x, p);
-  const int32_t Mc = std::min(M, kScanMaxM);
+  int32_t G = grid_ctas(x, p);
+  int32_t Mc = std::min(M, kScanMaxM);
+  if (gate) {
+    // A gated launch costs its CTAs' start and exit even when closed, so the
+    // redo keeps each launch to about one wave: up to sm_count queries per
+    // launch, sm_count / queries CTAs each (at least one). When open it
+    // streams the corpus once per query all the same, on every SM.
+    Mc = std::min<int32_t>(M, std::max<int32_t>(kScanMaxM, x->sm_count));
+    G = std::max<int32_t>(1, std::min<int32_t>(G, x->sm_count / Mc));
+  }
   int rc = ensure_topk_scratch(x, Mc, geo.kp, G, st);
   if (rc != FI8_OK) return rc;
   p.k = k;
@@ -619,6 +635,7 @@ static int launch_topk_scan(fi8_index* x, const float* d_q, int32_t M, int32_t k
   p.counter2 = x->d_counter2;
   p.lvl1 = x->d_lvl1;
   p.lvl2 = x->d_lvl2;
+  p.gate = gate;
   for (int32_t m0 = 0; m0 < M; m0 += Mc) {
     const int32_t mm = std::min(Mc, M - m0);
     p.q = d_q + (size_t)m0 * x->dim;
@@ -626,7 +643,10 @@ static int launch_topk_scan(fi8_index* x, const float* d_q, int32_t M, int32_t k
     cudaEvent_t t0 = timer_begin(x, st);
     cudaError_t e = scan_launch(p, true, mm, G, st);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(topk)");
-    timer_end(x, st, t0, FI8_KERNEL_SCAN, scan_bytes(x, mm));
+    if (gate)
+      timer_end(x, st, t0, FI8_KERNEL_REDO, 0.0);
+    else
+      timer_end(x, st, t0, FI8_KERNEL_SCAN, scan_bytes(x, mm));
     x->last_launches++;
   }
   return FI8_OK;
@@ -769,11 +789,32 @@ static int launch_topk_gemm(fi8_index* x, const GemmCorpus& corpus, const float*
   return FI8_OK;
 }
 
+// After a batched top-k: the latch moves the selects' dropped-candidate flag
+// into the index's redo gate, then the per-query scan (which has no
+// candidate buffer) recomputes the batch into d_keys, gated on that flag. The
+// gated launches return at once when nothing was dropped, so every answer is
+// exact in stream order, with no host round trip. When no scan form exists
+// for this k the flag stays set and surfaces at the next sync.
+static int launch_topk_redo(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
+                            cudaStream_t st) {
+  ScanGeometry geo;
+  if (!scan_geometry(x->dpad, k, true, &geo)) return FI8_OK;
+  cudaEvent_t t0 = timer_begin(x, st);
+  cudaError_t e = overflow_latch_launch(x->d_err, x->d_redo, st);
+  if (e != cudaSuccess) return cuda_fail(e, "overflow_latch_launch");
+  timer_end(x, st, t0, FI8_KERNEL_REDO, 0.0);
+  x->last_launches++;
+  return launch_topk_scan(x, d_q, M, k, d_keys, st, x->d_redo);
+}
+
 static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uint64_t* d_keys,
                        cudaStream_t st) {
   x->last_launches = 0;
-  if (M >= x->gemm_min_batch && x->has_tmB)
-    return launch_topk_gemm(x, GemmCorpus{&x->tmB, x->d_scales, nullptr, 0}, d_q, M, k, d_keys, st);
+  if (M >= x->gemm_min_batch && x->has_tmB) {
+    const int rc = launch_topk_gemm(x, GemmCorpus{&x->tmB, x->d_scales, nullptr, 0}, d_q, M, k, d_keys, st);
+    if (rc != FI8_OK) return rc;
+    return launch_topk_redo(x, d_q, M, k, d_keys, st);
+  }
   return launch_topk_scan(x, d_q, M, k, d_keys, st);
 }
 
@@ -870,8 +911,9 @@ static int stage_keep(fi8_index* x, const uint64_t* keep, int64_t nbits, const u
   return FI8_OK;
 }
 
-// Top-k of the M queries staged in x->d_q into x->h_keys (M*k keys), with the
-// batched path's overflow fallback. Caller holds x->mu and the device.
+// Top-k of the M queries staged in x->d_q into x->h_keys (M*k keys). A
+// batched answer that dropped candidates is redone on the device inside
+// launch_topk. Caller holds x->mu and the device.
 static int topk_staged(fi8_index* x, int32_t M, int32_t k) {
   const size_t nk = (size_t)M * k;
   int rc;
@@ -883,20 +925,6 @@ static int topk_staged(fi8_index* x, int32_t M, int32_t k) {
   FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
            "D2H err");
   FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
-  if (*x->h_err == 2u) {
-    // The batched path dropped candidates (a row range admitted more than its
-    // per-query buffer holds, e.g. on a corpus ordered against the queries).
-    // Its answer is incomplete; recompute the batch with the per-query scan,
-    // which has no such limit.
-    *x->h_err = 0;
-    FI8_CUDA(cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream), "memset err");
-    if ((rc = launch_topk_scan(x, x->d_q, M, k, x->d_keys, x->stream)) != FI8_OK) return rc;
-    FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
-             "D2H keys");
-    FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
-             "D2H err");
-    FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
-  }
   return check_device_error(x);
 }
 
@@ -1179,22 +1207,15 @@ constexpr int32_t kBinMaxCand = kMergeMaxK < kRerankMaxCand ? kMergeMaxK : kRera
 constexpr int32_t kBinMaxM = 16;
 }  // namespace
 
-// The prefilter (packing, the distance pass with its histogram, the cut and
-// the shortlist) for M queries. sorted: each query's keys sorted descending,
-// as a cross-shard key merge needs. Caller holds b->ix->mu and the device.
-// allow_tensor = false keeps a batch on the popcount pass whatever the
-// tensor-prefilter setting (the exact redo after a GEMM candidate overflow).
-static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
-                                bool sorted, cudaStream_t st, bool allow_tensor = true) {
+// The popcount prefilter (packing, the distance pass with its histogram, the
+// cut and the shortlist) for M queries. sorted: each query's keys sorted
+// descending, as a cross-shard key merge needs. gate: null for a plain
+// launch; otherwise the launches are the exact redo of a tensor-core
+// shortlist and run only when *gate is set (timed as FI8_KERNEL_REDO).
+// Caller holds b->ix->mu and the device.
+static int launch_bin_popcount(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
+                               bool sorted, cudaStream_t st, const unsigned int* gate = nullptr) {
   fi8_index* x = b->ix;
-  if (allow_tensor && b->d_sign && b->tensor_min_m > 0 && M >= b->tensor_min_m) {
-    // The shortlist is the cand best rows under (distance asc, id asc); as
-    // packed keys (-distance, id) that is the exact top-cand the GEMM path
-    // selects, sorted descending (so it also serves a key merge).
-    if (cand > kBinMaxCand)
-      return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond %d)", cand, kBinMaxCand);
-    return launch_topk_gemm(x, GemmCorpus{&b->tmS, nullptr, b->d_center, x->dim}, d_q, M, cand, d_keys, st);
-  }
   const int32_t bpad = b->wpad * 8;
   const int32_t nbins = bpad * 8 + 1;
   ScanGeometry geo;
@@ -1218,27 +1239,61 @@ static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t
   p.hist = b->d_hist;
   p.nbins = nbins;
   p.qbits = b->d_qbits;
+  p.gate = gate;
   const int32_t G = grid_ctas(x, p);
+  auto timed = [&](cudaEvent_t t0, int kind, double bytes) {
+    if (gate)
+      timer_end(x, st, t0, FI8_KERNEL_REDO, 0.0);
+    else
+      timer_end(x, st, t0, kind, bytes);
+  };
   for (int32_t m0 = 0; m0 < M; m0 += Mc) {
     const int32_t mm = std::min(Mc, M - m0);
     const float* q = d_q + (size_t)m0 * x->dim;
     cudaEvent_t t0 = timer_begin(x, st);
-    cudaError_t e = binary_prep_launch(q, mm, x->dim, b->d_center, b->wpad, b->d_qbits, b->d_hist, nbins, st);
+    cudaError_t e = binary_prep_launch(q, mm, x->dim, b->d_center, b->wpad, b->d_qbits, b->d_hist, nbins, st, gate);
     if (e != cudaSuccess) return cuda_fail(e, "binary_prep_launch");
-    timer_end(x, st, t0, FI8_KERNEL_QUANTIZE, (double)mm * x->dim * 4);
+    timed(t0, FI8_KERNEL_QUANTIZE, (double)mm * x->dim * 4);
     t0 = timer_begin(x, st);
     e = scan_launch(p, false, mm, G, st, true);
     if (e != cudaSuccess) return cuda_fail(e, "scan_launch(binary)");
     // the packed codes once per query, plus the u16 distance written per row
-    timer_end(x, st, t0, FI8_KERNEL_SCAN, (double)mm * ((double)x->n * bpad + (double)bpad + 2.0 * x->n));
+    timed(t0, FI8_KERNEL_SCAN, (double)mm * ((double)x->n * bpad + (double)bpad + 2.0 * x->n));
     t0 = timer_begin(x, st);
     e = shortlist_launch(b->d_dist, x->n, x->n_alloc, mm, b->d_hist, nbins, cand, P, b->d_counts, x->id_base,
-                         d_keys + (size_t)m0 * cand, sorted, st);
+                         d_keys + (size_t)m0 * cand, sorted, st, gate);
     if (e != cudaSuccess) return cuda_fail(e, "shortlist_launch");
-    timer_end(x, st, t0, FI8_KERNEL_SELECT, (double)mm * 2.0 * 2.0 * x->n);
+    timed(t0, FI8_KERNEL_SELECT, (double)mm * 2.0 * 2.0 * x->n);
     x->last_launches += sorted ? 5 : 4;
   }
   return FI8_OK;
+}
+
+// The prefilter for M queries: the tensor-core GEMM for batches of at least
+// the tensor-prefilter size (with its gated popcount redo after it: a row
+// range that admitted more candidates than its per-query buffer holds, e.g.
+// on a corpus ordered against the query, leaves an incomplete shortlist,
+// which the popcount pass, without such a buffer, recomputes exactly), the
+// popcount pass otherwise. Caller holds b->ix->mu and the device.
+static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys,
+                                bool sorted, cudaStream_t st) {
+  fi8_index* x = b->ix;
+  if (b->d_sign && b->tensor_min_m > 0 && M >= b->tensor_min_m) {
+    // The shortlist is the cand best rows under (distance asc, id asc); as
+    // packed keys (-distance, id) that is the exact top-cand the GEMM path
+    // selects, sorted descending (so it also serves a key merge).
+    if (cand > kBinMaxCand)
+      return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond %d)", cand, kBinMaxCand);
+    int rc = launch_topk_gemm(x, GemmCorpus{&b->tmS, nullptr, b->d_center, x->dim}, d_q, M, cand, d_keys, st);
+    if (rc != FI8_OK) return rc;
+    cudaEvent_t t0 = timer_begin(x, st);
+    cudaError_t e = overflow_latch_launch(x->d_err, x->d_redo, st);
+    if (e != cudaSuccess) return cuda_fail(e, "overflow_latch_launch");
+    timer_end(x, st, t0, FI8_KERNEL_REDO, 0.0);
+    x->last_launches++;
+    return launch_bin_popcount(b, d_q, M, cand, d_keys, sorted, st, x->d_redo);
+  }
+  return launch_bin_popcount(b, d_q, M, cand, d_keys, sorted, st);
 }
 
 static int launch_bin_rerank(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand,
@@ -1305,6 +1360,86 @@ int fi8_bin_index_create(fi8_ctx* ctx, const uint64_t* codes, int32_t words, con
   }
   *out = b;
   return FI8_OK;
+}
+
+int fi8_bin_index_create_empty(fi8_ctx* ctx, int64_t n, int32_t dim, int32_t words, const float* center,
+                               int32_t overquery, int64_t id_base, fi8_bin** out) {
+  if (!out) return fail(FI8_ERR_ARG, "fi8_bin_index_create_empty: null out");
+  *out = nullptr;
+  if (!ctx) return fail(FI8_ERR_ARG, "fi8_bin_index_create_empty: null ctx");
+  if (dim <= 0 || words != (dim + 63) / 64)  // linalg.PackedWords
+    return fail(FI8_ERR_ARG, "fi8_bin_index_create_empty: words=%d does not match dim %d", words, dim);
+  const int32_t wpad = (words + 1) / 2 * 2;
+  if (wpad * 8 > kScanMaxDpad)
+    return fail(FI8_ERR_DECLINED, "fi8_bin_index_create_empty: dim %d exceeds the supported packed width", dim);
+  fi8_index* ix = nullptr;
+  int rc = fi8_index_create_empty(ctx, n, dim, id_base, &ix);
+  if (rc != FI8_OK) return rc;
+  fi8_bin* b = new (std::nothrow) fi8_bin;
+  if (!b) {
+    fi8_index_destroy(ix);
+    return fail(FI8_ERR_OOM, "fi8_bin_index_create_empty: host allocation");
+  }
+  b->ix = ix;
+  b->words = words;
+  b->wpad = wpad;
+  b->over = overquery < 1 ? 1 : overquery;
+  DeviceGuard g(ix->device);
+  const size_t bytes = (size_t)ix->n_alloc * wpad * 8;
+  cudaError_t e = cudaMalloc(&b->d_bits, bytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_bits, 0, bytes, ix->stream);
+  if (e == cudaSuccess && center) {
+    e = cudaMalloc(&b->d_center, (size_t)dim * sizeof(float));
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(b->d_center, center, (size_t)dim * sizeof(float), cudaMemcpyHostToDevice, ix->stream);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
+  if (e != cudaSuccess) {
+    rc = cuda_fail(e, "gpu: binary index allocation failed");
+    fi8_bin_index_destroy(b);
+    return rc;
+  }
+  *out = b;
+  return FI8_OK;
+}
+
+int fi8_bin_upload_rows(fi8_bin* b, int64_t row0, const uint64_t* codes, const int8_t* i8, const float* scales,
+                        int64_t rows) {
+  if (!b) return fail(FI8_ERR_ARG, "fi8_bin_upload_rows: null index");
+  if (rows == 0) return FI8_OK;
+  fi8_index* x = b->ix;
+  if (rows < 0 || row0 < 0 || row0 + rows > x->n || !codes || !i8 || !scales)
+    return fail(FI8_ERR_ARG, "fi8_bin_upload_rows: rows [%lld, %lld) outside [0, %lld) or null data",
+                (long long)row0, (long long)(row0 + rows), (long long)x->n);
+  std::lock_guard<std::mutex> lk(x->mu);
+  DeviceGuard g(x->device);
+  if (b->d_sign)
+    return fail(FI8_ERR_ARG, "fi8_bin_upload_rows: the tensor-core prefilter's sign rows are built; "
+                             "upload every row first");
+  if (!x->up_stage) {
+    x->up_stage = new (std::nothrow) PinnedStager;
+    if (!x->up_stage) return fail(FI8_ERR_OOM, "fi8_bin_upload_rows: host allocation");
+    cudaError_t e = x->up_stage->init();
+    if (e != cudaSuccess) {
+      delete x->up_stage;
+      x->up_stage = nullptr;
+      return cuda_fail(e, "gpu: pinned staging buffers");
+    }
+  }
+  const size_t wb = (size_t)b->words * 8;
+  cudaError_t e = x->up_stage->put_rows(x->d_codes + (size_t)row0 * x->dpad, x->dpad, i8, x->dim, x->dim, rows,
+                                        x->stream);
+  if (e == cudaSuccess) e = x->up_stage->put_rows(x->d_scales + row0, 4, scales, 4, 4, rows, x->stream);
+  if (e == cudaSuccess)
+    e = x->up_stage->put_rows(b->d_bits + (size_t)row0 * b->wpad, (size_t)b->wpad * 8, codes, wb, wb, rows,
+                              x->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "gpu: device upload failed");
+  return FI8_OK;
+}
+
+int fi8_bin_upload_finish(fi8_bin* b) {
+  if (!b) return fail(FI8_ERR_ARG, "fi8_bin_upload_finish: null index");
+  return fi8_index_upload_finish(b->ix);
 }
 
 int fi8_bin_index_create_f32(fi8_ctx* ctx, const float* vecs, const uint8_t* valid, int64_t n, int32_t dim,
@@ -1510,26 +1645,16 @@ int fi8_bin_query_topk_keep(fi8_bin* b, const float* q, int32_t M, int32_t k, co
   if ((rc = ensure_host(&x->h_keys, &x->h_keys_cap, nk, "pinned keys")) != FI8_OK) return rc;
   if (cand > kBinMaxCand)
     return fail(FI8_ERR_DECLINED, "gpu: binary TopK declined (cand=%lld beyond %d)", (long long)cand, kBinMaxCand);
-  for (int pass = 0; pass < 2; pass++) {
-    // pass 1 runs only after the tensor-core prefilter dropped candidates (a
-    // row range admitted more than its per-query buffer holds, e.g. on a
-    // corpus ordered against the queries): its shortlist is incomplete, so
-    // the popcount pass, which has no such limit, redoes it exactly
-    if ((rc = launch_bin_prefilter(b, x->d_q, M, (int32_t)cand, b->d_short, false, x->stream, pass == 0)) !=
-        FI8_OK)
-      return rc;
-    if ((rc = launch_bin_rerank(b, x->d_q, M, b->d_short, (int32_t)cand, k, x->d_keys, x->stream)) != FI8_OK)
-      return rc;
-    FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
-             "D2H keys");
-    FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
-             "D2H err");
-    FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
-    // only the GEMM's select sets the overflow flag (2) alone
-    if (*x->h_err != 2u || pass == 1) break;
-    *x->h_err = 0;
-    FI8_CUDA(cudaMemsetAsync(x->d_err, 0, sizeof(unsigned int), x->stream), "memset err");
-  }
+  // (a tensor-core shortlist that dropped candidates is redone on the
+  // device inside launch_bin_prefilter)
+  if ((rc = launch_bin_prefilter(b, x->d_q, M, (int32_t)cand, b->d_short, false, x->stream)) != FI8_OK) return rc;
+  if ((rc = launch_bin_rerank(b, x->d_q, M, b->d_short, (int32_t)cand, k, x->d_keys, x->stream)) != FI8_OK)
+    return rc;
+  FI8_CUDA(cudaMemcpyAsync(x->h_keys, x->d_keys, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, x->stream),
+           "D2H keys");
+  FI8_CUDA(cudaMemcpyAsync(x->h_err, x->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost, x->stream),
+           "D2H err");
+  FI8_CUDA(cudaStreamSynchronize(x->stream), "sync");
   if ((rc = check_device_error(x)) != FI8_OK) return rc;
   return fi8_keys_unpack(x->h_keys, (int64_t)nk, out_idx, out_score);
 }

@@ -34,7 +34,9 @@ constexpr int kRerankRowsPerCta = kRerankThreads / 8;  // one 8-lane group per r
 
 // One CTA per query; thread per dimension, warp ballots build the words.
 __global__ void __launch_bounds__(1024) binary_prep_kernel(const float* q, int d, const float* center, int wpad,
-                                                           uint64_t* qbits, unsigned int* hist, int nbins) {
+                                                           uint64_t* qbits, unsigned int* hist, int nbins,
+                                                           const unsigned int* gate) {
+  if (gate && *reinterpret_cast<const volatile unsigned int*>(gate) == 0u) return;  // a closed redo gate
   const int y = blockIdx.x;
   const float* row = q + (size_t)y * d;
   uint32_t* out = reinterpret_cast<uint32_t*>(qbits + (size_t)y * wpad);
@@ -137,10 +139,12 @@ __device__ __forceinline__ void load8(const uint16_t* dist, int64_t r, int64_t h
 __global__ void __launch_bounds__(kSegThreads) shortlist_count_kernel(const uint16_t* dist, int64_t n,
                                                                       int64_t dstride, const unsigned int* hist,
                                                                       int nbins,
-                                                                      int64_t cand, int P, unsigned int* counts) {
+                                                                      int64_t cand, int P, unsigned int* counts,
+                                                                      const unsigned int* gate) {
   const int p = blockIdx.x, y = blockIdx.y;
   pdl_launch_dependents();
   pdl_wait_prior();  // the distance pass has completed
+  if (gate && *reinterpret_cast<const volatile unsigned int*>(gate) == 0u) return;
   int t;
   int64_t lt_all;
   find_cut(hist + (size_t)y * nbins, nbins, cand, &t, &lt_all);
@@ -210,10 +214,12 @@ __global__ void __launch_bounds__(kSegThreads) shortlist_emit_kernel(const uint1
                                                                      int64_t dstride, const unsigned int* hist,
                                                                      int nbins,
                                                                      int64_t cand, int P, const unsigned int* counts,
-                                                                     uint32_t id_base, uint64_t* out) {
+                                                                     uint32_t id_base, uint64_t* out,
+                                                                     const unsigned int* gate) {
   const int p = blockIdx.x, y = blockIdx.y;
   pdl_launch_dependents();
   pdl_wait_prior();  // the segment counts are complete
+  if (gate && *reinterpret_cast<const volatile unsigned int*>(gate) == 0u) return;
   int t;
   int64_t lt_all;
   find_cut(hist + (size_t)y * nbins, nbins, cand, &t, &lt_all);
@@ -300,12 +306,14 @@ __global__ void __launch_bounds__(256) sign_rows_kernel(const uint64_t* bits, in
 }
 
 // One CTA per query: sort its cand keys descending (for the cross-shard merge).
-__global__ void __launch_bounds__(1024) sort_keys_kernel(uint64_t* keys, int cand, int candp) {
+__global__ void __launch_bounds__(1024) sort_keys_kernel(uint64_t* keys, int cand, int candp,
+                                                         const unsigned int* gate) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* buf = reinterpret_cast<uint64_t*>(smem);
   uint64_t* ky = keys + (size_t)blockIdx.x * cand;
   pdl_launch_dependents();
   pdl_wait_prior();
+  if (gate && *reinterpret_cast<const volatile unsigned int*>(gate) == 0u) return;
   for (int i = threadIdx.x; i < candp; i += 1024) buf[i] = i < cand ? ky[i] : kEmptyKey;
   named_sync(1, 1024);
   group_sort_desc<1024>(buf, candp, threadIdx.x, 1);
@@ -408,9 +416,10 @@ int pow2_ceil(int x) {
 }  // namespace
 
 cudaError_t binary_prep_launch(const float* q, int32_t M, int32_t d, const float* center, int32_t wpad,
-                               uint64_t* qbits, unsigned int* hist, int32_t nbins, cudaStream_t stream) {
+                               uint64_t* qbits, unsigned int* hist, int32_t nbins, cudaStream_t stream,
+                               const unsigned int* gate) {
   if (M <= 0 || d <= 0 || wpad * 64 < d) return cudaErrorInvalidValue;
-  binary_prep_kernel<<<M, 1024, 0, stream>>>(q, d, center, wpad, qbits, hist, nbins);
+  binary_prep_kernel<<<M, 1024, 0, stream>>>(q, d, center, wpad, qbits, hist, nbins, gate);
   return cudaGetLastError();
 }
 
@@ -419,20 +428,20 @@ int32_t shortlist_segments(int32_t sm_count) { return 4 * (sm_count > 0 ? sm_cou
 cudaError_t shortlist_launch(const uint16_t* dist, int64_t n, int64_t dstride, int32_t M, const unsigned int* hist,
                              int32_t nbins,
                              int32_t cand, int32_t P, unsigned int* counts, uint32_t id_base, uint64_t* out,
-                             bool sorted, cudaStream_t stream) {
+                             bool sorted, cudaStream_t stream, const unsigned int* gate) {
   if (M <= 0 || cand <= 0 || P <= 0 || dstride % kRowsPerThread != 0) return cudaErrorInvalidValue;
   dim3 grid((unsigned)P, (unsigned)M);
   cudaError_t e = launch_pdl(shortlist_count_kernel, grid, dim3(kSegThreads), 0, stream, dist, n, dstride, hist,
-                             nbins, (int64_t)cand, P, counts);
+                             nbins, (int64_t)cand, P, counts, gate);
   if (e != cudaSuccess) return e;
   e = launch_pdl(shortlist_emit_kernel, grid, dim3(kSegThreads), 0, stream, dist, n, dstride, hist, nbins,
-                 (int64_t)cand, P, (const unsigned int*)counts, id_base, out);
+                 (int64_t)cand, P, (const unsigned int*)counts, id_base, out, gate);
   if (e != cudaSuccess || !sorted) return e;
   if (cand > kRerankMaxCand) return cudaErrorInvalidValue;
   const int candp = pow2_ceil(cand);
   e = cudaFuncSetAttribute(sort_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRerankMaxCand * 8);
   if (e != cudaSuccess) return e;
-  return launch_pdl(sort_keys_kernel, dim3((unsigned)M), dim3(1024), (size_t)candp * 8, stream, out, cand, candp);
+  return launch_pdl(sort_keys_kernel, dim3((unsigned)M), dim3(1024), (size_t)candp * 8, stream, out, cand, candp, gate);
 }
 
 cudaError_t sign_rows_launch(const uint64_t* bits, int64_t n, int64_t n_alloc, int32_t wpad, int32_t d, int32_t dpad,

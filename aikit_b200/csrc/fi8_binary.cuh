@@ -12,8 +12,11 @@ namespace fi8 {
 // qbits[y][w] = the packed sign bits of (q[y] - center) (center may be null):
 // bit i%64 of word i/64 is set iff q[y][i] - center[i] >= 0 in float32, bits
 // past d are zero; wpad = row pitch in words. Also zeroes hist[y][0..nbins).
+// gate (optional): the launch does nothing unless *gate != 0 (the exact redo
+// of a tensor-core shortlist that dropped candidates).
 cudaError_t binary_prep_launch(const float* q, int32_t M, int32_t d, const float* center, int32_t wpad,
-                               uint64_t* qbits, unsigned int* hist, int32_t nbins, cudaStream_t stream);
+                               uint64_t* qbits, unsigned int* hist, int32_t nbins, cudaStream_t stream,
+                               const unsigned int* gate = nullptr);
 
 // Row segments the shortlist kernels split a corpus into (counts holds
 // [M][P][2] entries).
@@ -24,9 +27,10 @@ int32_t shortlist_segments(int32_t sm_count);
 // (-distance, id_base + row) of prefilterHist's cand rows -- every row below
 // the cut t, then the first ties at t in id order -- 0 past the rows there
 // are. sorted: also sort each query's keys descending (for a key merge).
+// gate as for binary_prep_launch.
 cudaError_t shortlist_launch(const uint16_t* dist, int64_t n, int64_t dstride, int32_t M, const unsigned int* hist,
                              int32_t nbins, int32_t cand, int32_t P, unsigned int* counts, uint32_t id_base,
-                             uint64_t* out, bool sorted, cudaStream_t stream);
+                             uint64_t* out, bool sorted, cudaStream_t stream, const unsigned int* gate = nullptr);
 
 // CTAs (slices of the shortlist) one query's rerank uses; parts holds
 // [rerank_parts(cand)][M][k] keys.

@@ -786,6 +786,17 @@ __global__ void __launch_bounds__(NT)
   }
 }
 
+// One thread, after a batch's last select: move the dropped-candidate flag
+// (bit 1 of the error word) into the redo gate and clear it there, so the
+// gated redo that follows runs exactly when this batch needs it and the
+// flag never outlives its batch.
+__global__ void overflow_latch_kernel(unsigned int* err, unsigned int* gate) {
+  pdl_launch_dependents();
+  pdl_wait_prior();  // the batch's selects have completed
+  const unsigned int v = atomicAnd(err, ~2u);
+  *gate = (v >> 1) & 1u;
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -866,6 +877,10 @@ cudaError_t mma_probe_launch(int32_t G, int64_t iters, unsigned int* err, cudaSt
 }
 
 double mma_probe_ops(int32_t G, int64_t iters) { return 2.0 * 128 * 256 * kGemmBK * (double)iters * G; }
+
+cudaError_t overflow_latch_launch(unsigned int* err, unsigned int* gate, cudaStream_t stream) {
+  return launch_pdl(overflow_latch_kernel, dim3(1), dim3(1), 0, stream, err, gate);
+}
 
 int32_t select_max_k() { return 4096; }  // kp <= 4096 keeps the select buffer at 64 KB
 

@@ -69,6 +69,10 @@ cudaError_t select_launch(int32_t M, int32_t k, int32_t kp, uint64_t* topk, unsi
 
 int32_t select_max_k();
 
+// After a batch's last select: *gate = whether a select dropped candidates
+// (err bit 1), and that bit cleared. A gated redo launch follows it.
+cudaError_t overflow_latch_launch(unsigned int* err, unsigned int* gate, cudaStream_t stream);
+
 // Tensor-pipe probe: G CTAs (one per SM) issue iters x 4 back-to-back
 // kind::i8 MMAs (M=128, N=256, K=32) on shared-memory operands; ops done.
 cudaError_t mma_probe_launch(int32_t G, int64_t iters, unsigned int* err, cudaStream_t stream);

@@ -98,6 +98,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) scan_kernel(ScanParams p) {
   const int64_t my_tiles = (p.ntiles > cta) ? (p.ntiles - cta + G - 1) / G : 0;
 
   pdl_launch_dependents();
+  if (p.gate) {
+    // a gated launch: nothing is read or written unless the gate is open
+    // (uniform over the grid, so every thread of every CTA returns alike)
+    pdl_wait_prior();
+    if (*reinterpret_cast<const volatile unsigned int*>(p.gate) == 0u) return;
+  }
   if (tid == 0) {
     for (int s = 0; s < S; s++) {
       mbar_init(&s_full[s], 1);
@@ -513,7 +519,7 @@ cudaError_t scan_launch(const ScanParams& p, bool topk, int32_t M, int32_t G, cu
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)G, (unsigned)M);
-  if (binary)  // follows the query packing kernel
+  if (binary || p.gate)  // follows the query packing kernel, or a gated redo chain
     return launch_pdl(fn, grid, dim3(kBlockThreads), (size_t)p.smem_bytes, stream, p);
   void* args[] = {const_cast<ScanParams*>(&p)};
   return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, dim3(kBlockThreads), args,

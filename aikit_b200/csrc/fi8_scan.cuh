@@ -43,6 +43,11 @@ struct ScanParams {
   // score mode
   float* out_scores;         // [M][n]
   unsigned int* err;         // device error flags (bit 0: wait timeout)
+  // optional gate: when set, the launch runs only if *gate != 0 (read after
+  // the previous kernel on the stream completes); otherwise every CTA
+  // returns at once. The batched path's exact redo after a dropped
+  // candidate is such a launch.
+  const unsigned int* gate;
 };
 
 struct ScanGeometry {

@@ -4,8 +4,9 @@
  * two-stage path.
  *
  * The ABI is what a Go adapter registered through ann.RegisterBackend
- * (ann/backend.go:139) binds with cgo or a purego-style dlopen; INTEGRATION.md
- * shows that adapter. Plain pointers and sizes only, no exceptions across the
+ * (ann/backend.go:139) binds, cgo-free through a purego-style dlopen (as the
+ * reference's gocudrv binds libcuda, gpu/cuda.go:11,54) or with cgo. Plain
+ * pointers and sizes only, no exceptions across the
  * boundary, integer status codes, and no CPU fallback: a call either runs on
  * the GPU or returns an error, which the Go seam already treats as "decline,
  * use the next tier" (ann/flat_i8.go:191-198, ann/backend.go:86-122).
@@ -149,8 +150,12 @@ int fi8_gemm_plan(int64_t n, int32_t M, int32_t k, int64_t* out_bounds, int32_t 
  * d_keys [M*k] packed uint64 keys (decode with fi8_keys_unpack), both device
  * pointers; stream is a cudaStream_t (NULL = the legacy default stream, as in
  * CUDA). Does not synchronize; device-side errors surface at the next
- * fi8_index_sync, a dropped-candidate overflow among them (fi8_topk_batch
- * redoes such a batch on the scan instead). Unlike fi8_topk_batch it accepts
+ * fi8_index_sync. The answer is exact: a batch on the GEMM path whose row
+ * range admitted more candidates than its per-query buffer holds (a corpus
+ * ordered against the query) is recomputed on the device, in stream order,
+ * by the per-query scan -- launches gated on the batch's own overflow flag,
+ * which return at once when nothing was dropped. d_q is read until the
+ * call's work completes on the stream. Unlike fi8_topk_batch it accepts
  * k >= n (a row shard smaller than k yields all of its
  * rows, then empty keys). Calls on one index must not overlap on the GPU (they
  * share the index's scratch); issue them on one stream. */
@@ -184,7 +189,8 @@ int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
 #define FI8_KERNEL_SELECT 2   /* per-query exact select of the candidates */
 #define FI8_KERNEL_QUANTIZE 3 /* query quantization / sign-bit packing */
 #define FI8_KERNEL_RERANK 4   /* FlatBinaryI8 shortlist rerank */
-#define FI8_KERNEL_KINDS 5
+#define FI8_KERNEL_REDO 5     /* the batched path's gated exact redo (see fi8_topk_batch_async) */
+#define FI8_KERNEL_KINDS 6
 
 /* Totals over the launches timed since the last reset, per kernel class:
  * launches[i], ms[i] (sum of per-launch device durations) and bytes[i]
@@ -200,7 +206,10 @@ int fi8_index_kernel_times(fi8_index* idx, int64_t* launches, double* ms, double
 int fi8_index_kernel_log(fi8_index* idx, int32_t cap, int32_t* count, int32_t* kinds, double* ms, double* bytes);
 
 /* Number of kernels the index's last query call launched (scan: one per 64
- * queries; batched: quantize + a GEMM and a select per row range). */
+ * queries; batched: quantize + a GEMM and a select per row range, then the
+ * gated redo -- a latch and one scan per 64 queries, or the popcount
+ * prefilter's launches for a tensor-core shortlist -- which return at once
+ * unless a candidate was dropped). */
 int fi8_index_last_launch_count(fi8_index* idx, int32_t* out);
 
 /* Wait for the index's stream and report any device-side error flag. */
@@ -248,6 +257,25 @@ int fi8_bin_index_create(fi8_ctx* ctx, const uint64_t* codes, int32_t words, con
                          int64_t id_base, fi8_bin** out);
 int fi8_bin_index_destroy(fi8_bin* b);
 
+/* Streamed and paged sources for a FlatBinaryI8, as fi8_index_create_empty /
+ * fi8_index_upload_rows / fi8_index_upload_finish are for a FlatI8: the
+ * prefilter's codes and the FlatI8 rows of a corpus larger than host RAM
+ * (an FI8 file walked block by block, or rows generated block by block) reach
+ * the device without the whole corpus ever being resident on the host.
+ * fi8_bin_index_create_empty: n rows of dim, all zero, with the prefilter's
+ * centre [dim] (NULL: uncentred; copied). fi8_bin_upload_rows: rows
+ * [row0, row0 + rows) from host codes [rows*words], i8 [rows*dim] and scales
+ * [rows]; the host memory may be reused when the call returns.
+ * fi8_bin_upload_finish: wait for every upload and free the staging buffers.
+ * Uploading every row gives the index fi8_bin_index_create builds from the
+ * same arrays. Upload before fi8_bin_set_tensor_prefilter (it unpacks the
+ * codes already on the device). No counterpart in the reference. */
+int fi8_bin_index_create_empty(fi8_ctx* ctx, int64_t n, int32_t dim, int32_t words, const float* center,
+                               int32_t overquery, int64_t id_base, fi8_bin** out);
+int fi8_bin_upload_rows(fi8_bin* b, int64_t row0, const uint64_t* codes, const int8_t* i8, const float* scales,
+                        int64_t rows);
+int fi8_bin_upload_finish(fi8_bin* b);
+
 /* newFlatBinaryI8 on the device (ann/flat_binary_i8.go:57-62): from f32 rows
  * vecs [n*dim], the FlatI8 rows (quantized as fi8_index_create_f32) and the
  * prefilter's sign codes. valid [n] (NULL = all) marks the rows of the
@@ -288,8 +316,8 @@ int fi8_bin_set_tensor_prefilter(fi8_bin* b, int32_t min_batch);
  * W8A8 score (rerank, :122-153). Declines k <= 0 and k >= n (the reference
  * returns the whole corpus there), and cand above the device limit (2048).
  * A batch on the tensor-core prefilter whose row range admits more candidates
- * than its buffer holds is redone with the popcount pass, so the answer stays
- * exact. */
+ * than its buffer holds is redone on the device with the popcount pass, so the
+ * answer stays exact (as for fi8_bin_prefilter_async). */
 int fi8_bin_query_topk(fi8_bin* b, const float* q, int32_t M, int32_t k, int32_t* out_idx, float* out_score);
 
 /* FlatBinaryI8.QueryFilter (flat_binary_i8.go:83): the keep filter applies in
@@ -309,7 +337,10 @@ int fi8_bin_query_topk_keep(fi8_bin* b, const float* q, int32_t M, int32_t k, co
  * descending, which the key merge needs (the rerank takes any order).
  * fi8_bin_rerank_async: d_short
  * [M*cand] keys (rows of other shards are skipped) -> d_keys [M*k] W8A8 keys,
- * sorted, 0-padded. Stream semantics as fi8_topk_batch_async. */
+ * sorted, 0-padded. Stream semantics as fi8_topk_batch_async: a tensor-core
+ * shortlist that dropped candidates is recomputed by the popcount pass in
+ * stream order (launches gated on that batch's overflow flag), so the keys
+ * are exact. */
 int fi8_bin_prefilter_async(fi8_bin* b, const float* d_q, int32_t M, int32_t cand, uint64_t* d_keys, int32_t sorted,
                             void* stream);
 int fi8_bin_rerank_async(fi8_bin* b, const float* d_q, int32_t M, const uint64_t* d_short, int32_t cand, int32_t k,

@@ -140,6 +140,89 @@ def test_batch_overflow_falls_back_exactly(backend):
     ix.Close()
 
 
+def _against_query_order(r, n, d):
+    """A corpus sorted by ascending score against the first query: every later
+    row beats every earlier one, so a row range admits more candidates than
+    its buffer holds."""
+    bq, bs = r.codes(n)
+    q = r.queries(2)
+    aq, as_ = oracle.quantize_queries(q[:1])
+    order = np.argsort(oracle.w8a8(aq, as_, bq, bs)[0], kind="stable")
+    return np.ascontiguousarray(bq[order]), np.ascontiguousarray(bs[order]), q
+
+
+@pytest.mark.parametrize("M", [2, 70])
+def test_async_overflow_is_exact(backend, M):
+    """The device-resident form on the same corpus: the gated redo runs in
+    stream order, so the keys are exact without a host round trip, the next
+    sync reports no error, and ShardedTopK (the multi-GPU path, here one
+    rank) hands the exact keys on. Batches of 2 (a 64-query tile) and 70 (a
+    128-query tile); the redo's scan runs many queries per launch on few CTAs
+    each."""
+    import torch
+    from aikit_b200.ann import unpack_keys
+    from aikit_b200.dist import ShardedTopK
+    r = synth.Recipe(synth.UNIT, 64, seed=8)
+    n, k = 400_000, 20
+    bq, bs, q2 = _against_query_order(r, n, 64)
+    Q = np.concatenate([q2, r.queries(M, row0=50)])[:M]
+    ix = backend.NewI8Index(bq, bs, n, 64)
+    stream = torch.cuda.Stream()
+    qd = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
+    keys = torch.zeros((M, k), dtype=torch.int64, device="cuda")
+    ix.topk_async(qd.data_ptr(), M, k, keys.data_ptr(), stream.cuda_stream)
+    stream.synchronize()
+    ix.sync()  # no overflow flag is left for the sync
+    sh = ShardedTopK(ix, backend.ctx, 1, stream)
+    merged = sh.topk_async(qd.data_ptr(), M, k)
+    stream.synchronize()
+    ix.sync()
+    widx, wsc = oracle_topk(bq, bs, Q, k)
+    for got in (keys, merged):
+        gi, gs = unpack_keys(got.cpu().numpy().view(np.uint64))
+        assert_same(gi.astype(np.int64), gs, widx, wsc, f"async overflow M={M}")
+    # the redo ran exactly once per call: its scan launches were opened
+    ix.set_kernel_timing(True)
+    ix.topk_async(qd.data_ptr(), M, k, keys.data_ptr(), stream.cuda_stream)
+    stream.synchronize()
+    ix.set_kernel_timing(False)
+    kt = ix.kernel_times()
+    chunk = max(64, backend.ctx.sm_count())  # queries per gated scan launch
+    assert kt["redo_gated"]["launches"] == 1 + (M + chunk - 1) // chunk
+    ix.Close()
+
+
+def test_async_without_overflow_leaves_gate_closed(backend):
+    """On an ordinary corpus the gated redo returns at once: the async keys
+    equal the oracle's, and each gated launch is short."""
+    import torch
+    from aikit_b200.ann import unpack_keys
+    r = synth.Recipe(synth.MIXTURE, 256, seed=31, ncl=40, sigma=0.3)
+    n, M, k = 200_000, 64, 100
+    bq, bs = r.codes(n)
+    Q = r.queries(M)
+    ix = backend.NewI8Index(bq, bs, n, 256)
+    stream = torch.cuda.Stream()
+    qd = torch.from_numpy(Q).cuda()
+    keys = torch.zeros((M, k), dtype=torch.int64, device="cuda")
+    ix.set_kernel_timing(True)
+    for _ in range(3):
+        ix.topk_async(qd.data_ptr(), M, k, keys.data_ptr(), stream.cuda_stream)
+    stream.synchronize()
+    ix.set_kernel_timing(False)
+    kt = ix.kernel_times()
+    ix.sync()
+    assert kt["redo_gated"]["launches"] == 3 * 2
+    # each closed-gate launch only waits for the previous kernel and returns
+    # (timed here with an event pair around it, which costs more than the
+    # launch itself when the launches chain back to back)
+    assert kt["redo_gated"]["ms"] / kt["redo_gated"]["launches"] < 0.1
+    gi, gs = unpack_keys(keys.cpu().numpy().view(np.uint64))
+    widx, wsc = oracle_topk(bq, bs, Q[:8], k)
+    assert_same(gi[:8].astype(np.int64), gs[:8], widx, wsc, "gate closed")
+    ix.Close()
+
+
 def test_batch_row_shard_ids(backend):
     """id_base offsets the returned indices of a shard in the batched path."""
     r = synth.Recipe(synth.UNIT, 192, seed=4)

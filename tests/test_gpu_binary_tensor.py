@@ -283,3 +283,35 @@ def test_tensor_prefilter_overflow_is_redone_exactly(backend):
     assert got[0].tolist() == want[0].tolist() and got[1].tobytes() == want[1].tobytes()
     assert_answers(got[0], got[1], *oracle_answers(codes, ctr, bq, bs, over, Q, k), "overflow")
     bix.Close()
+
+
+def test_tensor_prefilter_async_overflow_is_exact(backend):
+    """The device-resident prefilter on the adversarially ordered corpus: the
+    popcount redo is gated on the batch's overflow flag and runs in stream
+    order, so fi8_bin_prefilter_async's keys are the popcount shortlist's,
+    sorted for the cross-shard merge, the sync reports no error, and
+    ShardedBinary (one rank here) returns the oracle's answers."""
+    import torch
+    from aikit_b200.dist import ShardedBinary
+    d, n, k, over = 64, 400_000, 10, 10
+    r = synth.Recipe(synth.UNIT, d, seed=12)
+    v, ctr, codes, bq, bs = build(r, n)
+    Q = r.queries(2)
+    dist = oracle.hamming_rows(oracle.pack_row(Q[0], ctr), codes).astype(np.int64)
+    order = np.argsort(-dist, kind="stable")  # the nearest rows last
+    codes, bq, bs = (np.ascontiguousarray(a[order]) for a in (codes, bq, bs))
+    bix = backend.NewBinaryI8Index(codes, codes.shape[1], ctr, bq, bs, n, d, over)
+    cand = k * over
+    want = shortlist(bix, Q, cand)  # the popcount pass
+    bix.set_tensor_prefilter(1)
+    got = shortlist(bix, Q, cand)   # the GEMM overflows; the gated redo recomputes it
+    bix.sync()
+    assert got.tobytes() == want.tobytes()
+    stream = torch.cuda.Stream()
+    qd = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
+    keys = ShardedBinary(bix, backend.ctx, 1, stream).topk_async(qd.data_ptr(), 2, k)
+    stream.synchronize()
+    bix.sync()
+    gi, gs = unpack_keys(keys.cpu().numpy().view(np.uint64))
+    assert_answers(gi, gs, *oracle_answers(codes, ctr, bq, bs, over, Q, k), "async overflow")
+    bix.Close()

@@ -1,7 +1,9 @@
 """Multi-GPU parity (2 ranks, one process per GPU, NCCL): the row-sharded
 FlatI8 top-k (aikit_b200.dist.ShardedTopK) and the sharded FlatBinaryI8 with
-the global shortlist (ShardedBinary) equal the CPU oracle on the whole corpus.
-Skipped on a box with fewer than two GPUs.
+the global shortlist (ShardedBinary) equal the CPU oracle on the whole corpus,
+including a corpus ordered against the query, whose shard-local batches drop
+candidates and are redone on the device before the all-gather. Skipped on a
+box with fewer than two GPUs.
 """
 import os
 import socket
@@ -75,6 +77,31 @@ def _worker(rank, world, port, results):
             if rank == 0:
                 for m in range(0, M, 5):
                     i, s = oracle.flat_i8_query(bq, bs, Qs[b][m], k)
+                    ok &= gi[m].tolist() == list(i) and gs[m].tobytes() == np.asarray(s, np.float32).tobytes()
+        ix.Close()
+        # a corpus ordered against the first query (every later row beats every
+        # earlier one): each shard's batched top-k drops candidates and its
+        # gated redo recomputes it before the all-gather reads the keys
+        d, n, k = 64, 400_000, 20
+        ra = synth.Recipe(synth.UNIT, d, seed=8)
+        bq, bs = ra.codes(n)
+        Q = ra.queries(6)
+        aq, as_ = oracle.quantize_queries(Q[:1])
+        order = np.argsort(oracle.w8a8(aq, as_, bq, bs)[0], kind="stable")
+        bq, bs = np.ascontiguousarray(bq[order]), np.ascontiguousarray(bs[order])
+        lo, hi = shard_bounds(n, world, rank)
+        ix = be.NewI8Index(bq[lo:hi], bs[lo:hi], hi - lo, d, id_base=lo)
+        for overlap in (False, True):
+            sha = ShardedTopK(ix, be.ctx, world, stream, overlap=overlap)
+            qd = torch.from_numpy(Q).cuda()
+            keys = sha.topk_async(qd.data_ptr(), len(Q), k)
+            sha.wait()
+            stream.synchronize()
+            ix.sync()
+            gi, gs = unpack_keys(keys.cpu().numpy().view(np.uint64))
+            if rank == 0:
+                for m in range(len(Q)):
+                    i, s = oracle.flat_i8_query(bq, bs, Q[m], k)
                     ok &= gi[m].tolist() == list(i) and gs[m].tobytes() == np.asarray(s, np.float32).tobytes()
         ix.Close()
         # FlatBinaryI8 with the global shortlist

@@ -59,3 +59,39 @@ def test_upload_rows_any_order_and_unuploaded_rows(backend):
     with pytest.raises(Fi8Error):
         ix.upload_rows(n - 10, bq[:20], bs[:20])  # past the end
     ix.Close()
+
+
+def test_binary_streamed_upload_equals_resident(backend):
+    """A FlatBinaryI8 shard filled block by block (fi8_bin_index_create_empty +
+    fi8_bin_upload_rows, out of order, a ragged last block) holds the same
+    codes and rows as fi8_bin_index_create's and answers identically: the
+    popcount prefilter, the tensor-core prefilter after the upload, and the
+    oracle's FlatBinaryI8.Query (ann/flat_binary_i8.go:86-109)."""
+    d, n, k, over = 320, 30001, 10, 20
+    r = synth.Recipe(synth.MIXTURE, d, seed=909, ncl=30, sigma=0.35)
+    v = r.floats(n)
+    ctr = oracle.center(v)
+    codes = oracle.pack_codes(v, ctr)
+    bq, bs = oracle.quantize_rows(v)
+    ix = backend.NewBinaryI8IndexEmpty(n, d, ctr, over)
+    blocks = [(a, min(a + 4096, n)) for a in range(0, n, 4096)]
+    for a, b in reversed(blocks):
+        ix.upload_rows(a, codes[a:b], bq[a:b], bs[a:b])
+    ix.upload_finish()
+    assert ix.read_codes().tobytes() == codes.tobytes()
+    got_q, got_s = ix.read_rows()
+    assert got_q.tobytes() == bq.tobytes() and got_s.tobytes() == bs.tobytes()
+    ref = backend.NewBinaryI8Index(codes, codes.shape[1], ctr, bq, bs, n, d, over)
+    Q = r.queries(20)
+    want = ref.topk_arrays(Q, k)
+    got = ix.topk_arrays(Q, k)
+    assert got[0].tolist() == want[0].tolist() and got[1].tobytes() == want[1].tobytes()
+    ix.set_tensor_prefilter(4)
+    got = ix.topk_arrays(Q, k)
+    assert got[0].tolist() == want[0].tolist() and got[1].tobytes() == want[1].tobytes()
+    i, s = oracle.flat_binary_i8_query(codes, ctr, bq, bs, over, Q[0], k)
+    assert got[0][0].tolist() == list(i)
+    with pytest.raises(Fi8Error):
+        ix.upload_rows(0, codes[:10], bq[:10], bs[:10])  # after the sign rows were built
+    ix.Close()
+    ref.Close()
