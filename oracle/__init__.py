@@ -8,8 +8,11 @@ has no CPU fallback.
 
 Each wrapper names the reference file:line it restates; the C source carries
 the line-level citations. Parity pinning status: pinned by the reference's
-literal test vectors and known-answer relations plus its real-data fixtures;
-no reference-run outputs exist (no Go toolchain here).
+literal test vectors and known-answer relations plus its real-data fixtures,
+and by outputs of the reference's own CUDA kernels (gpu/anncuda/gemv_w8a8.cu
+compiled for sm_100a, ``oracle/ref_anncuda.py``) run on a B200: W8A8 scores
+and top-k ids and scores, committed as ``tests/golden/ref_anncuda_outputs.npz``.
+The Go path itself cannot run (no Go toolchain here or on the GPU box).
 """
 from __future__ import annotations
 
@@ -27,9 +30,17 @@ _P = C.c_void_p
 _I64 = C.c_int64
 
 
+REFERENCE = "/root/reference"
+
+
 def build() -> str:
-    """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
+    """Compile the oracle with its Makefile (gcc, -ffp-contract=off), and,
+    where the reference source tree is present (the build machine, not the GPU
+    box, which only receives the built files), the reference's own CUDA
+    kernels into oracle/_ref/ (see ref_anncuda.py)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    if os.path.isfile(os.path.join(REFERENCE, "gpu", "anncuda", "gemv_w8a8.cu")):
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={REFERENCE}"], check=True)
     return _LIB_PATH
 
 

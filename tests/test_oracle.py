@@ -347,6 +347,29 @@ def test_oracle_reproduces_committed_goldens():
             assert s.tolist() == c["score"][m][:len(s)], name
 
 
+def test_oracle_reproduces_reference_kernel_outputs():
+    """Reference-run outputs: the reference's own CUDA kernels
+    (gpu/anncuda/gemv_w8a8.cu, compiled for sm_100a from its source and run on
+    a B200 by tests/golden/make_ref_gpu_golden.py, launched as
+    gpu/anncuda/backend.go does) scored and selected these inputs. The
+    oracle's W8A8 (linalg/quant.go:248-298) must give the same score matrix
+    byte for byte, and its topHits (ann/flat_i8.go:214-246) the same ids and
+    float32 scores: the reference's device path is the one its own tests hold
+    equal to the Go path (gpu/anncuda/backend_test.go:44, :306)."""
+    z = np.load(os.path.join(GOLDEN, "ref_anncuda_outputs.npz"))
+    names = sorted({f.split("/")[0] for f in z.files})
+    assert len(names) == 4
+    for name in names:
+        g = lambda key: z[f"{name}/{key}"]
+        scores = oracle.w8a8(g("qi8"), g("qscale"), g("codes"), g("scales"))
+        assert scores.tobytes() == g("scores").tobytes(), name
+        k = int(g("k"))
+        for m in range(scores.shape[0]):
+            i, sc = oracle.top_hits(scores[m], k)
+            assert list(i) == g("idx")[m].astype(np.int64).tolist(), (name, m)
+            assert np.asarray(sc, np.float32).tobytes() == g("val")[m].tobytes(), (name, m)
+
+
 def test_synth_quantizer_matches_oracle():
     v = synth.Recipe(synth.MIXTURE, 200, seed=4, ncl=10, sigma=0.3).floats(500)
     v[3] = 0
