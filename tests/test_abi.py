@@ -57,3 +57,31 @@ def test_keys_unpack_round_trip_host():
     order = sorted(range(len(cases)), key=lambda j: -int(keys[j]))
     want = sorted(range(len(cases)), key=lambda j: (-cases[j][0], cases[j][1]))
     assert order == want
+
+
+def test_purego_adapter_binds_declared_symbols():
+    """The cgo-free Go adapter in INTEGRATION.md (purego.RegisterLibFunc, the
+    way the reference's gocudrv binds libcuda, gpu/cuda.go:11,54) binds only
+    symbols that include/fi8.h declares and the library exports, and covers
+    every call the seam's interfaces need: ann.Backend.NewI8Index,
+    I8Index.Score/Close, I8BatchIndex.ScoreBatch, I8TopKIndex.TopKBatch
+    (ann/backend.go:16-55), QueryFilter, the paged upload and the
+    FlatBinaryI8 index."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    start = doc.index("## Go adapter (cgo-free, purego)")
+    block = doc[start:doc.index("```\n", doc.index("```go", start) + 5)]
+    bound = set(re.findall(r'"(fi8_[a-z0-9_]+)":\s*&fi8\.', block))
+    declared = set(declared_symbols())
+    assert bound <= declared, sorted(bound - declared)
+    lib = ctypes.CDLL(build_fi8())
+    assert all(hasattr(lib, s) for s in bound)
+    needed = {"fi8_last_error", "fi8_device_count", "fi8_ctx_create", "fi8_index_create", "fi8_index_destroy",
+              "fi8_score", "fi8_score_batch", "fi8_topk_batch", "fi8_topk_batch_keep",
+              "fi8_index_create_empty", "fi8_index_upload_rows", "fi8_index_upload_finish",
+              "fi8_bin_index_create", "fi8_bin_query_topk", "fi8_bin_query_topk_keep",
+              "fi8_bin_set_tensor_prefilter", "fi8_bin_index_destroy"}
+    assert needed <= bound, sorted(needed - bound)
+    # every bound entry point is called through the table somewhere in the doc
+    fields = re.findall(r'"fi8_[a-z0-9_]+":\s*&fi8\.([A-Za-z0-9]+)', block)
+    for f in fields:
+        assert f"fi8.{f}(" in doc, f
