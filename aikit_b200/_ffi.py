@@ -17,6 +17,7 @@ FI8_ERR_DEVICE = 5
 FI8_OPT_GEMM_MIN_BATCH = 1
 FI8_OPT_KERNEL_TIMING = 2
 FI8_OPT_GEMM_CTAS = 3
+FI8_OPT_GEMM_PAIR = 4
 # kernel classes of fi8_index_kernel_times, in index order
 KERNEL_KINDS = ("scan_kernel", "gemm_kernel", "select_kernel", "quantize_kernel", "rerank_kernel",
                 "redo_gated")

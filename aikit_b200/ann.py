@@ -360,6 +360,12 @@ class I8Index:
         from ._ffi import FI8_OPT_GEMM_CTAS
         check(lib().fi8_index_set_option(self._h, FI8_OPT_GEMM_CTAS, ctas))
 
+    def set_gemm_pair(self, on: bool) -> None:
+        """Run batches of more than 128 queries on CTA pairs (tcgen05
+        cta_group::2) or on single CTAs (the default). Results are identical."""
+        from ._ffi import FI8_OPT_GEMM_PAIR
+        check(lib().fi8_index_set_option(self._h, FI8_OPT_GEMM_PAIR, 1 if on else 0))
+
     def _queries(self, queries) -> np.ndarray:
         if isinstance(queries, np.ndarray) and queries.ndim == 2:
             Q = _f32(queries)
@@ -453,6 +459,12 @@ class BinaryI8Index:
         more HBM); 0 frees the rows and keeps every batch on the popcount
         pass. The shortlist is the same either way."""
         check(lib().fi8_bin_set_tensor_prefilter(self._h, int(min_batch)))
+
+    def set_gemm_pair(self, on: bool) -> None:
+        """The tensor-core prefilter's batches of more than 128 queries on CTA
+        pairs or single CTAs (the default); the shortlist is the same."""
+        from ._ffi import FI8_OPT_GEMM_PAIR
+        check(lib().fi8_index_set_option(self._ih, FI8_OPT_GEMM_PAIR, 1 if on else 0))
 
     def Query(self, q, k: int) -> list[Hit]:
         """FlatBinaryI8.Query (flat_binary_i8.go:78) for one query."""

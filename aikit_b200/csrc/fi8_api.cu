@@ -152,6 +152,8 @@ struct fi8_index {
   // batched (tcgen05 GEMM) path
   CUtensorMap tmB;       // corpus codes [n_alloc][dpad], 256-row boxes
   bool has_tmB = false;
+  CUtensorMap tmB2;      // the same rows in 128-row boxes (a CTA pair's halves)
+  bool has_tmB2 = false;
   int8_t* d_A = nullptr;  // quantized queries [Mpad][dpad]
   size_t A_cap = 0;
   CUtensorMap tmA;       // over d_A, rebuilt when d_A moves
@@ -170,6 +172,7 @@ struct fi8_index {
   size_t topk_cap = 0;
   int32_t gemm_min_batch = 2;  // batches of at least this many queries use the GEMM path
   int32_t gemm_ctas = 0;       // cap on the GEMM's persistent CTAs (0: one per SM)
+  int32_t gemm_pair = 0;       // batches of more than 128 queries on CTA pairs (FI8_OPT_GEMM_PAIR)
   int32_t last_launches = 0;   // kernels launched by the last query call
 
   // incremental uploads (fi8_index_upload_rows): the pinned double buffer,
@@ -384,6 +387,7 @@ static int index_finish(fi8_index* x) {
   DeviceGuard g(x->device);
   FI8_CUDA(cudaStreamSynchronize(x->stream), "gpu: device upload failed");
   x->has_tmB = make_tmap_i8(&x->tmB, x->d_codes, (uint64_t)x->n_alloc, (uint64_t)x->dpad, (uint32_t)kGemmBN);
+  x->has_tmB2 = make_tmap_i8(&x->tmB2, x->d_codes, (uint64_t)x->n_alloc, (uint64_t)x->dpad, (uint32_t)(kGemmBN / 2));
   return FI8_OK;
 }
 
@@ -710,6 +714,7 @@ static void plan_ranges(int64_t n, int32_t M, int32_t k, int32_t cap, std::vecto
 // a binary index's sign rows (+1/-1 per code bit) scored by -Hamming distance.
 struct GemmCorpus {
   const CUtensorMap* tmB;  // [n_alloc][dpad] int8 rows, 256-row boxes
+  const CUtensorMap* tmB2; // the same rows in 128-row boxes (null: no CTA pairs)
   const float* scales;     // W8A8: the row scales; null in Hamming mode
   const float* center;     // Hamming mode: the prefilter's centre (null: none)
   int32_t ham_dim;         // > 0: Hamming mode over this many bits
@@ -721,7 +726,11 @@ static int launch_topk_gemm(fi8_index* x, const GemmCorpus& corpus, const float*
     return fail(FI8_ERR_DECLINED, "gpu: TopKBatch declined (k=%d beyond the device top-K)", k);
   const int32_t kp = pow2_ge_host(k);
   const int32_t bm = M <= 64 ? 64 : kGemmBM;  // the MMA's M: a small batch is one 64-query tile
-  const int32_t Mpad = (M + bm - 1) / bm * bm;
+  // Batches of more than one 128-query tile are tensor-bound: they run on CTA
+  // pairs (256-query x 256-row units, 2/3 of the operand bytes per SM).
+  const int32_t pair_clusters = gemm_pair_max_clusters();
+  const bool pair = x->gemm_pair && M > kGemmBM && corpus.tmB2 && pair_clusters > 0;
+  const int32_t Mpad = pair ? (M + 2 * kGemmBM - 1) / (2 * kGemmBM) * (2 * kGemmBM) : (M + bm - 1) / bm * bm;
   const int32_t cap = gemm_cap(M);
   int rc;
   if ((rc = ensure_device(&x->d_A, &x->A_cap, (size_t)Mpad * x->dpad, "gemm A")) != FI8_OK) return rc;
@@ -769,11 +778,14 @@ static int launch_topk_gemm(fi8_index* x, const GemmCorpus& corpus, const float*
     p.row_hi = ranges[i].row_hi;
     p.rtiles = (p.row_hi - p.row_lo + kGemmBN - 1) / kGemmBN;
     p.producer_waits = i == 0 ? 1 : 0;  // the first range follows the quantize kernel
-    const int64_t units = (int64_t)p.qtiles * p.rtiles;
+    const int64_t units = (int64_t)(pair ? p.qtiles / 2 : p.qtiles) * p.rtiles;
     const int32_t ctas = x->gemm_ctas > 0 ? std::min(x->gemm_ctas, x->sm_count) : x->sm_count;
-    const int32_t G = (int32_t)std::max<int64_t>(1, std::min<int64_t>(ctas, units));
+    // CTAs: one per SM, or pairs of them, no more than there are units
+    const int32_t G = pair ? 2 * (int32_t)std::max<int64_t>(1, std::min<int64_t>({(int64_t)ctas / 2,
+                                                                                   (int64_t)pair_clusters, units}))
+                           : (int32_t)std::max<int64_t>(1, std::min<int64_t>(ctas, units));
     t0 = timer_begin(x, st);
-    e = gemm_launch(x->tmA, *corpus.tmB, p, G, bm, st);
+    e = gemm_launch(x->tmA, pair ? *corpus.tmB2 : *corpus.tmB, p, G, bm, pair, st);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_launch");
     // the range's rows (and scales), plus the int8 query tile
     timer_end(x, st, t0, FI8_KERNEL_GEMM,
@@ -811,7 +823,8 @@ static int launch_topk(fi8_index* x, const float* d_q, int32_t M, int32_t k, uin
                        cudaStream_t st) {
   x->last_launches = 0;
   if (M >= x->gemm_min_batch && x->has_tmB) {
-    const int rc = launch_topk_gemm(x, GemmCorpus{&x->tmB, x->d_scales, nullptr, 0}, d_q, M, k, d_keys, st);
+    const int rc = launch_topk_gemm(x, GemmCorpus{&x->tmB, x->has_tmB2 ? &x->tmB2 : nullptr, x->d_scales, nullptr, 0},
+                                    d_q, M, k, d_keys, st);
     if (rc != FI8_OK) return rc;
     return launch_topk_redo(x, d_q, M, k, d_keys, st);
   }
@@ -989,6 +1002,10 @@ int fi8_index_set_option(fi8_index* idx, int option, int64_t value) {
     case FI8_OPT_GEMM_CTAS:
       if (value < 0) return fail(FI8_ERR_ARG, "fi8_index_set_option: GEMM_CTAS must be >= 0");
       idx->gemm_ctas = (int32_t)std::min<int64_t>(value, 1 << 30);
+      return FI8_OK;
+    case FI8_OPT_GEMM_PAIR:
+      if (value != 0 && value != 1) return fail(FI8_ERR_ARG, "fi8_index_set_option: GEMM_PAIR is 0 or 1");
+      idx->gemm_pair = (int32_t)value;
       return FI8_OK;
     default:
       return fail(FI8_ERR_ARG, "fi8_index_set_option: unknown option %d", option);
@@ -1196,6 +1213,8 @@ struct fi8_bin {
   // to +1/-1 int8 rows, so a batch's Hamming distances are one kind::i8 GEMM
   int8_t* d_sign = nullptr;     // [n_alloc][dpad]; 0 past dim and for rows >= n
   CUtensorMap tmS;              // over d_sign, 256-row boxes
+  CUtensorMap tmS2;             // over d_sign, 128-row boxes (CTA pairs)
+  bool has_tmS2 = false;
   int32_t tensor_min_m = 0;     // batches of at least this many queries use it (0: off)
 };
 
@@ -1221,8 +1240,16 @@ static int launch_bin_popcount(fi8_bin* b, const float* d_q, int32_t M, int32_t 
   ScanGeometry geo;
   if (cand > kBinMaxCand || !scan_geometry(bpad, 0, false, &geo, true))
     return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond %d)", cand, kBinMaxCand);
-  const int32_t Mc = std::min(M, kBinMaxM);
-  const int32_t P = shortlist_segments(x->sm_count);
+  int32_t Mc = std::min(M, kBinMaxM);
+  int32_t P = shortlist_segments(x->sm_count);
+  if (gate) {
+    // The gated redo's launches cost their CTAs' start and exit even when
+    // closed, so each keeps to about one wave: up to 64 queries per pass
+    // (16 when their distance rows would pass 4 GB), sm_count / queries CTAs
+    // and row segments each. When open, every SM still streams the codes.
+    Mc = std::min<int32_t>(M, (size_t)64 * x->n_alloc * sizeof(uint16_t) <= ((size_t)4 << 30) ? 64 : kBinMaxM);
+    P = std::max<int32_t>(1, x->sm_count / Mc);
+  }
   int rc;
   if ((rc = ensure_device(&b->d_qbits, &b->qbits_cap, (size_t)Mc * b->wpad, "binary query bits")) != FI8_OK)
     return rc;
@@ -1240,7 +1267,8 @@ static int launch_bin_popcount(fi8_bin* b, const float* d_q, int32_t M, int32_t 
   p.nbins = nbins;
   p.qbits = b->d_qbits;
   p.gate = gate;
-  const int32_t G = grid_ctas(x, p);
+  int32_t G = grid_ctas(x, p);
+  if (gate) G = std::max<int32_t>(1, std::min<int32_t>(G, x->sm_count / Mc));
   auto timed = [&](cudaEvent_t t0, int kind, double bytes) {
     if (gate)
       timer_end(x, st, t0, FI8_KERNEL_REDO, 0.0);
@@ -1284,7 +1312,8 @@ static int launch_bin_prefilter(fi8_bin* b, const float* d_q, int32_t M, int32_t
     // selects, sorted descending (so it also serves a key merge).
     if (cand > kBinMaxCand)
       return fail(FI8_ERR_DECLINED, "gpu: binary prefilter declined (cand=%d beyond %d)", cand, kBinMaxCand);
-    int rc = launch_topk_gemm(x, GemmCorpus{&b->tmS, nullptr, b->d_center, x->dim}, d_q, M, cand, d_keys, st);
+    int rc = launch_topk_gemm(x, GemmCorpus{&b->tmS, b->has_tmS2 ? &b->tmS2 : nullptr, nullptr, b->d_center, x->dim},
+                              d_q, M, cand, d_keys, st);
     if (rc != FI8_OK) return rc;
     cudaEvent_t t0 = timer_begin(x, st);
     cudaError_t e = overflow_latch_launch(x->d_err, x->d_redo, st);
@@ -1592,6 +1621,8 @@ int fi8_bin_set_tensor_prefilter(fi8_bin* b, int32_t min_batch) {
     if (e == cudaSuccess && !make_tmap_i8(&b->tmS, b->d_sign, (uint64_t)x->n_alloc, (uint64_t)x->dpad,
                                           (uint32_t)kGemmBN))
       e = cudaErrorInvalidValue;
+    if (e == cudaSuccess)
+      b->has_tmS2 = make_tmap_i8(&b->tmS2, b->d_sign, (uint64_t)x->n_alloc, (uint64_t)x->dpad, (uint32_t)(kGemmBN / 2));
     if (e != cudaSuccess) {
       cudaFree(b->d_sign);
       b->d_sign = nullptr;

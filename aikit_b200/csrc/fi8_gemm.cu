@@ -39,23 +39,30 @@ namespace {
 // Query tiles of BM = 64 or 128 queries (the MMA's M). A batch of at most 64
 // queries uses M = 64: half the tensor work and half the query-tile traffic of
 // padding it to 128.
+// A CTA pair (PAIR, tcgen05 cta_group::2) computes a 256-query x 256-row tile:
+// each CTA stages its own 128 query rows and half (128) of the corpus rows,
+// and the pair's M = 256 MMA reads the corpus half of both CTAs. A CTA then
+// pulls 32 KB of operands per K stage instead of 48 KB for the same MMA work.
 template <int BM>
 __host__ __device__ constexpr int stage_a() { return BM * kGemmBK; }  // 8 / 16 KB
-constexpr int kStageB = kGemmBN * kGemmBK;                      // 32 KB
-template <int BM>
-__host__ __device__ constexpr int stage_bytes() { return stage_a<BM>() + kStageB; }
-constexpr int kStages = 4;
+template <bool PAIR>
+__host__ __device__ constexpr int stage_b() { return (PAIR ? kGemmBN / 2 : kGemmBN) * kGemmBK; }  // 16 / 32 KB
+template <int BM, bool PAIR = false>
+__host__ __device__ constexpr int stage_bytes() { return stage_a<BM>() + stage_b<PAIR>(); }
+template <bool PAIR>
+__host__ __device__ constexpr int stages() { return PAIR ? 6 : 4; }  // the pair's stages are 2/3 the size
 constexpr int kEpiWarps = 16;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kGemmThreads = 64 + kEpiThreads;
 constexpr int kTmemCols = 512;  // two 256-column accumulators
 constexpr int kStageKeys = 4;   // staged candidate keys per epilogue thread
-template <int BM>
-constexpr size_t gemm_smem() { return (size_t)kStages * stage_bytes<BM>() + 1024; }  // + alignment slack
+constexpr int kChunkCols = 16;  // accumulator columns an epilogue thread loads and tests at a time
+template <int BM, bool PAIR>
+constexpr size_t gemm_smem() { return (size_t)stages<PAIR>() * stage_bytes<BM, PAIR>() + 1024; }  // + alignment slack
 
 // tcgen05 instruction descriptor, kind::i8: D = s32 (c_format 2), A and B
 // signed 8-bit (format 1), both K-major, N = 256 (n_dim = N>>3), M = BM
-// (m_dim = M>>4).
+// (m_dim = M>>4; the pair's M is 256).
 template <int BM>
 __host__ __device__ constexpr uint32_t idesc() {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGemmBN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -100,9 +107,75 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_
       : "memory");
 }
 
+// The pair's MMA (M = 256 across the two CTAs' TMEM, issued by the even CTA):
+// A rows 0-127 and corpus rows 0-127 from the even CTA's shared memory, A rows
+// 128-255 and corpus rows 128-255 from the odd CTA's, at the same offsets.
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc<256>()), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// The pair's commits: to the barrier at this offset in both CTAs, or in this
+// CTA only.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+  const uint16_t mask = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of this CTA's variable at `p` in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of either CTA of the cluster (cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// A tiled load whose completion is counted on an mbarrier of either CTA of
+// the pair (cluster address); never multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -118,6 +191,55 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Two IEEE round-to-nearest float32 products at once (sm_100's packed f32x2
+// multiply): each lane is exactly __fmul_rn of the same operands.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+
+// max(a, b, c) in one instruction (NaN operands are ignored, as fmaxf does)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// The largest exact W8A8 score of a 16-column chunk: float32(dot) * qs *
+// rs, two rounded multiplies left to right per column (the reference's
+// order, linalg/quant.go:290-296), the pairs multiplied packed. NaN scores
+// are skipped (a NaN never passes the filter), so the chunk can hold a
+// passing score only if this max passes.
+__device__ __forceinline__ float chunk_max_w8a8(const uint32_t (&v)[kChunkCols], float qs, const float* scl) {
+  const float2 q2 = make_float2(qs, qs);
+  const float4* s4 = reinterpret_cast<const float4*>(scl);
+  float m = -INFINITY;
+#pragma unroll
+  for (int i4 = 0; i4 < kChunkCols / 4; i4++) {
+    const float4 rs = s4[i4];
+    const float2 a0 = mul2_rn(make_float2(__int2float_rn((int32_t)v[4 * i4]), __int2float_rn((int32_t)v[4 * i4 + 1])), q2);
+    const float2 a1 =
+        mul2_rn(make_float2(__int2float_rn((int32_t)v[4 * i4 + 2]), __int2float_rn((int32_t)v[4 * i4 + 3])), q2);
+    const float2 s0 = mul2_rn(a0, make_float2(rs.x, rs.y));
+    const float2 s1 = mul2_rn(a1, make_float2(rs.z, rs.w));
+    m = max3f(m, max3f(s0.x, s0.y, s1.x), s1.y);
+  }
+  return m;
 }
 
 // Which query of a tile an A row holds, and which query a TMEM lane's
@@ -177,11 +299,22 @@ struct UnitWalk {
   }
 };
 
-template <int BM, bool HAM>
+// PAIR (BM = 128): launched in clusters of two CTAs. Both CTAs walk the
+// same units (cluster c takes units c, c + clusters, ...) over 256-query
+// tiles: CTA r of the pair holds query tile 2 * tile + r and loads corpus rows
+// row0 + 128 r .. + 127 of the unit's 256. Both CTAs' loads complete on the
+// even CTA's full barriers; the even CTA's MMA thread issues the pair's
+// M = 256 MMAs and commits to both CTAs' barriers; both CTAs' epilogues read
+// their own TMEM and release the accumulator on the even CTA's barrier. A
+// cluster barrier follows the set-up and precedes the teardown, so no CTA
+// signals a barrier of its peer before it exists or after it is gone.
+template <int BM, bool HAM, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  static_assert(!PAIR || BM == 128, "CTA pairs use 128-query tiles");
+  constexpr int kStages = stages<PAIR>();
   constexpr int kStageA = stage_a<BM>();
-  constexpr int kStageBytes = stage_bytes<BM>();
+  constexpr int kStageBytes = stage_bytes<BM, PAIR>();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ uint64_t s_full[kStages], s_empty[kStages], s_tfull[2], s_tempty[2], s_done;
   __shared__ uint32_t s_tmem;
@@ -193,9 +326,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const int64_t units = (int64_t)p.qtiles * p.rtiles;
-  const int64_t my_units = units > blockIdx.x ? (units - blockIdx.x + G - 1) / G : 0;
+  // unit walkers: CTAs, or CTA pairs walking 256-query tiles
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int G = PAIR ? (int)cluster_count() : (int)gridDim.x;
+  const int walker = PAIR ? (int)cluster_id() : (int)blockIdx.x;
+  const int wtiles = PAIR ? p.qtiles / 2 : p.qtiles;  // query tiles of the walk
+  const int64_t units = (int64_t)wtiles * p.rtiles;
+  const int64_t my_units = units > walker ? (units - walker + G - 1) / G : 0;
+  const bool leader = rank == 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -204,20 +342,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&s_tfull[b], 1);
-      mbar_init(&s_tempty[b], kEpiWarps);
+      mbar_init(&s_tempty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);  // the pair's: both CTAs' epilogues
     }
     mbar_init(&s_done, 1);
     fence_mbar_init();
     s_abort = 0;
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (PAIR) {  // one warp of each CTA of the pair: the same columns in both
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // both CTAs' barriers and TMEM exist before either signals the other
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
@@ -230,10 +378,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       if (p.producer_waits) pdl_wait_prior();
       int64_t step = 0;
-      UnitWalk w(blockIdx.x, G, p.qtiles);
+      UnitWalk w(walker, G, wtiles);
       for (int64_t u = 0; u < my_units && !s_abort; u++, w.next()) {
-        const int qt = w.qt;
-        const int32_t row0 = (int32_t)(p.row_lo + w.rt * kGemmBN);
+        const int qt = PAIR ? 2 * w.qt + (int)rank : w.qt;
+        // this CTA's corpus rows: the unit's 256, or its half of them
+        const int32_t row0 = (int32_t)(p.row_lo + w.rt * kGemmBN) + (PAIR ? (int32_t)rank * (kGemmBN / 2) : 0);
         for (int kc = 0; kc < p.kchunks; kc++, step++) {
           const int s = (int)(step % kStages);
           if (step >= kStages && !mbar_wait_bounded(&s_empty[s], (uint32_t)(((step / kStages) - 1) & 1))) {
@@ -242,18 +391,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           unsigned char* st = smem + (size_t)s * kStageBytes;
-          mbar_arrive_expect_tx(&s_full[s], kStageBytes);
-          tma_load_2d(st, &tmA, kc * kGemmBK, qt * BM, &s_full[s]);
-          tma_load_2d(st + kStageA, &tmB, kc * kGemmBK, row0, &s_full[s]);
+          if (PAIR) {
+            // both CTAs' bytes complete on the even CTA's barrier
+            if (leader) mbar_arrive_expect_tx(&s_full[s], 2 * kStageBytes);
+            const uint32_t full = cluster_addr(&s_full[s], 0);
+            tma_load_2d_pair(st, &tmA, kc * kGemmBK, qt * BM, full);
+            tma_load_2d_pair(st + kStageA, &tmB, kc * kGemmBK, row0, full);
+          } else {
+            mbar_arrive_expect_tx(&s_full[s], kStageBytes);
+            tma_load_2d(st, &tmA, kc * kGemmBK, qt * BM, &s_full[s]);
+            tma_load_2d(st + kStageA, &tmB, kc * kGemmBK, row0, &s_full[s]);
+          }
         }
       }
-      // let issued copies land before teardown (bounded; a no-op when drained)
-      for (int64_t j = (step > kStages ? step - kStages : 0); j < step; j++)
-        mbar_wait_bounded(&s_full[j % kStages], (uint32_t)((j / kStages) & 1));
+      // let issued copies land before teardown (bounded; a no-op when drained).
+      // The pair's full barriers are the even CTA's and count both CTAs' bytes;
+      // the odd CTA's copies have landed once its epilogue has seen the last
+      // accumulator, which follows every MMA that read them.
+      if (leader)
+        for (int64_t j = (step > kStages ? step - kStages : 0); j < step; j++)
+          mbar_wait_bounded(&s_full[j % kStages], (uint32_t)((j / kStages) & 1));
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0) {
+    // (the pair's MMAs are the even CTA's)
+    if (lane == 0 && leader) {
       int64_t step = 0;
       for (int64_t u = 0; u < my_units && !s_abort; u++) {
         const int b = (int)(u & 1);
@@ -277,16 +439,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kGemmBK / 32; k++) {
             // advance K by 32 bytes inside the swizzled 128-byte rows
-            umma_i8<BM>(d_tmem, sw128_desc(a_base) + (uint64_t)(2 * k), sw128_desc(b_base) + (uint64_t)(2 * k),
-                    (kc > 0 || k > 0) ? 1u : 0u);
+            const uint64_t ad = sw128_desc(a_base) + (uint64_t)(2 * k), bd = sw128_desc(b_base) + (uint64_t)(2 * k);
+            if (PAIR)
+              umma_i8_pair(d_tmem, ad, bd, (kc > 0 || k > 0) ? 1u : 0u);
+            else
+              umma_i8<BM>(d_tmem, ad, bd, (kc > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&s_empty[s]);
+          if (PAIR)
+            umma_commit_pair_both(&s_empty[s]);  // frees the stage in both CTAs
+          else
+            umma_commit(&s_empty[s]);
         }
         if (s_abort) break;
-        umma_commit(&s_tfull[b]);
+        if (PAIR)
+          umma_commit_pair_both(&s_tfull[b]);  // both CTAs' accumulators are ready
+        else
+          umma_commit(&s_tfull[b]);
       }
       // every MMA this thread issued has completed before TMEM is released
-      umma_commit(&s_done);
+      if (PAIR)
+        umma_commit_pair_local(&s_done);
+      else
+        umma_commit(&s_done);
       mbar_wait_bounded(&s_done, 0);
     }
   } else {
@@ -302,7 +476,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int r = quarter * 32 + lane;  // A row / TMEM lane of this thread
     float* const my_scale = &s_scale[ew][0][0];
     if (!HAM && my_units > 0) {
-      const int64_t row0 = p.row_lo + ((int64_t)blockIdx.x / p.qtiles) * kGemmBN;
+      const int64_t row0 = p.row_lo + ((int64_t)walker / wtiles) * kGemmBN;
       cp_async8(my_scale + 2 * lane, p.scales + row0 + cq * 64 + 2 * lane);
     }
     cp_async_commit();
@@ -336,10 +510,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       qs_next = valid ? p.qscale[qt_f * BM + query_arow<BM>(j, m_t)] : 0.0f;
       T_next = valid ? p.thr[qt_f * BM + j] : ~0ull;
     };
-    UnitWalk w(blockIdx.x, G, p.qtiles);
-    if (my_units > 0) fetch_tile_state(w.qt);
+    // the query tile of a walk position: the walker's own, or this CTA's
+    // half of the pair's 256-query tile
+    auto tile_of = [&](int wqt) { return PAIR ? 2 * wqt + (int)rank : wqt; };
+    UnitWalk w(walker, G, wtiles);
+    if (my_units > 0) fetch_tile_state(tile_of(w.qt));
     for (int64_t u = 0; u < my_units; u++) {
-      const int qt = w.qt;
+      const int qt = tile_of(w.qt);
       const int64_t row0 = p.row_lo + w.rt * kGemmBN;
       const int b = (int)(u & 1);
       if (qt != cur_qt) {
@@ -367,7 +544,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                : p.ham_dim + 2 * ((int32_t)key_score(T) + 1);
       }
       w.next();  // from here on, the next unit's tiles
-      if (u + 1 < my_units && w.qt != qt) fetch_tile_state(w.qt);
+      if (u + 1 < my_units && tile_of(w.qt) != qt) fetch_tile_state(tile_of(w.qt));
       if (s_abort) break;
       // this unit's scales (copied during the previous unit) have landed;
       // start the copy of the next unit's into the other slot
@@ -386,11 +563,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int64_t lim = p.row_hi - row0;  // valid columns of this tile
 #pragma unroll 1
-      for (int c = 0; c < 2; c++) {
-        const int col0 = cq * 64 + c * 32;
-        const float* scl = my_scale + b * 64 + c * 32;
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kGemmBN + col0), v);
+      for (int c = 0; c < 64 / kChunkCols; c++) {
+        uint32_t v[kChunkCols];
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kGemmBN + cq * 64 + c * kChunkCols), v);
+        const int col0 = cq * 64 + c * kChunkCols;
+        const float* scl = my_scale + b * 64 + c * kChunkCols;
+        // The chunk's test first: past the first range a chunk rarely holds a
+        // row above its query's threshold, so one max over its columns -- of
+        // the exact scores (W8A8) or of the dots (Hamming) -- rejects it with
+        // a few instructions per column. Only a chunk that passes builds the
+        // exact per-column mask below.
+        bool any;
+        if (HAM) {
+          int32_t mx = (int32_t)v[0];
+#pragma unroll
+          for (int i = 1; i < kChunkCols; i++) mx = max(mx, (int32_t)v[i]);
+          any = mx >= hthr;
+        } else {
+          any = chunk_max_w8a8(v, qs, scl) >= Tscore;
+          if (qs == 0.0f) any = 0.0f >= Tscore;  // an all-zero query scores exactly 0
+        }
+        if (!any || !lane_valid || col0 >= lim) continue;
         // branch-free pass: the plain product equals the exact (x86 NaN
         // semantics) score whenever it is not NaN, and NaN never passes. The
         // score replaces the accumulator in v for the append below.
@@ -402,11 +595,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // v keeps the dots and survivors get their scores when appended.
           const int32_t tm1 = hthr - 1;
 #pragma unroll
-          for (int i = 31; i >= 0; i--) mask = __funnelshift_l((uint32_t)(tm1 - (int32_t)v[i]), mask, 1);
+          for (int i = kChunkCols - 1; i >= 0; i--)
+            mask = __funnelshift_l((uint32_t)(tm1 - (int32_t)v[i]), mask, 1);
         } else {
           const float4* s4 = reinterpret_cast<const float4*>(scl);
 #pragma unroll
-          for (int i4 = 0; i4 < 8; i4++) {
+          for (int i4 = 0; i4 < kChunkCols / 4; i4++) {
             const float4 rs = s4[i4];
             const float rsv[4] = {rs.x, rs.y, rs.z, rs.w};
 #pragma unroll
@@ -418,14 +612,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
+        constexpr uint32_t kAll = (1u << kChunkCols) - 1u;
         if (!HAM && qs == 0.0f) {  // an all-zero query scores exactly 0
-          mask = (0.0f >= Tscore) ? 0xFFFFFFFFu : 0u;
+          mask = (0.0f >= Tscore) ? kAll : 0u;
 #pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = 0u;
+          for (int i = 0; i < kChunkCols; i++) v[i] = 0u;
         }
-        if (!lane_valid) mask = 0u;
-        if (col0 + 32 > lim) mask &= (col0 >= lim) ? 0u : ((1u << (uint32_t)(lim - col0)) - 1u);
-        if (p.keep && mask) mask &= keep_bits32(p.keep, p.keep_nbits, (uint64_t)p.id_base + row0 + col0);
+        if (col0 + kChunkCols > lim) mask &= (1u << (uint32_t)(lim - col0)) - 1u;
+        if (p.keep && mask) mask &= keep_bits32(p.keep, p.keep_nbits, (uint64_t)p.id_base + row0 + col0) & kAll;
         if (mask) {
           // Survivors go to this thread's few shared staging slots while they
           // fit; otherwise one reservation in the query's global list takes
@@ -451,7 +645,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t id0 = p.id_base + (uint32_t)(row0 + col0);
           // survivors are sparse: visit only the 4-column groups that hold one
 #pragma unroll
-          for (int g = 0; g < 8; g++) {
+          for (int g = 0; g < kChunkCols / 4; g++) {
             const uint32_t nib = (mask >> (4 * g)) & 0xFu;
             if (nib) {
 #pragma unroll
@@ -472,16 +666,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive1(&s_tempty[b]);
+      if (lane == 0) {
+        if (PAIR)
+          mbar_arrive_cluster(cluster_addr(&s_tempty[b], 0));  // the pair's accumulator is the even CTA's to reuse
+        else
+          mbar_arrive1(&s_tempty[b]);
+      }
     }
     cp_async_wait_all();  // no copy into shared memory outlives the loop
     flush_staged(p, q, my_stage, staged);
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // neither CTA leaves while its peer may still signal or read it
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
@@ -896,22 +1101,67 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pi
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BM, bool HAM>
+template <int BM, bool HAM, bool PAIR>
 static cudaError_t gemm_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G,
                                  cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BM, HAM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)gemm_smem<BM>());
+  auto kern = gemm_kernel<BM, HAM, PAIR>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<BM, PAIR>());
   if (e != cudaSuccess) return e;
-  return launch_pdl(gemm_kernel<BM, HAM>, dim3((unsigned)G), dim3(kGemmThreads), gemm_smem<BM>(), stream, tmA, tmB,
-                    p);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)G);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = gemm_smem<BM, PAIR>();
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = PAIR ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p);
 }
 
 cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G, int32_t bm,
-                        cudaStream_t stream) {
+                        bool pair, cudaStream_t stream) {
   const bool ham = p.ham_dim > 0;
-  if (bm == 64) return ham ? gemm_launch_t<64, true>(tmA, tmB, p, G, stream) : gemm_launch_t<64, false>(tmA, tmB, p, G, stream);
+  if (pair) {
+    if (bm != 128 || G % 2 != 0 || p.qtiles % 2 != 0) return cudaErrorInvalidValue;
+    return ham ? gemm_launch_t<128, true, true>(tmA, tmB, p, G, stream)
+               : gemm_launch_t<128, false, true>(tmA, tmB, p, G, stream);
+  }
+  if (bm == 64)
+    return ham ? gemm_launch_t<64, true, false>(tmA, tmB, p, G, stream)
+               : gemm_launch_t<64, false, false>(tmA, tmB, p, G, stream);
   if (bm != 128) return cudaErrorInvalidValue;
-  return ham ? gemm_launch_t<128, true>(tmA, tmB, p, G, stream) : gemm_launch_t<128, false>(tmA, tmB, p, G, stream);
+  return ham ? gemm_launch_t<128, true, false>(tmA, tmB, p, G, stream)
+             : gemm_launch_t<128, false, false>(tmA, tmB, p, G, stream);
+}
+
+int32_t gemm_pair_max_clusters() {
+  static int32_t n = [] {
+    auto kern = gemm_kernel<128, false, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<128, true>()) !=
+        cudaSuccess)
+      return 0;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = gemm_smem<128, true>();
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess) return 0;
+    return (int32_t)c;
+  }();
+  return n;
 }
 
 cudaError_t quantize_launch(const float* q, int32_t M, int32_t Mpad, int32_t d, int32_t dpad, int8_t* A,

@@ -44,9 +44,16 @@ struct GemmParams {
 // (pitch a multiple of 16 bytes) with a {128 bytes, box_rows} box.
 bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t pitch, uint32_t box_rows);
 
-// bm: the query tile (64 or 128); tmA's box must be bm rows.
+// bm: the query tile (64 or 128); tmA's box must be bm rows. pair: clusters
+// of two CTAs (tcgen05 cta_group::2) over 256-query x 256-row units; then bm
+// is 128, G (CTAs) and p.qtiles are even, and tmB's box is 128 rows (each CTA
+// loads half of a unit's corpus rows); otherwise tmB's box is 256 rows.
 cudaError_t gemm_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int32_t G, int32_t bm,
-                        cudaStream_t stream);
+                        bool pair, cudaStream_t stream);
+
+// Clusters of two GEMM CTAs that can be resident at once on this device (0 if
+// the pair form cannot launch).
+int32_t gemm_pair_max_clusters();
 
 // Quantize M queries ([M][d] f32) into A ([Mpad][dpad] int8, zero padded) and
 // qscale ([Mpad]); also resets the per-query select state (thr, cnt, topk).

@@ -1,26 +1,36 @@
 #!/usr/bin/env python
-"""FlatI8 exact top-K queries/sec on B200 (BASELINE.json metric, configs[1]).
+"""FlatI8 exact top-K queries/sec on B200 (BASELINE.json metric).
 
-Workload (C2): N = 10,000,000 corpus rows, d = 768, a seeded mixture of 1,000
-Gaussian clusters (centres N(0,1), sigma 0.3), L2-normalised and quantized per
-row as NewFlatI8 does; queries from the same mixture; K = 100. One step is one
-TopKBatch over a batch of 64 queries (the headline); the batch-1 latency form
-is reported alongside. Synthetic data stands in for the reference's Model2Vec
-embeddings. The corpus (7.7 GB) is far larger than L2, so no flush is needed
-between steps.
+Headline workload: C3 (the largest configuration
+that fits one B200): N = 50,000,000 corpus rows, d = 1024, a seeded mixture of
+10,000 Gaussian clusters (centres N(0,1), sigma 0.25), L2-normalised and
+quantized per row as NewFlatI8 does; queries from the same mixture; K = 100.
+One step is one TopKBatch of 4096 queries (C3's tensor-bound batch). The
+51 GB corpus is generated and uploaded 1M rows at a time, so it is never whole
+on the host, and it is far larger than L2, so no flush is needed between
+steps. Synthetic data stands in for the reference's Model2Vec embeddings.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-With --gpus N > 1 (launched under torch.distributed.run) the corpus rows are
-sharded contiguously over the ranks (strong scaling of the fixed C2 corpus):
-each rank runs the fused scan + top-K on its shard, the M x K candidate keys are
-all-gathered over NCCL and every rank merges them on the device. Consecutive
-batches are pipelined: a batch's all-gather and merge run on a second stream
-beside the next batch's GEMM, which leaves two SMs to the collective.
+With --gpus N > 1 (under torch.distributed.run) the C3 rows are split into N
+contiguous shards (strong scaling of the fixed corpus): each rank runs the
+GEMM + exact select on its shard, the 4096 x 100 candidate keys are
+all-gathered over NCCL and merged on every rank's device, a batch's all-gather
+overlapping the next batch's GEMM.
+
+At N = 1 the line also carries the other configurations as short legs:
+C3 at batch 256 and batch 1, C2 (configs[1], batch 64 and batch 1), C5
+(configs[4], batch 1024 at K = 1000 over heavy ties) and the FlatBinaryI8
+two-stage path on C4's per-GPU shard (configs[3], batch 1 and batch 512).
+Every leg checks sampled queries against the CPU oracle (parity); the
+cpu_baseline leg is that oracle (the reference's algorithm) timed on every host
+thread over the whole headline corpus.
 
 --impl reference times the reference's CPU algorithm (the C restatement under
-oracle/, the only CPU implementation that can run here: the reference is Go and
-no Go toolchain exists) on the host cores, on a bounded row sample.
+oracle/: the reference is Go and no Go toolchain exists) on the host cores,
+one FlatI8.Query per step over a row sample of the same corpus, and the
+reference's own CUDA kernels (gpu/anncuda/gemv_w8a8.cu compiled for sm_100a)
+on C2 as a device comparator.
 """
 from __future__ import annotations
 
@@ -37,15 +47,28 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_ROWS = 10_000_000
-DIM = 768
-K = 100
-BATCH = 64
-NCL = 1000
-SIGMA = 0.3
 SEED = 20260
 METRIC = "FlatI8 exact top-K queries/sec"
-WORKLOAD = "C2: FlatI8 N=10M d=768 mixture(1000 clusters, sigma 0.3), K=100, batch 64 (+ batch 1)"
+CHUNK = 1 << 20  # rows generated and uploaded at a time
+
+# BASELINE.json configs (C1 is the CPU-scale case, a parity-test size)
+C2 = dict(n=10_000_000, dim=768, ncl=1000, sigma=0.3, seed=SEED, k=100)
+C3 = dict(n=50_000_000, dim=1024, ncl=10_000, sigma=0.25, seed=SEED + 3, k=100)
+C3_BATCH, C3_BATCH_SMALL = 4096, 256
+C4 = dict(rows_per_gpu=25_000_000, dim=1024, seed=SEED + 4, k=10, over=100)
+C4_BATCH, C4_TENSOR_MIN = 512, 16
+C5 = dict(n=100_000_000, dim=256, seed=SEED + 5, k=1000)
+C5_BATCH = 1024
+
+WORKLOAD = ("C3: FlatI8 N=50M d=1024 mixture(10,000 clusters, sigma 0.25), K=100, batch 4096")
+
+
+def config(world: int) -> dict:
+    """The headline's config (the reference arm reports the same one)."""
+    return {"workload": WORKLOAD, "n_rows": C3["n"], "dim": C3["dim"], "k": C3["k"], "batch": C3_BATCH,
+            "parallelism": (f"row-shard x{world}, NCCL all-gather + device merge, overlapped with the next "
+                            "batch's GEMM") if world > 1 else "single GPU",
+            "l2": "corpus 51 GB >> 126 MB L2: inputs larger than L2, no flush"}
 
 
 def peaks():
@@ -57,53 +80,24 @@ def peaks():
 
 # DRAM traffic of one launch from an ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) next to that launch's algorithmic bytes; the ratio
-# scales the bench's average launch. Summaries: profiles/<kernel>_*.md.
+# scales the bench's mean launch. Summaries: profiles/<kernel>_*.md.
 NCU_TRAFFIC = {
-    "gemm_kernel": {"dram_bytes": 1493.600e6 + 5.124096e6, "algorithmic_bytes": 1_934_464 * (DIM + 4) + 64 * DIM,
-                    "profile": "profiles/gemm_kernel_c2_batch64.md"},
-    "scan_kernel": {"dram_bytes": 3.088071e9 + 3.871744e6, "algorithmic_bytes": 4_000_000 * (DIM + 4) + DIM * 4,
-                    "profile": "profiles/scan_kernel_c2_batch1.md"},
-    # binary (Hamming histogram) mode: 4M rows x 128-byte codes, plus the u16 distance written per row
-    "scan_kernel_binary": {"dram_bytes": 512.031744e6 + 10.409216e6,
-                           "algorithmic_bytes": 4_000_000 * 128 + 128 + 2 * 4_000_000,
-                           "profile": "profiles/scan_kernel_binary_c4.md"},
-    # Hamming-mode GEMM (tensor-core prefilter), batch 512: 737,856 sign rows of 1024 B, plus the query tile
-    # W8A8 GEMM at batch 4096 (C3 row shape): 737,856 rows of 1024 codes + scales, plus the query tile
-    "gemm_kernel_c3": {"dram_bytes": 763.026176e6 + 12.11648e6, "algorithmic_bytes": 737_856 * 1028 + 4096 * 1024,
-                       "profile": "profiles/gemm_kernel_c3_batch4096.md"},
-    "gemm_kernel_ham": {"dram_bytes": 756.334080e6 + 11.297024e6,
-                        "algorithmic_bytes": 737_856 * 1024 + 512 * 1024,
-                        "profile": "profiles/gemm_kernel_ham_c4_batch512.md"},
+    "gemm_c2": (1493.600e6 + 5.124096e6, 1_934_464 * (768 + 4) + 64 * 768, "profiles/gemm_kernel_c2_batch64.md"),
+    "scan_c2": (3.088071e9 + 3.871744e6, 4_000_000 * (768 + 4) + 768 * 4, "profiles/scan_kernel_c2_batch1.md"),
+    "scan_binary": (512.031744e6 + 10.409216e6, 4_000_000 * 128 + 128 + 2 * 4_000_000,
+                    "profiles/scan_kernel_binary_c4.md"),
+    "gemm_c3": (763.026176e6 + 12.11648e6, 737_856 * 1028 + 4096 * 1024, "profiles/gemm_kernel_c3_batch4096.md"),
+    "gemm_ham": (756.334080e6 + 11.297024e6, 737_856 * 1024 + 512 * 1024, "profiles/gemm_kernel_ham_c4_batch512.md"),
 }
 
 
-def kernel_roofline(kt: dict, kernel: str, pk: dict, pk_kind: str, region_ms: float,
-                    ncu_key: str | None = None) -> dict:
-    """Roofline of the dominant kernel from the library's per-launch CUDA events
-    over the timed region: algorithmic bytes per launch / mean launch time."""
-    t = kt[kernel]
-    per_launch_bytes = t["bytes"] / t["launches"]
-    per_launch_ms = t["ms"] / t["launches"]
-    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
-    ncu = NCU_TRAFFIC.get(ncu_key or kernel)
-    out = {
-        "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-        "frac": achieved / pk["hbm_gbs"],
-        "traffic": per_launch_bytes * ncu["dram_bytes"] / ncu["algorithmic_bytes"] if ncu else None,
-        "kernel": kernel, "launches": t["launches"], "ms_per_launch": per_launch_ms,
-        "algorithmic_bytes_per_launch": per_launch_bytes,
-        "share_of_region": t["ms"] / region_ms,
-        "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
-        "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json copy bandwidth)",
-    }
-    if ncu:
-        out["traffic_source"] = (f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
-                                 "times this run's mean launch bytes")
-    return out
+def traffic(key: str, algorithmic: float):
+    dram, alg, _ = NCU_TRAFFIC[key]
+    return algorithmic * dram / alg
 
 
 # ----------------------------------------------------------------------------
-# clocks during the timed region (NVML sampler)
+# clocks during a timed region (NVML sampler)
 # ----------------------------------------------------------------------------
 class ClockSampler:
     REASONS = {
@@ -174,153 +168,316 @@ class ClockSampler:
         return out
 
 
-# ----------------------------------------------------------------------------
-# CPU baseline: the reference algorithm (oracle port) on a bounded row sample
-# ----------------------------------------------------------------------------
-def cpu_baseline(budget_s: float = 12.0):
-    import oracle
-    from aikit_b200 import synth
-    rows = 500_000
-    r = synth.Recipe(synth.MIXTURE, DIM, seed=SEED, ncl=NCL, sigma=SIGMA)
-    bq, bs = r.codes(rows)
-    Q = r.queries(BATCH)
-    threads = os.cpu_count() or 1
-    done, t0 = 0, time.perf_counter()
-    while done < BATCH and (done < 2 or time.perf_counter() - t0 < budget_s):
-        oracle.flat_i8_query(bq, bs, Q[done], K, nthreads=threads)  # FlatI8.Query per row of the batch
-        done += 1
-    dt = time.perf_counter() - t0
-    per_query_full = dt / done * (N_ROWS / rows)
-    return {
-        "value": 1.0 / per_query_full, "unit": "queries/s", "cores": threads, "kind": "port",
-        "sample": f"{done} batch-1 FlatI8.Query calls (quantize, W8A8 AVX2 column-sharded over {threads} "
-                  f"threads, topHits) over {rows:,} of the {N_ROWS:,} C2 rows; time scaled by "
-                  f"{N_ROWS // rows}x to the full corpus (the scan is linear in rows)",
-    }
+def short_clocks(c: dict) -> dict:
+    return {"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons")}
 
 
 # ----------------------------------------------------------------------------
-# distributed helpers
+# the cpu_baseline leg: the oracle (the reference's algorithm) as the checker
 # ----------------------------------------------------------------------------
+class FlatI8Check:
+    """FlatI8.Query on the CPU (the oracle port of ann/flat_i8.go:124-206, on
+    every host thread) for a few sampled queries, over every chunk of the
+    corpus as it is generated; the chunk answers merge by queryBatchSharded's
+    rule (ann/backend.go:262-277), which is exact because selection
+    decomposes. `seconds` is the CPU time of those full-corpus queries: the
+    cpu_baseline. `agree` compares the device's keys with the answers."""
+
+    def __init__(self, Q, k: int):
+        import oracle
+        self.oracle, self.Q, self.k = oracle, np.ascontiguousarray(Q, np.float32), k
+        self.threads = os.cpu_count() or 1
+        self.best = [(np.empty(0, np.int64), np.empty(0, np.float64)) for _ in range(len(Q))]
+        self.seconds, self.rows = 0.0, 0
+
+    def chunk(self, bq, bs, row0: int) -> None:
+        o = self.oracle
+        t = time.perf_counter()
+        for m, q in enumerate(self.Q):
+            i, s = o.flat_i8_query(bq, bs, q, self.k, nthreads=self.threads)
+            self.best[m] = o.merge_hits([self.best[m], (np.asarray(i, np.int64) + row0, s)], self.k)
+        self.seconds += time.perf_counter() - t
+        self.rows += len(bs)
+
+    def gather(self, world: int) -> None:
+        """Merge the ranks' shard answers (every rank calls it alike)."""
+        if world == 1:
+            return
+        import torch
+        import torch.distributed as dist
+        S, k = len(self.Q), self.k
+        idx = torch.full((S, k), -1, dtype=torch.int64, device="cuda")
+        sc = torch.zeros((S, k), dtype=torch.float64, device="cuda")
+        for m, (i, s) in enumerate(self.best):
+            idx[m, :len(i)] = torch.from_numpy(np.asarray(i, np.int64))
+            sc[m, :len(s)] = torch.from_numpy(np.asarray(s, np.float64))
+        gi = torch.empty((world, S, k), dtype=torch.int64, device="cuda")
+        gs = torch.empty((world, S, k), dtype=torch.float64, device="cuda")
+        dist.all_gather_into_tensor(gi.view(-1), idx.view(-1))
+        dist.all_gather_into_tensor(gs.view(-1), sc.view(-1))
+        gi, gs = gi.cpu().numpy(), gs.cpu().numpy()
+        for m in range(S):
+            parts = [(gi[r, m][gi[r, m] >= 0], gs[r, m][gi[r, m] >= 0]) for r in range(world)]
+            self.best[m] = self.oracle.merge_hits(parts, k)
+
+    def agree(self, keys_rows) -> bool:
+        """keys_rows: the device keys (uint64 [k]) of each sampled query."""
+        from aikit_b200.ann import unpack_keys
+        ok = True
+        for m, keys in enumerate(keys_rows):
+            gi, gs = unpack_keys(np.asarray(keys, np.uint64))
+            wi, ws = self.best[m]
+            n = len(wi)
+            ok &= gi[:n].astype(np.int64).tolist() == list(wi) and bool((gi[n:] < 0).all())
+            ok &= gs[:n].tobytes() == np.asarray(ws, np.float32).tobytes()
+        return bool(ok)
+
+
+class BinaryCheck:
+    """FlatBinaryI8.Query on the CPU (oracle port of ann/flat_binary_i8.go:
+    86-153) for sampled queries, chunk by chunk: each chunk's prefilterHist
+    shortlist (prefilter.go:145-216) joins the running one and the union is
+    cut again to the cand nearest under (distance, id) -- the global shortlist,
+    since the cut decomposes -- keeping the shortlist rows' int8 codes; at the
+    end the shortlist is reranked as the reference does (W8A8 over the cand
+    rows in id order, best k)."""
+
+    def __init__(self, Q, ctr, dim: int, k: int, over: int):
+        import oracle
+        self.o, self.Q, self.ctr, self.dim, self.k, self.cand = oracle, Q, ctr, dim, k, k * over
+        self.qc = [oracle.pack_row(q, ctr) for q in Q]
+        self.keep = [None] * len(Q)  # per query: (gids, codes, i8, scales) of the running shortlist
+
+    def chunk(self, bits, bq, bs, row0: int) -> None:
+        o = self.o
+        for m, qc in enumerate(self.qc):
+            ids = o.prefilter_hist(qc, bits, self.dim, self.cand)
+            part = (ids + row0, bits[ids], bq[ids], bs[ids])
+            if self.keep[m] is not None:
+                part = tuple(np.concatenate([a, b]) for a, b in zip(self.keep[m], part))
+                sel = o.prefilter_hist(qc, part[1], self.dim, self.cand)  # ids ascending = gids ascending
+                part = tuple(a[sel] for a in part)
+            self.keep[m] = part
+
+    def answers(self):
+        out = []
+        for m, q in enumerate(self.Q):
+            gids, bits, bq, bs = self.keep[m]
+            # the shortlist is the whole candidate set: FlatI8's exact top-k over
+            # its rows (flat_binary_i8.go:95-97), i.e. the rerank
+            i, s = self.o.flat_binary_i8_query(bits, self.ctr, bq, bs, self.cand, q, self.k)
+            out.append((gids[np.asarray(i, np.int64)], s))
+        return out
+
+    def agree(self, keys_rows) -> bool:
+        from aikit_b200.ann import unpack_keys
+        ok = True
+        for (wi, ws), keys in zip(self.answers(), keys_rows):
+            gi, gs = unpack_keys(np.asarray(keys, np.uint64))
+            ok &= gi.astype(np.int64).tolist() == list(wi)
+            ok &= gs.tobytes() == np.asarray(ws, np.float32).tobytes()
+        return bool(ok)
+
+
+# ----------------------------------------------------------------------------
+# corpus builds: generated and uploaded one chunk at a time
+# ----------------------------------------------------------------------------
+def build_i8(be, recipe, lo: int, hi: int, check=None):
+    ix = be.NewI8IndexEmpty(hi - lo, recipe.d, id_base=lo)
+    q = np.empty((CHUNK, recipe.d), np.int8)
+    s = np.empty(CHUNK, np.float32)
+    gen = up = 0.0
+    for r0 in range(lo, hi, CHUNK):
+        m = min(CHUNK, hi - r0)
+        t = time.perf_counter()
+        recipe.codes(m, row0=r0, out_q=q[:m], out_s=s[:m])
+        gen += time.perf_counter() - t
+        if check is not None:
+            check.chunk(q[:m], s[:m], r0)
+        t = time.perf_counter()
+        ix.upload_rows(r0 - lo, q[:m], s[:m])
+        up += time.perf_counter() - t
+    t = time.perf_counter()
+    ix.upload_finish()
+    up += time.perf_counter() - t
+    return ix, {"gen_s": round(gen, 1), "upload_s": round(up, 1)}
+
+
+def build_binary(be, recipe, ctr, lo: int, hi: int, over: int, check=None):
+    bix = be.NewBinaryI8IndexEmpty(hi - lo, recipe.d, ctr, over, id_base=lo)
+    gen = up = 0.0
+    for r0 in range(lo, hi, CHUNK):
+        m = min(CHUNK, hi - r0)
+        t = time.perf_counter()
+        bits, q, s = recipe.binary(m, ctr, row0=r0)
+        gen += time.perf_counter() - t
+        if check is not None:
+            check.chunk(bits, q, s, r0)
+        t = time.perf_counter()
+        bix.upload_rows(r0 - lo, bits, q, s)
+        up += time.perf_counter() - t
+    t = time.perf_counter()
+    bix.upload_finish()
+    up += time.perf_counter() - t
+    return bix, {"gen_s": round(gen, 1), "upload_s": round(up, 1)}
+
+
+# ----------------------------------------------------------------------------
+# timing helpers
+# ----------------------------------------------------------------------------
+def timed(step, nsteps: int, stream, index, kernel_events: bool, world: int = 1, finish=None):
+    """Device time of nsteps steps on `stream` (CUDA events, barrier and sync
+    on both sides, max over ranks), the kernels launched, and, with
+    kernel_events, the library's per-kernel event times."""
+    import torch
+    import torch.distributed as dist
+    index.kernel_times(reset=True)
+    index.set_kernel_timing(kernel_events)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    launches = 0
+    for i in range(nsteps):
+        launches += step(i)
+    if finish is not None:
+        finish()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    index.set_kernel_timing(False)
+    kt = index.kernel_times(reset=True)
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, launches, kt
+
+
+def hbm_roof(kt: dict, kernel: str, pk: dict, pk_kind: str, ncu_key: str) -> dict:
+    """Roofline of an HBM-bound kernel from the library's per-launch events:
+    algorithmic bytes per launch / mean launch time, against the measured
+    copy bandwidth."""
+    t = kt[kernel]
+    per_b = t["bytes"] / t["launches"]
+    per_ms = t["ms"] / t["launches"]
+    ach = per_b / (per_ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / pk["hbm_gbs"], 4), "traffic": round(traffic(ncu_key, per_b)),
+            "kernel": kernel, "launches": t["launches"], "ms_per_launch": round(per_ms, 5),
+            "algorithmic_bytes_per_launch": per_b,
+            "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json, copy bandwidth)",
+            "traffic_source": f"ncu DRAM bytes / algorithmic bytes of one launch ({NCU_TRAFFIC[ncu_key][2]}) x "
+                              "this run's mean launch bytes"}
+
+
+def tensor_roof(kt: dict, ops_per_step: float, steps: int, peak, ncu_key: str, step_bytes: float,
+                kernel: str = "gemm_kernel") -> dict:
+    """Roofline of a tensor-bound batch: the batch's int8 ops over its GEMM
+    launches' event time, against our tcgen05 kind::i8 probe (MEASURED_PEAKS.json
+    has no int8 figure)."""
+    g = kt[kernel]
+    gemm_ms = g["ms"] / steps
+    ach = ops_per_step / (gemm_ms / 1e3)
+    return {"bound": "tensor", "achieved": round(ach / 1e12, 1), "peak": round(peak["ops"] / 1e12, 1),
+            "unit": "TOP/s (int8)", "frac": round(ach / peak["ops"], 4),
+            "frac_of_burst_probe": round(ach / peak["burst_ops"], 4),
+            "traffic": round(traffic(ncu_key, step_bytes)), "traffic_unit": "bytes per step",
+            "kernel": kernel, "launches": g["launches"], "gemm_ms_per_step": round(gemm_ms, 3),
+            "algorithmic_ops_per_step": ops_per_step,
+            "peak_source": peak["source"],
+            "traffic_source": f"ncu DRAM bytes / algorithmic bytes of one launch ({NCU_TRAFFIC[ncu_key][2]}) x "
+                              "this step's corpus bytes"}
+
+
+def kernel_summary(kt: dict, steps: int) -> dict:
+    return {k: [v["launches"], round(v["ms"] / steps, 3)] for k, v in kt.items()}
+
+
 def dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
+# ----------------------------------------------------------------------------
+# the B200 arm
+# ----------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--rows", type=int, default=N_ROWS, help=argparse.SUPPRESS)
     args = ap.parse_args()
     world, rank, local = dist_env()
-
     if args.impl == "reference":
-        if rank != 0:
-            return 0
-        return reference_arm(args, world)
+        return 0 if rank != 0 else reference_arm(args, world, local)
 
     import torch
     import torch.distributed as dist
     from aikit_b200 import synth
     from aikit_b200.ann import B200Backend, unpack_keys
+    from aikit_b200.dist import ShardedTopK, shard_bounds
 
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    from aikit_b200.dist import ShardedTopK, shard_bounds
-    n_total = args.rows
-    lo, hi = shard_bounds(n_total, world, rank)
-    recipe = synth.Recipe(synth.MIXTURE, DIM, seed=SEED, ncl=NCL, sigma=SIGMA)
-    t0 = time.time()
-    bq, bs = recipe.codes(hi - lo, row0=lo)
-    gen_s = time.time() - t0
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     be = B200Backend(local)
-    t0 = time.perf_counter()
-    ix = be.NewI8Index(bq, bs, hi - lo, DIM, id_base=lo)
-    upload_s = time.perf_counter() - t0
-    upload_bytes = bq.nbytes + bs.nbytes
-    del bq, bs
-
-    nb = 8  # distinct query batches cycled through the steps
-    Qh = recipe.queries(nb * BATCH).reshape(nb, BATCH, DIM)
-    Qd = torch.from_numpy(Qh).cuda()
-    # a dedicated (non-default) stream: events, launches and NCCL all order on it
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    st = stream.cuda_stream
+    pk, pk_kind = peaks()
+    peak = tensor_peak(be, local)  # first, while the GPU is idle and cool (the burst figure)
+    M, K = C3_BATCH, C3["k"]
+
+    # --- C3 headline: build the shard; the cpu_baseline leg checks sampled queries
+    recipe = synth.Recipe(synth.MIXTURE, C3["dim"], seed=C3["seed"], ncl=C3["ncl"], sigma=C3["sigma"])
+    nb = 2  # distinct query batches cycled through the steps
+    Qh = recipe.queries(nb * M).reshape(nb, M, C3["dim"])
+    sample = [0, C3_BATCH_SMALL - 1, M // 2, M - 1]  # of batch 0: also the batch-256 and batch-1 legs' queries
+    check = FlatI8Check(Qh[0][sample], K)
+    lo, hi = shard_bounds(C3["n"], world, rank)
+    t0 = time.time()
+    ix, build = build_i8(be, recipe, lo, hi, check)
+    build["wall_s"] = round(time.time() - t0, 1)
+    Qd = torch.from_numpy(Qh).cuda()
     sharded = ShardedTopK(ix, be.ctx, world, stream, overlap=world > 1)
     result = {}
 
-    def step(i, m=BATCH):
-        # multi-GPU runs the batch-64 form only: local scan, all-gather, merge
-        result["keys"] = sharded.topk_async(Qd[i % nb].data_ptr(), m, K)
+    def step(i):
+        result[i % nb] = sharded.topk_async(Qd[i % nb].data_ptr(), M, K)
         return ix.last_launch_count() + (1 if world > 1 else 0)
 
-    def timed(nsteps, m, kernel_events=False):
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        # per-kernel CUDA events (recorded by the library on this stream); they
-        # separate the launches, so the headline pass runs without them
-        ix.kernel_times(reset=True)
-        ix.set_kernel_timing(kernel_events)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        launches = 0
-        for i in range(nsteps):
-            launches += step(i, m)
-        sharded.wait()  # the last batches' all-gathers and merges are inside the region
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        ix.set_kernel_timing(False)
-        kt = ix.kernel_times(reset=True)
-        ms = ev0.elapsed_time(ev1)
-        if world > 1:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms, launches, kt
-
-    # warm-up (both batch forms), then the timed regions
     for i in range(args.warmup):
         step(i)
-        step(i, 1) if world == 1 else None
+    sharded.wait()
     torch.cuda.synchronize()
     ix.sync()
-
     with ClockSampler(local) as clk:
-        ms64, launches, _ = timed(args.steps, BATCH)
-        ms1, launches1, _ = timed(args.steps, 1) if world == 1 else (None, 0, {})
-        # the same steps again with an event pair around every kernel: the
-        # per-kernel durations behind the rooflines
-        ms64_ev, _, kt64 = timed(args.steps, BATCH, kernel_events=True)
-        ms1_ev, _, kt1 = timed(args.steps, 1, kernel_events=True) if world == 1 else (None, 0, {})
+        ms, launches, _ = timed(step, args.steps, stream, ix, False, world, sharded.wait)
+        ms_ev, _, kt = timed(step, args.steps, stream, ix, True, world, sharded.wait)
     ix.sync()
+    step(0)  # batch 0 once more, for the parity check
+    sharded.wait()
+    torch.cuda.synchronize()
+    batch0 = result[0].cpu().numpy().view(np.uint64)
+    check.gather(world)
+    parity = check.agree(batch0[sample])
 
-    # e2e through the public C ABI with host buffers (pinned), N=1: fi8_topk_batch
-    e2e = None
+    # e2e: pinned host queries in, keys out, every step
+    Qpin = torch.from_numpy(Qh.copy()).pin_memory()
     if world == 1:
-        Qpin = torch.from_numpy(Qh.copy()).pin_memory().numpy()
-        for i in range(2):
-            ix.topk_arrays(Qpin[i % nb], K)
+        Qpn = Qpin.numpy()
+        ix.topk_arrays(Qpn[0], K)
         t0 = time.perf_counter()
         for i in range(args.steps):
-            idx, sc = ix.topk_arrays(Qpin[i % nb], K)
+            ix.topk_arrays(Qpn[i % nb], K)
         e2e_s = time.perf_counter() - t0
-        e2e = {"value": BATCH * args.steps / e2e_s, "unit": "queries/s",
-               "h2d_bytes_per_step": BATCH * DIM * 4, "d2h_bytes_per_step": BATCH * K * 8,
-               "api": "fi8_topk_batch (include/fi8.h) with pinned host query buffer"}
+        api = "fi8_topk_batch (include/fi8.h): pinned host queries in, ids and scores out"
     else:
-        # multi-GPU e2e: pinned host queries -> device, scan, all-gather, merge, keys -> host
-        Qpin = torch.from_numpy(Qh.copy()).pin_memory()
-        hk = torch.empty((BATCH, K), dtype=torch.int64).pin_memory()
+        hk = torch.empty((M, K), dtype=torch.int64).pin_memory()
         dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -328,361 +485,383 @@ def main():
             Qd[i % nb].copy_(Qpin[i % nb], non_blocking=True)
             step(i)
             sharded.wait()
-            hk.copy_(result["keys"], non_blocking=True)
+            hk.copy_(result[i % nb], non_blocking=True)
             torch.cuda.synchronize()
             unpack_keys(hk.numpy().view(np.uint64))
         e2e_s = time.perf_counter() - t0
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-        e2e = {"value": BATCH * args.steps / e2e_s, "unit": "queries/s",
-               "h2d_bytes_per_step": BATCH * DIM * 4, "d2h_bytes_per_step": BATCH * K * 8,
-               "api": "fi8_topk_batch_async + NCCL all-gather + fi8_merge_keys_async, pinned host I/O"}
+        api = "fi8_topk_batch_async + NCCL all-gather + fi8_merge_keys_async, pinned host I/O"
+    e2e = {"value": round(M * args.steps / e2e_s, 1), "unit": "queries/s",
+           "h2d_bytes_per_step": M * C3["dim"] * 4, "d2h_bytes_per_step": M * K * 8, "api": api}
 
-    # sanity: spot-check one query of the last batch against the device answer shape
-    gidx, _ = unpack_keys(result["keys"].cpu().numpy().view(np.uint64))
-    assert (gidx[0] >= 0).all(), "top-K came back short"
-
+    legs, detail = {}, {"c3_kernels": kernel_summary(kt, args.steps), "c3_build": build,
+                        "tensor_probe": {k: v for k, v in peak.items() if k != "source"}}
+    if world == 1:
+        legs.update(c3_small_legs(ix, args, stream, pk, pk_kind, check, Qd, sample, local, detail))
+    ix.Close()
+    del Qd
+    torch.cuda.empty_cache()
+    if world == 1:
+        legs["c2"] = c2_leg(be, args, stream, pk, pk_kind, local, detail)
+        legs["c5"] = c5_leg(be, args, stream, peak, local, detail)
+        legs["c4"] = c4_leg(be, args, stream, pk, pk_kind, peak, local, detail)
+    else:
+        legs["c4_sharded"] = c4_sharded_leg(be, args, stream, peak, world, rank, local, detail)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return 0
 
-    pk, pk_kind = peaks()
-    shard_rows = hi - lo
-    per_step_ms = ms64 / args.steps
-    value = BATCH * args.steps / (ms64 / 1e3)
-    roof64 = kernel_roofline(kt64, "gemm_kernel", pk, pk_kind, ms64_ev)
-    roof64["kernel_events_pass_ms_per_step"] = ms64_ev / args.steps
+    ops = 2.0 * M * (hi - lo) * C3["dim"]  # this rank's shard, per step
+    roof = tensor_roof(kt, ops, args.steps, peak, "gemm_c3", (hi - lo) * (C3["dim"] + 4) + M * C3["dim"])
+    if world > 1:
+        roof["note"] = "rank 0's GEMM over its shard"
     out = {
-        "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step_ms,
-        "higher_is_better": True, "scaling": "strong",  # a fixed corpus split over the ranks
-        "vs_baseline": None, "dtype": "int8 (int32 accumulate, f32 epilogue)", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "n_rows": n_total, "dim": DIM, "k": K, "batch": BATCH,
-                   "parallelism": (f"row-shard x{world}, NCCL all-gather + merge of a batch overlapped with the next "
-                                   "batch's GEMM") if world > 1 else "single GPU",
-                   "l2": "corpus 7.7 GB >> 126 MB L2: no flush needed",
-                   "corpus_gen_s": round(gen_s, 1),
-                   "upload": {"s": round(upload_s, 3), "gbs": round(upload_bytes / upload_s / 1e9, 1),
-                              "api": "fi8_index_create from pageable host arrays (pinned double-buffer staging)"}},
-        "roofline": roof64,
-        "gpu_launches": launches + launches1,
+        "metric": METRIC, "value": round(M * args.steps / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 (int32 accumulate, f32 epilogue)", "data": "synthetic (seeded C3 mixture recipe)",
+        "config": config(world),
+        "roofline": roof,
+        "gpu_launches": launches,
         "e2e": e2e,
         "clocks": clk.summary(),
+        "parity": ("exact" if parity else "MISMATCH") + f": {len(sample)} sampled queries vs the CPU oracle "
+                  "(ids + f32 score bits)",
     }
-    if ms1 is not None:
-        per1 = ms1 / args.steps
-        out["batch1"] = {"value": 1e3 / per1, "unit": "queries/s", "ms_per_query": per1,
-                         "roofline": kernel_roofline(kt1, "scan_kernel", pk, pk_kind, ms1_ev)}
+    if world > 1:
+        out["legs"] = legs
     if world == 1:
-        peak_ops, probe_ms = be.ctx.probe_tensor_i8(60000)  # the int8 tensor roofline, measured live
-        tensor_peak = (peak_ops, probe_ms)
-        out["c3_sample"] = c3_leg(be, args, stream, local, tensor_peak)
-        out["flat_binary"] = binary_leg(be, args, stream, pk, pk_kind, local, tensor_peak)
-        out["cpu_baseline"] = cpu_baseline()
-    print(json.dumps(out))
+        out["cpu_baseline"] = {
+            "value": round(len(sample) / check.seconds, 3), "unit": "queries/s", "cores": check.threads,
+            "kind": "port",
+            "sample": f"{len(sample)} FlatI8.Query calls (oracle port: AVX2 W8A8 column-split over "
+                      f"{check.threads} threads, topHits) over all {check.rows:,} C3 rows, 1M-row chunks merged "
+                      "by queryBatchSharded's rule; the reference's QueryBatch runs one Query per query on the CPU"}
+        out["legs"] = legs
+    print("bench-detail " + json.dumps(detail), file=sys.stderr)
+    print(json.dumps(out, separators=(",", ":")))
     return 0
 
 
-# ----------------------------------------------------------------------------
-# C3 row shape, tensor-bound batch: a row sample of the 50M-row corpus
-# ----------------------------------------------------------------------------
-C3_ROWS = 4_000_000   # a sample of C3's 50M rows (6.25M per GPU at 8)
-C3_DIM = 1024
-C3_K = 100
-C3_BATCH = 4096
+def tensor_peak(be, local: int = 0) -> dict:
+    """Our tcgen05 kind::i8 probe (MEASURED_PEAKS.json has no int8 figure),
+    measured the way MEASURED_PEAKS.json measures bf16: a burst (the best of
+    three ~20 ms launches) for kernels timed alone, and sustained (launches
+    of ~0.4 s back to back for ~4 s under the power cap, the median of the
+    last five) for kernels timed inside a long step."""
+    burst = max(be.ctx.probe_tensor_i8(60000)[0] for _ in range(3))
+    runs = []
+    with ClockSampler(local) as clk:
+        for _ in range(10):
+            runs.append(be.ctx.probe_tensor_i8(1_200_000)[0])
+    sustained = statistics.median(runs[5:])
+    c = clk.summary()
+    return {"burst_ops": burst, "sustained_ops": sustained, "ops": sustained,
+            "clocks": {"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons"),
+                       "power_w_median": c.get("power_w_median")},
+            "source": f"fi8_probe_tensor_i8 (back-to-back kind::i8 MMAs on every SM, shared-memory operands): "
+                      f"sustained {sustained / 1e12:.0f} TOP/s (~4 s under the power cap, median of the last five "
+                      f"0.4 s launches), the denominator for a GEMM timed inside seconds-long steps; burst "
+                      f"{burst / 1e12:.0f} TOP/s (best of three 20 ms launches) in frac_of_burst_probe"}
 
 
-def c3_leg(be, args, stream, local, tensor_peak):
-    """TopKBatch of 4096 queries (C3's large batch) over a 4M-row sample of
-    the C3 corpus recipe (10,000 clusters, sigma 0.25, d = 1024, K = 100). The
-    GEMM is tensor-bound here: the roofline is its int8 ops against our own
-    tcgen05 probe's measured peak."""
+def c3_small_legs(ix, args, stream, pk, pk_kind, check, Qd, sample, local, detail) -> dict:
+    """C3's HBM-bound forms on the same corpus: batch 256 (one GEMM pass) and
+    batch 1 (the fused scan), both checked against the oracle's answers for
+    the same queries."""
+    import torch
+    st = stream.cuda_stream
+    K = C3["k"]
+    legs = {}
+    for name, M in (("c3_b256", C3_BATCH_SMALL), ("c3_b1", 1)):
+        keys = torch.zeros((M, K), dtype=torch.int64, device="cuda")
+
+        def step(i):
+            ix.topk_async(Qd[0].data_ptr(), M, K, keys.data_ptr(), st)
+            return ix.last_launch_count()
+
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        ix.sync()
+        with ClockSampler(local) as clk:
+            ms, launches, _ = timed(step, args.steps, stream, ix, False)
+            _, _, kt = timed(step, args.steps, stream, ix, True)
+        ix.sync()
+        got = keys.cpu().numpy().view(np.uint64)
+        rows = [i for i, s in enumerate(sample) if s < M]
+        ok = FlatI8Check.agree(_subset(check, rows), got[[sample[i] for i in rows]])
+        kern, ncu = ("gemm_kernel", "gemm_c3") if M > 1 else ("scan_kernel", "scan_c2")
+        roof = hbm_roof(kt, kern, pk, pk_kind, ncu)
+        legs[name] = {"qps": round(M * args.steps / (ms / 1e3), 1), "ms": round(ms / args.steps, 3),
+                      "hbm_frac": roof["frac"], "parity": "exact" if ok else "MISMATCH",
+                      "clk": short_clocks(clk.summary())}
+        detail[name] = {"roofline": roof, "kernels": kernel_summary(kt, args.steps), "launches": launches}
+    return legs
+
+
+def _subset(check, rows):
+    sub = FlatI8Check.__new__(FlatI8Check)
+    sub.best = [check.best[i] for i in rows]
+    return sub
+
+
+def c2_leg(be, args, stream, pk, pk_kind, local, detail) -> dict:
+    """C2: 10M x 768, K = 100, batch 64 and batch 1 -- the
+    previous headline, kept comparable."""
     import torch
     from aikit_b200 import synth
-    from aikit_b200.ann import unpack_keys
-    r = synth.Recipe(synth.MIXTURE, C3_DIM, seed=SEED + 3, ncl=10000, sigma=0.25)
-    bq, bs = r.codes(C3_ROWS)
-    ix = be.NewI8Index(bq, bs, C3_ROWS, C3_DIM)
-    del bq, bs
-    Q = torch.from_numpy(r.queries(C3_BATCH)).cuda()
-    keys = torch.zeros((C3_BATCH, C3_K), dtype=torch.int64, device="cuda")
+    r = synth.Recipe(synth.MIXTURE, C2["dim"], seed=C2["seed"], ncl=C2["ncl"], sigma=C2["sigma"])
+    Q = r.queries(64)
+    check = FlatI8Check(Q[[0, 63]], C2["k"])
+    ix, build = build_i8(be, r, 0, C2["n"], check)
+    Qd = torch.from_numpy(Q).cuda()
     st = stream.cuda_stream
-    steps = max(3, min(args.steps, 5))  # each step is ~15 ms of tensor work
+    out = {}
+    for name, M in (("b64", 64), ("b1", 1)):
+        keys = torch.zeros((M, C2["k"]), dtype=torch.int64, device="cuda")
 
-    def step():
-        ix.topk_async(Q.data_ptr(), C3_BATCH, C3_K, keys.data_ptr(), st)
-        return ix.last_launch_count()
+        def step(i):
+            ix.topk_async(Qd.data_ptr(), M, C2["k"], keys.data_ptr(), st)
+            return ix.last_launch_count()
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    ix.sync()
-
-    def timed(kernel_events):
-        ix.kernel_times(reset=True)
-        ix.set_kernel_timing(kernel_events)
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
+        for i in range(args.warmup):
+            step(i)
         torch.cuda.synchronize()
-        ev0.record(stream)
-        n_launch = sum(step() for _ in range(steps))
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        ix.set_kernel_timing(False)
-        return ev0.elapsed_time(ev1), n_launch, ix.kernel_times(reset=True)
-
-    with ClockSampler(local) as clk:
-        ms, launches, _ = timed(False)
-        _, _, kt = timed(True)
-    ix.sync()
-    gidx, _ = unpack_keys(keys.cpu().numpy().view(np.uint64))
-    assert (gidx >= 0).all(), "C3 top-K came back short"
+        ix.sync()
+        with ClockSampler(local) as clk:
+            ms, launches, _ = timed(step, args.steps, stream, ix, False)
+            _, _, kt = timed(step, args.steps, stream, ix, True)
+        ix.sync()
+        got = keys.cpu().numpy().view(np.uint64)
+        ok = check.agree(got[[0, 63]]) if M == 64 else _subset(check, [0]).agree(got[[0]])
+        kern, ncu = ("gemm_kernel", "gemm_c2") if M > 1 else ("scan_kernel", "scan_c2")
+        roof = hbm_roof(kt, kern, pk, pk_kind, ncu)
+        out[name] = {"qps": round(M * args.steps / (ms / 1e3), 1), "ms": round(ms / args.steps, 3),
+                     "hbm_frac": roof["frac"], "parity": "exact" if ok else "MISMATCH",
+                     "clk": short_clocks(clk.summary())}
+        detail["c2_" + name] = {"roofline": roof, "kernels": kernel_summary(kt, args.steps), "build": build}
+    # e2e of the batch-64 form through the host entry point
+    Qpin = torch.from_numpy(Q.copy()).pin_memory().numpy()
+    ix.topk_arrays(Qpin, C2["k"])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        ix.topk_arrays(Qpin, C2["k"])
+    out["b64"]["e2e_qps"] = round(64 * args.steps / (time.perf_counter() - t0), 1)
     ix.Close()
-    peak_ops, probe_ms = tensor_peak
-    gemm_ms = kt["gemm_kernel"]["ms"] / steps
-    ops = 2.0 * C3_BATCH * C3_ROWS * C3_DIM
-    achieved = ops / (gemm_ms / 1e3)
-    ncu = NCU_TRAFFIC["gemm_kernel_c3"]
-    traffic = (C3_ROWS * (C3_DIM + 4) + C3_BATCH * C3_DIM) * ncu["dram_bytes"] / ncu["algorithmic_bytes"]
-    return {
-        "metric": "FlatI8 exact top-K queries/sec, batch 4096", "value": C3_BATCH * steps / (ms / 1e3),
-        "unit": "queries/s", "ms_per_step": ms / steps, "steps": steps,
-        "config": {"workload": f"C3 row shape: {C3_ROWS:,}-row sample of the 50M-row mixture (10,000 clusters, "
-                               f"sigma 0.25), d={C3_DIM}, K={C3_K}, batch {C3_BATCH}",
-                   "l2": "codes 4.1 GB > 126 MB L2"},
-        "roofline": {"bound": "tensor", "achieved": achieved / 1e12, "peak": peak_ops / 1e12, "unit": "TOPS",
-                     "frac": achieved / peak_ops, "traffic": traffic, "traffic_unit": "bytes per step",
-                     "traffic_source": f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
-                                       "times this step's corpus bytes",
-                     "kernel": "gemm_kernel (W8A8)",
-                     "gemm_ms_per_step": gemm_ms, "algorithmic_ops_per_step": ops,
-                     "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
-                     "peak_source": f"fi8_probe_tensor_i8 measured live ({probe_ms:.1f} ms)"},
-        "gpu_launches": launches,
-        "clocks": clk.summary(),
-    }
-
-
-# ----------------------------------------------------------------------------
-# FlatBinaryI8 (C4 row shape): sign-bit Hamming prefilter + int8 rerank
-# ----------------------------------------------------------------------------
-BIN_ROWS = 25_000_000  # C4's per-GPU shard (C4: 2e8 rows over 8 GPUs)
-BIN_DIM = 1024
-BIN_K = 10
-BIN_OVER = 100         # cand = K * over = 1000, BASELINE's shortlist
-BIN_BATCH = 512        # C4's batch form
-BIN_TENSOR_MIN = 16    # batches of at least this many queries prefilter on the tensor cores
-
-
-def binary_leg(be, args, stream, pk, pk_kind, local, tensor_peak):
-    """Batch-1 FlatBinaryI8 queries on C4's per-GPU shard: device-resident
-    prefilter + rerank timed on the device, then the host entry point."""
-    import torch
-    from aikit_b200 import synth
-    from aikit_b200.ann import unpack_keys
-    r = synth.Recipe(synth.UNIT, BIN_DIM, seed=SEED + 4)
-    t0 = time.time()
-    ctr = r.center(BIN_ROWS)
-    bits, q8, sc = r.binary(BIN_ROWS, ctr)
-    gen_s = time.time() - t0
-    bix = be.NewBinaryI8Index(bits, bits.shape[1], ctr, q8, sc, BIN_ROWS, BIN_DIM, BIN_OVER)
-    del q8, sc
-    cand = BIN_K * BIN_OVER
-    nb = 16
-    Qh = r.queries(nb)
-    Qd = torch.from_numpy(Qh).cuda()
-    short = torch.zeros((1, cand), dtype=torch.int64, device="cuda")
-    keys = torch.zeros((1, BIN_K), dtype=torch.int64, device="cuda")
-    st = stream.cuda_stream
-
-    def step(i):
-        bix.prefilter_async(Qd[i % nb].data_ptr(), 1, cand, short.data_ptr(), st, sorted_keys=False)
-        n = bix.last_launch_count()
-        bix.rerank_async(Qd[i % nb].data_ptr(), 1, short.data_ptr(), cand, BIN_K, keys.data_ptr(), st)
-        return n + bix.last_launch_count()
-
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    bix.sync()
-
-    def timed(kernel_events):
-        bix.kernel_times(reset=True)
-        bix.set_kernel_timing(kernel_events)
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        n_launch = 0
-        for i in range(args.steps):
-            n_launch += step(i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        bix.set_kernel_timing(False)
-        return ev0.elapsed_time(ev1), n_launch, bix.kernel_times(reset=True)
-
-    with ClockSampler(local) as clk:
-        ms, launches, _ = timed(False)       # the headline: launches back to back
-        ms_ev, _, kt = timed(True)           # the same steps with per-kernel events
-    bix.sync()
-    gidx, _ = unpack_keys(keys.cpu().numpy().view(np.uint64))
-    assert (gidx[0] >= 0).all(), "binary top-K came back short"
-    # e2e: the host entry point (fi8_bin_query_topk) from pinned query rows
-    Qpin = torch.from_numpy(Qh.copy()).pin_memory().numpy()
-    bix.topk_arrays(Qpin[0:1], BIN_K)
-    t1 = time.perf_counter()
-    for i in range(args.steps):
-        bix.topk_arrays(Qpin[i % nb:i % nb + 1], BIN_K)
-    e2e_s = time.perf_counter() - t1
-    out = {
-        "metric": "FlatBinaryI8 top-K queries/sec", "value": args.steps / (ms / 1e3), "unit": "queries/s",
-        "ms_per_query": ms / args.steps, "dtype": "u64 popcount + int8 rerank",
-        "config": {"workload": f"C4 row shape: d={BIN_DIM} sign codes (128 B) of centred N(0,1) rows + int8 "
-                               f"copies, K={BIN_K}, overquery {BIN_OVER} (cand {cand}), batch 1, "
-                               f"{BIN_ROWS:,} rows (C4's per-GPU shard of 200M rows over 8 GPUs)",
-                   "n_rows": BIN_ROWS, "codes_bytes": int(bits.nbytes),
-                   "l2": f"codes {bits.nbytes / 1e9:.1f} GB > 126 MB L2",
-                   "corpus_gen_s": round(gen_s, 1)},
-        "roofline": dict(kernel_roofline(kt, "scan_kernel", pk, pk_kind, ms_ev, ncu_key="scan_kernel_binary"),
-                         kernel_events_pass_ms_per_query=ms_ev / args.steps),
-        "gpu_launches": launches,
-        "e2e": {"value": args.steps / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": BIN_DIM * 4,
-                "d2h_bytes_per_step": BIN_K * 8, "api": "fi8_bin_query_topk (include/fi8.h), pinned host query"},
-        "clocks": clk.summary(),
-        "cpu_baseline": binary_cpu_baseline(bits, ctr, Qh, r),
-    }
-    out["batch512"] = binary_batch_leg(be, bix, r, args, stream, local, tensor_peak)
-    bix.Close()
+    torch.cuda.empty_cache()
     return out
 
 
-def binary_batch_leg(be, bix, r, args, stream, local, tensor_peak):
-    """C4's batch form on the same shard: 512 queries per step, the prefilter
-    as one tcgen05 kind::i8 GEMM over the codes unpacked to +1/-1 int8 rows
-    (dot = dim - 2 * distance), then the rerank. Tensor-bound: the roofline is
-    the GEMM's int8 ops against our own tcgen05 probe's measured peak."""
+def c5_leg(be, args, stream, peak, local, detail) -> dict:
+    """C5: 100M x 256 codes uniform over {-2..2} with the scale
+    fixed at 1/127 (the FI8 blob a hand-written corpus would hold), queries
+    from the same distribution, batch 1024 at K = 1000: heavy exact ties."""
     import torch
-    from aikit_b200.ann import unpack_keys
-    M, cand = BIN_BATCH, BIN_K * BIN_OVER
-    peak_ops, probe_ms = tensor_peak
-    t0 = time.perf_counter()
-    bix.set_tensor_prefilter(BIN_TENSOR_MIN)
-    sign_s = time.perf_counter() - t0
-    nb = 2
-    Qh = r.queries(nb * M, row0=4096).reshape(nb, M, BIN_DIM)
-    Qd = torch.from_numpy(Qh).cuda()
-    short = torch.zeros((M, cand), dtype=torch.int64, device="cuda")
-    keys = torch.zeros((M, BIN_K), dtype=torch.int64, device="cuda")
+    from aikit_b200 import synth
+    r = synth.Recipe(synth.TIES, C5["dim"], seed=C5["seed"])
+    M, K = C5_BATCH, C5["k"]
+    Q = r.queries(M)
+    check = FlatI8Check(Q[[0, M - 1]], K)
+    ix, build = build_i8(be, r, 0, C5["n"], check)
+    Qd = torch.from_numpy(Q).cuda()
+    keys = torch.zeros((M, K), dtype=torch.int64, device="cuda")
     st = stream.cuda_stream
 
     def step(i):
-        bix.prefilter_async(Qd[i % nb].data_ptr(), M, cand, short.data_ptr(), st, sorted_keys=False)
-        n = bix.last_launch_count()
-        bix.rerank_async(Qd[i % nb].data_ptr(), M, short.data_ptr(), cand, BIN_K, keys.data_ptr(), st)
-        return n + bix.last_launch_count()
+        ix.topk_async(Qd.data_ptr(), M, K, keys.data_ptr(), st)
+        return ix.last_launch_count()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ix.sync()
+    steps = max(3, args.steps // 2)
+    with ClockSampler(local) as clk:
+        ms, launches, _ = timed(step, steps, stream, ix, False)
+        _, _, kt = timed(step, steps, stream, ix, True)
+    ix.sync()
+    got = keys.cpu().numpy().view(np.uint64)
+    ok = check.agree(got[[0, M - 1]])
+    ops = 2.0 * M * C5["n"] * C5["dim"]
+    roof = tensor_roof(kt, ops, steps, peak, "gemm_c3", C5["n"] * (C5["dim"] + 4))
+    ix.Close()
+    torch.cuda.empty_cache()
+    detail["c5"] = {"roofline": roof, "kernels": kernel_summary(kt, steps), "build": build}
+    return {"qps": round(M * steps / (ms / 1e3), 1), "ms": round(ms / steps, 3), "tensor_frac": roof["frac"],
+            "parity": "exact" if ok else "MISMATCH", "clk": short_clocks(clk.summary())}
+
+
+def c4_leg(be, args, stream, pk, pk_kind, peak, local, detail) -> dict:
+    """FlatBinaryI8 on C4's per-GPU shard (configs[3]: 200M rows over 8
+    GPUs): 25M sign codes (128 B) of centred N(0,1) rows plus their int8
+    copies, K = 10, overquery 100 (shortlist 1000); batch 1 (the popcount
+    pass, HBM-bound) and batch 512 (the prefilter on the tensor cores)."""
+    import torch
+    from aikit_b200 import synth
+    r = synth.Recipe(synth.UNIT, C4["dim"], seed=C4["seed"])
+    n, k, over = C4["rows_per_gpu"], C4["k"], C4["over"]
+    cand = k * over
+    ctr = r.center(CHUNK)  # the prefilter's centre: the mean of the first 1M rows
+    Q1 = r.queries(16)
+    Qb = r.queries(C4_BATCH, row0=4096)
+    check = BinaryCheck(np.concatenate([Q1[:1], Qb[[0, C4_BATCH - 1]]]), ctr, C4["dim"], k, over)
+    bix, build = build_binary(be, r, ctr, 0, n, over, check)
+    st = stream.cuda_stream
+    out = {}
+    for name, Q in (("b1", Q1), ("b512", Qb)):
+        M = 1 if name == "b1" else C4_BATCH
+        if M > 1:
+            t0 = time.perf_counter()
+            bix.set_tensor_prefilter(C4_TENSOR_MIN)
+            build["sign_rows_s"] = round(time.perf_counter() - t0, 2)
+        Qd = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
+        short = torch.zeros((M, cand), dtype=torch.int64, device="cuda")
+        keys = torch.zeros((M, k), dtype=torch.int64, device="cuda")
+        nq = len(Q) // M
+
+        def step(i):
+            q = Qd[(i % nq) * M:(i % nq + 1) * M].data_ptr()
+            bix.prefilter_async(q, M, cand, short.data_ptr(), st, sorted_keys=False)
+            n1 = bix.last_launch_count()
+            bix.rerank_async(q, M, short.data_ptr(), cand, k, keys.data_ptr(), st)
+            return n1 + bix.last_launch_count()
+
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        bix.sync()
+        with ClockSampler(local) as clk:
+            ms, launches, _ = timed(step, args.steps, stream, bix, False)
+            _, _, kt = timed(step, args.steps, stream, bix, True)
+        step(0)
+        torch.cuda.synchronize()
+        bix.sync()
+        got = keys.cpu().numpy().view(np.uint64)
+        if M == 1:
+            ok = BinaryCheck.agree(_bin_subset(check, [0]), got[[0]])
+            roof = hbm_roof(kt, "scan_kernel", pk, pk_kind, "scan_binary")
+            frac = {"hbm_frac": roof["frac"]}
+        else:
+            ok = BinaryCheck.agree(_bin_subset(check, [1, 2]), got[[0, M - 1]])
+            roof = tensor_roof(kt, 2.0 * M * n * C4["dim"], args.steps, peak, "gemm_ham", n * C4["dim"] + M * C4["dim"])
+            frac = {"tensor_frac": roof["frac"]}
+        Qpin = torch.from_numpy(np.ascontiguousarray(Q[:M])).pin_memory().numpy()
+        bix.topk_arrays(Qpin, k)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            bix.topk_arrays(Qpin, k)
+        e2e_qps = M * args.steps / (time.perf_counter() - t0)
+        out[name] = {"qps": round(M * args.steps / (ms / 1e3), 1), "ms": round(ms / args.steps, 3), **frac,
+                     "e2e_qps": round(e2e_qps, 1), "parity": "exact" if ok else "MISMATCH",
+                     "clk": short_clocks(clk.summary())}
+        detail["c4_" + name] = {"roofline": roof, "kernels": kernel_summary(kt, args.steps), "build": build}
+    bix.Close()
+    torch.cuda.empty_cache()
+    return out
+
+
+def c4_sharded_leg(be, args, stream, peak, world: int, rank: int, local: int, detail) -> dict:
+    """FlatBinaryI8 at N GPUs with C4's 25M rows per GPU (weak scaling; at
+    N = 8 this is C4's whole 200M-row corpus): each rank prefilters its shard
+    on the tensor cores, the M x cand shortlist keys are all-gathered and
+    merged into the global shortlist (the cand nearest over every rank's rows,
+    as the reference computes it over the whole corpus), every rank reranks
+    the shortlist rows it holds, and the M x k results are merged again
+    (aikit_b200.dist.ShardedBinary). Batch 512, K = 10, cand 1000. Parity:
+    the merged global shortlist of two sampled queries against the oracle's
+    prefilterHist over every rank's rows."""
+    import torch
+    import torch.distributed as dist
+    from aikit_b200 import synth
+    from aikit_b200.ann import unpack_keys
+    from aikit_b200.dist import ShardedBinary
+    r = synth.Recipe(synth.UNIT, C4["dim"], seed=C4["seed"])
+    n_rank, k, over, M = C4["rows_per_gpu"], C4["k"], C4["over"], C4_BATCH
+    cand = k * over
+    ctr = r.center(CHUNK)  # the prefilter's centre, the same on every rank
+    Q = r.queries(M, row0=4096)
+    sample = [0, M - 1]
+    check = BinaryCheck(Q[sample], ctr, C4["dim"], k, over)
+    lo = rank * n_rank
+    bix, build = build_binary(be, r, ctr, lo, lo + n_rank, over, check)
+    bix.set_tensor_prefilter(C4_TENSOR_MIN)
+    Qd = torch.from_numpy(Q).cuda()
+    sh = ShardedBinary(bix, be.ctx, world, stream)
+
+    def step(i):
+        sh.topk_async(Qd.data_ptr(), M, k)
+        return bix.last_launch_count() + 4  # + the two all-gathers and two merges
 
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
     bix.sync()
-
-    def timed(kernel_events):
-        bix.kernel_times(reset=True)
-        bix.set_kernel_timing(kernel_events)
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        n_launch = 0
-        for i in range(args.steps):
-            n_launch += step(i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        bix.set_kernel_timing(False)
-        return ev0.elapsed_time(ev1), n_launch, bix.kernel_times(reset=True)
-
-    with ClockSampler(local) as clk:
-        ms, launches, _ = timed(False)
-        ms_ev, _, kt = timed(True)
+    ms, launches, kt = timed(step, args.steps, stream, bix, False, world)
     bix.sync()
-    gidx, _ = unpack_keys(keys.cpu().numpy().view(np.uint64))
-    assert (gidx >= 0).all(), "binary batch top-K came back short"
-    # e2e: the host entry point (fi8_bin_query_topk) with a pinned batch
-    Qpin = torch.from_numpy(Qh.copy()).pin_memory().numpy()
-    bix.topk_arrays(Qpin[0], BIN_K)
-    t1 = time.perf_counter()
-    for i in range(args.steps):
-        bix.topk_arrays(Qpin[i % nb], BIN_K)
-    e2e_s = time.perf_counter() - t1
-    gemm = kt["gemm_kernel"]
-    gemm_ms = gemm["ms"] / args.steps
-    ops = 2.0 * M * BIN_ROWS * BIN_DIM  # every row once per step, over the ranges
-    achieved = ops / (gemm_ms / 1e3)
-    ncu = NCU_TRAFFIC["gemm_kernel_ham"]
-    step_bytes = BIN_ROWS * BIN_DIM + M * BIN_DIM
-    traffic = step_bytes * ncu["dram_bytes"] / ncu["algorithmic_bytes"]
-    return {
-        "metric": "FlatBinaryI8 top-K queries/sec, batch 512", "value": M * args.steps / (ms / 1e3),
-        "unit": "queries/s", "ms_per_step": ms / args.steps,
-        "dtype": "int8 +1/-1 sign rows (int32 accumulate) + int8 rerank",
-        "config": {"workload": f"C4 batch form: {M} queries per step, d={BIN_DIM}, K={BIN_K}, cand {cand}, "
-                               f"{BIN_ROWS:,} rows; prefilter batches of >= {BIN_TENSOR_MIN} on the tensor cores",
-                   "sign_rows_bytes": BIN_ROWS * BIN_DIM, "sign_rows_build_s": round(sign_s, 3)},
-        "roofline": {"bound": "tensor", "achieved": achieved / 1e12, "peak": peak_ops / 1e12, "unit": "TOPS",
-                     "frac": achieved / peak_ops, "traffic": traffic, "traffic_unit": "bytes per step",
-                     "traffic_source": f"ncu dram bytes/algorithmic bytes of one captured launch ({ncu['profile']}), "
-                                       "times this step's sign-row bytes",
-                     "kernel": "gemm_kernel (Hamming mode)",
-                     "launches": gemm["launches"], "ms_per_step": gemm_ms,
-                     "algorithmic_ops_per_step": ops,
-                     "hbm_view_gbs": BIN_ROWS * BIN_DIM / (gemm_ms / 1e3) / 1e9,
-                     "kernels": {k: {"launches": v["launches"], "ms": v["ms"]} for k, v in kt.items()},
-                     "peak_source": f"fi8_probe_tensor_i8 measured live ({probe_ms:.1f} ms of back-to-back "
-                                    "kind::i8 MMAs on all SMs); MEASURED_PEAKS.json has no int8 figure"},
-        "gpu_launches": launches,
-        "e2e": {"value": M * args.steps / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": M * BIN_DIM * 4,
-                "d2h_bytes_per_step": M * BIN_K * 8, "api": "fi8_bin_query_topk (include/fi8.h), pinned host batch"},
-        "clocks": clk.summary(),
-    }
+    # the global shortlist of the sampled queries (ShardedBinary's merged
+    # shortlist buffer) against the oracle's over all ranks' rows
+    merged_short = sh._buffers(M, cand, k)[2].cpu().numpy().view(np.uint64)[sample]
+    o = check.o
+    mine = []
+    for m, qc in enumerate(check.qc):
+        gids, bits, _, _ = check.keep[m]
+        d = o.hamming_rows(qc, bits).astype(np.int64)
+        mine.append(np.stack([d, gids.astype(np.int64)], axis=1))
+    S = len(sample)
+    pairs = torch.from_numpy(np.stack(mine)).cuda()            # [S, cand, 2] (distance, id)
+    allp = torch.empty((world, S, cand, 2), dtype=torch.int64, device="cuda")
+    dist.all_gather_into_tensor(allp.view(-1), pairs.reshape(-1))
+    allp = allp.cpu().numpy()
+    ok = True
+    for m in range(S):
+        u = allp[:, m].reshape(-1, 2)
+        u = u[np.lexsort((u[:, 1], u[:, 0]))][:cand]           # the cand nearest by (distance, id)
+        gi, gs = unpack_keys(merged_short[m])
+        ok &= gi.astype(np.int64).tolist() == u[:, 1].tolist()
+        ok &= (-gs).astype(np.int64).tolist() == u[:, 0].tolist()
+    bix.Close()
+    torch.cuda.empty_cache()
+    detail["c4_sharded"] = {"build": build, "kernels_rank0": kernel_summary(kt, args.steps) if kt else None}
+    return {"qps": round(M * args.steps / (ms / 1e3), 1), "ms": round(ms / args.steps, 3),
+            "rows": n_rank * world, "launches": launches,
+            "parity": ("exact" if ok else "MISMATCH") + " (global shortlist of 2 sampled queries vs the oracle)"}
 
 
-def binary_cpu_baseline(bits, ctr, Qh, r, budget_s: float = 6.0):
-    """The reference algorithm (oracle port of FlatBinaryI8.Query) on a row
-    sample of the same corpus, scaled linearly to the shard; the Hamming scan
-    splits over every host thread as the reference's binQueryWorkers does."""
-    import oracle
-    rows = 2_000_000
-    cores = os.cpu_count() or 1
-    q8, sc = r.codes(rows)  # the UNIT recipe's FlatI8 rows (same arithmetic as r.binary's)
-    oracle.flat_binary_i8_query(bits[:rows], ctr, q8, sc, BIN_OVER, Qh[0], BIN_K, nthreads=cores)  # warm
-    done, t0 = 0, time.perf_counter()
-    while done < len(Qh) and (done < 2 or time.perf_counter() - t0 < budget_s):
-        oracle.flat_binary_i8_query(bits[:rows], ctr, q8, sc, BIN_OVER, Qh[done], BIN_K, nthreads=cores)
-        done += 1
-    dt = time.perf_counter() - t0
-    per_query = dt / done * (BIN_ROWS / rows)
-    return {"value": 1.0 / per_query, "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"{done} FlatBinaryI8.Query calls (pack, prefilterHist with its worker split over "
-                      f"{cores} threads, rerank) over {rows:,} of {BIN_ROWS:,} rows, time scaled by "
-                      f"{BIN_ROWS / rows:g}x"}
+def _bin_subset(check, rows):
+    sub = BinaryCheck.__new__(BinaryCheck)
+    sub.o, sub.ctr, sub.dim, sub.k, sub.cand = check.o, check.ctr, check.dim, check.k, check.cand
+    sub.Q = [check.Q[i] for i in rows]
+    sub.qc = [check.qc[i] for i in rows]
+    sub.keep = [check.keep[i] for i in rows]
+    return sub
 
 
-def reference_arm(args, world):
-    """The reference's own CPU path (oracle port) on this host's cores."""
+# ----------------------------------------------------------------------------
+# the reference arm
+# ----------------------------------------------------------------------------
+REF_ROWS = 2_000_000  # the row sample one reference step scans
+
+
+def reference_arm(args, world, local):
+    """The reference's CPU path (the oracle port of FlatI8.Query, every host
+    thread) on the headline's config: its QueryBatch answers a batch one Query
+    at a time on the CPU (ann/backend.go:118-122), so one step is one Query
+    over a fixed 2M-row sample of the C3 corpus, timed as it runs, and the
+    rate is scaled to the full 50M rows (the scan is linear in rows). Also the
+    reference's own CUDA kernels on C2 (device_comparator)."""
     import oracle
     from aikit_b200 import synth
-    rows = 250_000
-    r = synth.Recipe(synth.MIXTURE, DIM, seed=SEED, ncl=NCL, sigma=SIGMA)
-    bq, bs = r.codes(rows)
-    Q = r.queries(BATCH)
+    r = synth.Recipe(synth.MIXTURE, C3["dim"], seed=C3["seed"], ncl=C3["ncl"], sigma=C3["sigma"])
+    bq, bs = r.codes(REF_ROWS)
+    Q = r.queries(64)
     threads = os.cpu_count() or 1
-    per_step_q = 4  # queries of the batch actually run per step (bounded sample)
 
     def step(i):
-        for j in range(per_step_q):
-            oracle.flat_i8_query(bq, bs, Q[(i * per_step_q + j) % BATCH], K, nthreads=threads)
+        oracle.flat_i8_query(bq, bs, Q[i % len(Q)], C3["k"], nthreads=threads)
 
     for i in range(args.warmup):
         step(i)
@@ -690,23 +869,103 @@ def reference_arm(args, world):
     for i in range(args.steps):
         step(i)
     dt = time.perf_counter() - t0
-    # full-corpus time per query, extrapolated linearly in rows
-    per_query = dt / (args.steps * per_step_q) * (N_ROWS / rows)
-    value = 1.0 / per_query
+    per_query_full = dt / args.steps * (C3["n"] / REF_ROWS)
+    value = 1.0 / per_query_full
     out = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_query * BATCH * 1e3,
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int8 (int32 accumulate, f32 epilogue)", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "n_rows": N_ROWS, "dim": DIM, "k": K, "batch": BATCH,
-                   "parallelism": "host threads"},
-        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": threads, "kind": "port",
-                         "sample": f"{per_step_q} FlatI8.Query calls per step over {rows:,} of "
-                                   f"{N_ROWS:,} rows, scaled linearly to the full corpus"},
-        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "dtype": "int8 (int32 accumulate, f32 epilogue)", "data": "synthetic (seeded C3 mixture recipe)",
+        "config": config(world),
+        "cpu_baseline": {"value": round(value, 4), "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": f"one FlatI8.Query per step over {REF_ROWS:,} of the {C3['n']:,} C3 rows "
+                                   f"(ms_per_step is that step as timed); value scales it by "
+                                   f"{C3['n'] // REF_ROWS}x to the whole corpus"},
+        "e2e": {"value": round(value, 4), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(out))
+    del bq, bs
+    try:
+        out["device_comparator"] = reference_kernels_c2(args, local)
+    except Exception as e:  # the comparator is context; the CPU arm stands alone
+        out["device_comparator"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    print(json.dumps(out, separators=(",", ":")))
     return 0
+
+
+def reference_kernels_c2(args, local) -> dict:
+    """The reference's own device path (gpu/anncuda/gemv_w8a8.cu kernels,
+    compiled for sm_100a, launched as gpu/anncuda/backend.go does) on C2 at
+    batch 1 and batch 64, K = 100: the scoring kernel writes the M x N score
+    matrix and the k > 64 selection runs topk_rows' k passes. Timed with CUDA
+    events over the kernels only (its host-side quantize and copies left out),
+    and checked against the oracle on query 0."""
+    import torch
+    import oracle
+    from oracle import ref_anncuda
+    from aikit_b200 import synth
+    from aikit_b200.ann import Context, unpack_keys  # noqa: F401
+    if not ref_anncuda.available():
+        return {"unavailable": "oracle/_ref/libref_anncuda.so not built"}
+    torch.cuda.set_device(local)
+    sm = Context(local).sm_count()
+    r = synth.Recipe(synth.MIXTURE, C2["dim"], seed=C2["seed"], ncl=C2["ncl"], sigma=C2["sigma"])
+    n, d, k = C2["n"], C2["dim"], C2["k"]
+    Q = r.queries(64)
+    check = FlatI8Check(Q[:1], k)
+    codes = torch.empty((n, d), dtype=torch.int8, device="cuda")
+    scales = torch.empty(n, dtype=torch.float32, device="cuda")
+    q = np.empty((CHUNK, d), np.int8)
+    s = np.empty(CHUNK, np.float32)
+    for r0 in range(0, n, CHUNK):
+        m = min(CHUNK, n - r0)
+        r.codes(m, row0=r0, out_q=q[:m], out_s=s[:m])
+        check.chunk(q[:m], s[:m], r0)
+        codes[r0:r0 + m].copy_(torch.from_numpy(q[:m]))
+        scales[r0:r0 + m].copy_(torch.from_numpy(s[:m]))
+    aq, as_ = oracle.quantize_queries(Q)
+    pk, _ = peaks()
+    out = {"what": "the reference's gpu/anncuda kernels (gemv_w8a8 / gemv_w8a8_batch16, then topk_rows for "
+                   "k > 64), built for sm_100a, on C2 (10M x 768, K=100)",
+           "timing": "CUDA events around its kernels only (host quantize and copies left out)"}
+    stream = torch.cuda.Stream()
+    st = stream.cuda_stream
+    wi, ws = check.best[0]
+    for M in (1, 64):
+        qi8 = torch.from_numpy(aq[:M].copy()).cuda()
+        qs = torch.from_numpy(as_[:M].copy()).cuda()
+        sc = torch.empty((M, n), dtype=torch.float32, device="cuda")
+        idx = torch.empty((M, k), dtype=torch.int32, device="cuda")
+        val = torch.empty((M, k), dtype=torch.float32, device="cuda")
+        plan = ref_anncuda.RefTopK(n, d, M, k, sm)
+        plan.score(codes.data_ptr(), scales.data_ptr(), qi8.data_ptr(), qs.data_ptr(), sc.data_ptr(), st)
+        plan.topk(sc.data_ptr(), idx.data_ptr(), val.data_ptr(), st)
+        torch.cuda.synchronize()
+        steps = 3
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        tot_s = tot_k = 0.0
+        for _ in range(steps):
+            e[0].record(stream)
+            plan.score(codes.data_ptr(), scales.data_ptr(), qi8.data_ptr(), qs.data_ptr(), sc.data_ptr(), st)
+            e[1].record(stream)
+            plan.topk(sc.data_ptr(), idx.data_ptr(), val.data_ptr(), st)
+            e[2].record(stream)
+            torch.cuda.synchronize()
+            tot_s += e[0].elapsed_time(e[1])
+            tot_k += e[1].elapsed_time(e[2])
+        gi, gv = idx[0].cpu().numpy(), val[0].cpu().numpy()
+        ok = gi.astype(np.int64).tolist() == list(wi) and gv.tobytes() == np.asarray(ws, np.float32).tobytes()
+        plan.close()
+        score_ms, topk_ms = tot_s / steps, tot_k / steps
+        planes = 1 if M == 1 else (M + 15) // 16  # corpus passes of the scoring kernel
+        moved = planes * n * (d + 4) + M * n * 4   # corpus reads + the score matrix written
+        out[f"b{M}"] = {"qps": round(M / ((score_ms + topk_ms) / 1e3), 1), "score_ms": round(score_ms, 3),
+                        "topk_ms": round(topk_ms, 3),
+                        "score_gbs": round(moved / (score_ms / 1e3) / 1e9, 1),
+                        "score_hbm_frac": round(moved / (score_ms / 1e3) / 1e9 / pk["hbm_gbs"], 3),
+                        "launches": plan.launches, "parity_vs_oracle": "exact" if ok else "MISMATCH"}
+        del sc, idx, val
+        torch.cuda.empty_cache()
+    return out
 
 
 if __name__ == "__main__":

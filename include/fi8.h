@@ -181,6 +181,13 @@ int fi8_topk_batch_async_keep(fi8_index* idx, const float* d_q, int32_t M, int32
  * with the next batch's GEMM leaves a few SMs free for the collective's
  * kernel; results are identical. */
 #define FI8_OPT_GEMM_CTAS 3
+/* FI8_OPT_GEMM_PAIR: 1 runs batches of more than 128 queries on pairs of
+ * CTAs (tcgen05 cta_group::2: 256-query x 256-row tiles, each SM loading 2/3
+ * of the operand bytes of a single-CTA tile); 0 (default) keeps one CTA per
+ * tile, which measured faster on B200: the epilogue, not the operand feed,
+ * bounds these batches, and a pair waits for the slower of two epilogues.
+ * Results are identical. No counterpart in the reference. */
+#define FI8_OPT_GEMM_PAIR 4
 int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
 
 /* Kernel classes reported by fi8_index_kernel_times. */

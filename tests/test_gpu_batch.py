@@ -258,3 +258,31 @@ def test_cpu_gpu_shard_split(backend, share):
         assert mi.tolist() == list(wi)
         assert np.asarray(ms, np.float32).tobytes() == np.asarray(ws, np.float32).tobytes()
     ix.Close()
+
+
+@pytest.mark.parametrize("n,d,M,k,ctas", [
+    (60000, 256, 129, 50, 0),     # one pair unit column: the odd CTA's tile holds one query
+    (50000, 1024, 300, 100, 0),   # two pairs, the second partial
+    (30000, 96, 1000, 20, 0),     # a zero-filled K tail, four pairs
+    (80000, 384, 520, 100, 6),    # three clusters walking many units
+    (40000, 512, 260, 64, 2),     # a single cluster
+])
+def test_cta_pair_equals_single_cta(backend, n, d, M, k, ctas):
+    """Batches above 128 queries run on CTA pairs (tcgen05 cta_group::2,
+    256-query x 256-row units, FI8_OPT_GEMM_PAIR): keys identical, byte for
+    byte, to the single-CTA GEMM and to the oracle on sampled queries."""
+    r = synth.Recipe(synth.MIXTURE, d, seed=n + M + d, ncl=60, sigma=0.3)
+    bq, bs = r.codes(n)
+    Q = r.queries(M)
+    ix = backend.NewI8Index(bq, bs, n, d)
+    if ctas:
+        ix.set_gemm_ctas(ctas)
+    ix.set_gemm_pair(True)
+    pair = ix.topk_arrays(Q, k)
+    ix.set_gemm_pair(False)
+    single = ix.topk_arrays(Q, k)
+    assert pair[0].tolist() == single[0].tolist() and pair[1].tobytes() == single[1].tobytes()
+    rows = [0, M // 2, M - 1]
+    widx, wsc = oracle_topk(bq, bs, Q[rows], k)
+    assert_same(pair[0][rows].astype(np.int64), pair[1][rows], widx, wsc, f"pair n={n} d={d} M={M}")
+    ix.Close()

@@ -315,3 +315,22 @@ def test_tensor_prefilter_async_overflow_is_exact(backend):
     gi, gs = unpack_keys(keys.cpu().numpy().view(np.uint64))
     assert_answers(gi, gs, *oracle_answers(codes, ctr, bq, bs, over, Q, k), "async overflow")
     bix.Close()
+
+
+def test_tensor_prefilter_cta_pair_equals_single(backend):
+    """The Hamming-mode GEMM on CTA pairs (batches above 128 queries) gives the
+    single-CTA shortlist keys byte for byte."""
+    d, n, k, over = 1024, 40000, 10, 100
+    r = synth.Recipe(synth.MIXTURE, d, seed=77, ncl=30, sigma=0.35)
+    v, ctr, codes, bq, bs = build(r, n)
+    bix = backend.NewBinaryI8Index(codes, codes.shape[1], ctr, bq, bs, n, d, over)
+    bix.set_tensor_prefilter(1)
+    bix.set_gemm_pair(True)
+    Q = r.queries(300)
+    pair = shortlist(bix, Q, k * over)
+    bix.set_gemm_pair(False)
+    single = shortlist(bix, Q, k * over)
+    assert pair.tobytes() == single.tobytes()
+    got = bix.topk_arrays(Q[:3], k)
+    assert_answers(got[0], got[1], *oracle_answers(codes, ctr, bq, bs, over, Q[:3], k), "pair")
+    bix.Close()

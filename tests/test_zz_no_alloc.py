@@ -64,3 +64,30 @@ def test_noalloc_rejects_k_beyond_limit(backend):
     with pytest.raises(Fi8Error, match="allocation-free limit"):
         ix.topk1_noalloc(q.data_ptr(), 257, keys.data_ptr())
     ix.Close()
+
+
+def test_noalloc_small_index_and_two_indexes_on_one_device(backend):
+    """A corpus of a few thousand rows (a scan grid of a handful of CTAs, far
+    below the SM count) and a second index on the same device, called one
+    after the other on one stream: both share the one array, and each answer
+    equals the allocating entry point's and the oracle's."""
+    import torch
+    stream = torch.cuda.Stream()
+    ra = synth.Recipe(synth.UNIT, 128, seed=41)
+    rb = synth.Recipe(synth.MIXTURE, 256, seed=42, ncl=20, sigma=0.3)
+    aq, as_ = ra.codes(3000)   # ~12 tiles: a few CTAs
+    bq, bs = rb.codes(90_000)
+    ia = backend.NewI8Index(aq, as_, 3000, 128)
+    ib = backend.NewI8Index(bq, bs, 90_000, 256)
+    Qa, Qb = ra.queries(2), rb.queries(2)
+    for m in range(2):
+        for ix, Q, codes, scales, k in ((ia, Qa, aq, as_, 64), (ib, Qb, bq, bs, 100)):
+            qd = torch.from_numpy(Q[m].copy()).cuda()
+            want = _device_keys(ix, qd, k, False, stream)
+            got = _device_keys(ix, qd, k, True, stream)
+            assert got.tobytes() == want.tobytes()
+            gi, gs = unpack_keys(got[None, :])
+            wi, ws = oracle_topk(codes, scales, Q[m:m + 1], k)
+            assert_same(gi.astype(np.int64), gs, wi, ws, "noalloc, two indexes")
+    ia.Close()
+    ib.Close()
