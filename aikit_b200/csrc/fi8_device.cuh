@@ -159,6 +159,7 @@ cudaError_t launch_pdl(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t sme
 // wall time (globaltimer), records an error and lets the kernel unwind.
 // ---------------------------------------------------------------------------
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kWaitSuspendNs = 20000;          // a sleeping test gives up after 20 us at most
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -196,6 +197,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+// try_wait with a suspend-time hint: the thread may sleep until the phase
+// completes (or the hint runs out) instead of returning at once, so a waiting
+// warp does not spin through issue slots the working warps of its SM need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
+// As mbar_wait_bounded, sleeping between tests (see mbar_try_wait_sleep).
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_sleep(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_sleep(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
 }
 
 // Returns false if the phase did not complete within kWaitLimitNs.

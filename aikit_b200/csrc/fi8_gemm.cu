@@ -28,6 +28,8 @@
 // Every TMA load here is a plain single-CTA load into this CTA's shared memory.
 #include <cuda.h>
 
+#include <cfloat>
+
 #include "fi8_device.cuh"
 #include "fi8_gemm.cuh"
 #include "fi8_select.cuh"
@@ -220,12 +222,13 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
-// The largest exact W8A8 score of a 16-column chunk: float32(dot) * qs *
-// rs, two rounded multiplies left to right per column (the reference's
-// order, linalg/quant.go:290-296), the pairs multiplied packed. NaN scores
-// are skipped (a NaN never passes the filter), so the chunk can hold a
-// passing score only if this max passes.
-__device__ __forceinline__ float chunk_max_w8a8(const uint32_t (&v)[kChunkCols], float qs, const float* scl) {
+// The exact W8A8 scores of a 16-column chunk, in place of its accumulators:
+// float32(dot) * qs * rs, two rounded multiplies left to right per column
+// (the reference's order, linalg/quant.go:290-296), the pairs multiplied
+// packed. Returns their largest, NaN skipped (a NaN never passes the filter),
+// so the chunk can hold a passing score only if this max passes. The plain
+// product equals the x86-semantics score whenever it is not NaN.
+__device__ __forceinline__ float chunk_scores_w8a8(uint32_t (&v)[kChunkCols], float qs, const float* scl) {
   const float2 q2 = make_float2(qs, qs);
   const float4* s4 = reinterpret_cast<const float4*>(scl);
   float m = -INFINITY;
@@ -237,6 +240,10 @@ __device__ __forceinline__ float chunk_max_w8a8(const uint32_t (&v)[kChunkCols],
         mul2_rn(make_float2(__int2float_rn((int32_t)v[4 * i4 + 2]), __int2float_rn((int32_t)v[4 * i4 + 3])), q2);
     const float2 s0 = mul2_rn(a0, make_float2(rs.x, rs.y));
     const float2 s1 = mul2_rn(a1, make_float2(rs.z, rs.w));
+    v[4 * i4] = __float_as_uint(s0.x);
+    v[4 * i4 + 1] = __float_as_uint(s0.y);
+    v[4 * i4 + 2] = __float_as_uint(s1.x);
+    v[4 * i4 + 3] = __float_as_uint(s1.y);
     m = max3f(m, max3f(s0.x, s0.y, s1.x), s1.y);
   }
   return m;
@@ -385,7 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int32_t row0 = (int32_t)(p.row_lo + w.rt * kGemmBN) + (PAIR ? (int32_t)rank * (kGemmBN / 2) : 0);
         for (int kc = 0; kc < p.kchunks; kc++, step++) {
           const int s = (int)(step % kStages);
-          if (step >= kStages && !mbar_wait_bounded(&s_empty[s], (uint32_t)(((step / kStages) - 1) & 1))) {
+          if (step >= kStages && !mbar_wait_bounded_sleep(&s_empty[s], (uint32_t)(((step / kStages) - 1) & 1))) {
             s_abort = 1;
             atomicOr(p.err, 1u);
             break;
@@ -410,7 +417,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // accumulator, which follows every MMA that read them.
       if (leader)
         for (int64_t j = (step > kStages ? step - kStages : 0); j < step; j++)
-          mbar_wait_bounded(&s_full[j % kStages], (uint32_t)((j / kStages) & 1));
+          mbar_wait_bounded_sleep(&s_full[j % kStages], (uint32_t)((j / kStages) & 1));
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
@@ -419,7 +426,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int64_t step = 0;
       for (int64_t u = 0; u < my_units && !s_abort; u++) {
         const int b = (int)(u & 1);
-        if (u >= 2 && !mbar_wait_bounded(&s_tempty[b], (uint32_t)(((u / 2) - 1) & 1))) {
+        if (u >= 2 && !mbar_wait_bounded_sleep(&s_tempty[b], (uint32_t)(((u / 2) - 1) & 1))) {
           s_abort = 1;
           atomicOr(p.err, 1u);
           break;
@@ -428,7 +435,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t d_tmem = tmem + (uint32_t)(b * kGemmBN);
         for (int kc = 0; kc < p.kchunks; kc++, step++) {
           const int s = (int)(step % kStages);
-          if (!mbar_wait_bounded(&s_full[s], (uint32_t)((step / kStages) & 1))) {
+          if (!mbar_wait_bounded_sleep(&s_full[s], (uint32_t)((step / kStages) & 1))) {
             s_abort = 1;
             atomicOr(p.err, 1u);
             break;
@@ -461,7 +468,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         umma_commit_pair_local(&s_done);
       else
         umma_commit(&s_done);
-      mbar_wait_bounded(&s_done, 0);
+      mbar_wait_bounded_sleep(&s_done, 0);
     }
   } else {
     // ------------------------------ epilogue ------------------------------
@@ -555,13 +562,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         cp_async8(my_scale + (b ^ 1) * 64 + 2 * lane, p.scales + nrow0 + cq * 64 + 2 * lane);
       }
       cp_async_commit();
-      if (!mbar_wait_bounded(&s_tfull[b], (uint32_t)((u / 2) & 1))) {
+      if (!mbar_wait_bounded_sleep(&s_tfull[b], (uint32_t)((u / 2) & 1))) {
         s_abort = 1;
         atomicOr(p.err, 1u);
         break;
       }
       tc_fence_after();
       const int64_t lim = p.row_hi - row0;  // valid columns of this tile
+      // W8A8: the largest row scale of each 16-column chunk (lane 8c holds
+      // chunk c's after the group reduction) and the lanes whose two scales
+      // are not finite and >= 0 (a chunk holding one gets no bound)
+      float cmax = 0.0f;
+      uint32_t cbad = 0u;
+      if (!HAM) {
+        const float2 s2 = reinterpret_cast<const float2*>(my_scale + b * 64)[lane];
+        const bool ok = s2.x >= 0.0f && s2.x <= FLT_MAX && s2.y >= 0.0f && s2.y <= FLT_MAX;
+        cmax = fmaxf(s2.x, s2.y);
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, off));
+        cbad = __ballot_sync(0xffffffffu, !ok);
+      }
 #pragma unroll 1
       for (int c = 0; c < 64 / kChunkCols; c++) {
         uint32_t v[kChunkCols];
@@ -573,20 +593,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // the exact scores (W8A8) or of the dots (Hamming) -- rejects it with
         // a few instructions per column. Only a chunk that passes builds the
         // exact per-column mask below.
+        int32_t mx = (int32_t)v[0];
+#pragma unroll
+        for (int i = 1; i < kChunkCols; i++) mx = max(mx, (int32_t)v[i]);
+        // (uniform over the warp: every lane takes part in the shuffle)
+        const float rs_max = HAM ? 0.0f : __shfl_sync(0xffffffffu, cmax, 8 * c);
+        const bool rs_ok = ((cbad >> (8 * c)) & 0xFFu) == 0u;
         bool any;
         if (HAM) {
-          int32_t mx = (int32_t)v[0];
-#pragma unroll
-          for (int i = 1; i < kChunkCols; i++) mx = max(mx, (int32_t)v[i]);
           any = mx >= hthr;
+        } else if (qs == 0.0f) {
+          any = 0.0f >= Tscore;  // an all-zero query scores exactly 0
         } else {
-          any = chunk_max_w8a8(v, qs, scl) >= Tscore;
-          if (qs == 0.0f) any = 0.0f >= Tscore;  // an all-zero query scores exactly 0
+          // A bound on the chunk's scores from its largest dot: with qs >= 0
+          // and every scale of the chunk in [0, rs_max], each score is at
+          // most RN(RN(mx * qs) * rs_max) when mx > 0, and at most 0 when
+          // mx <= 0 (rounding is monotone). Only a chunk whose bound passes
+          // gets its exact scores (in place of v), then their max is tested;
+          // a chunk with a scale outside that range goes straight to them.
+          const float bnd = mx > 0 ? __fmul_rn(__fmul_rn(__int2float_rn(mx), qs), rs_max) : 0.0f;
+          any = !rs_ok || bnd >= Tscore;
+          if (any && lane_valid) any = chunk_scores_w8a8(v, qs, scl) >= Tscore;
         }
         if (!any || !lane_valid || col0 >= lim) continue;
-        // branch-free pass: the plain product equals the exact (x86 NaN
-        // semantics) score whenever it is not NaN, and NaN never passes. The
-        // score replaces the accumulator in v for the append below.
+        // The chunk's exact mask (a chunk reaches here when any of its 32
+        // lanes' queries has a column above its threshold, so the whole warp
+        // runs this part far more often than one lane would need it).
         uint32_t mask = 0;
         if (HAM) {
           // Hamming mode: A and B hold +1/-1 per sign bit (0 past dim), so
@@ -598,19 +630,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int i = kChunkCols - 1; i >= 0; i--)
             mask = __funnelshift_l((uint32_t)(tm1 - (int32_t)v[i]), mask, 1);
         } else {
-          const float4* s4 = reinterpret_cast<const float4*>(scl);
 #pragma unroll
-          for (int i4 = 0; i4 < kChunkCols / 4; i4++) {
-            const float4 rs = s4[i4];
-            const float rsv[4] = {rs.x, rs.y, rs.z, rs.w};
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-              const int i = i4 * 4 + t;
-              const float sc = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), qs), rsv[t]);
-              v[i] = __float_as_uint(sc);
-              mask |= (sc >= Tscore ? 1u : 0u) << i;
-            }
-          }
+          for (int i = 0; i < kChunkCols; i++) mask |= (__uint_as_float(v[i]) >= Tscore ? 1u : 0u) << i;
         }
         constexpr uint32_t kAll = (1u << kChunkCols) - 1u;
         if (!HAM && qs == 0.0f) {  // an all-zero query scores exactly 0
