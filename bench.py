@@ -86,7 +86,7 @@ NCU_TRAFFIC = {
     "scan_c2": (3.088071e9 + 3.871744e6, 4_000_000 * (768 + 4) + 768 * 4, "profiles/scan_kernel_c2_batch1.md"),
     "scan_binary": (512.031744e6 + 10.409216e6, 4_000_000 * 128 + 128 + 2 * 4_000_000,
                     "profiles/scan_kernel_binary_c4.md"),
-    "gemm_c3": (763.026176e6 + 12.11648e6, 737_856 * 1028 + 4096 * 1024, "profiles/gemm_kernel_c3_batch4096.md"),
+    "gemm_c3": (763.78112e6 + 12.463104e6, 737_856 * 1028 + 4096 * 1024, "profiles/gemm_kernel_c3_batch4096.md"),
     "gemm_ham": (756.334080e6 + 11.297024e6, 737_856 * 1024 + 512 * 1024, "profiles/gemm_kernel_ham_c4_batch512.md"),
 }
 
