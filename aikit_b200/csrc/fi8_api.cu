@@ -689,6 +689,24 @@ static int32_t gemm_cap(int32_t M) {
 //    at k = 1000 from 2.73 to 2.37 ms (4M rows) and a batch of 1024 at
 //    k = 1000 from 4.04 to 3.67 ms, with batch 4096 at k = 100 unchanged.
 // All factors stay within a quarter of the per-query buffer.
+// CTAs of a batched GEMM launch (at most `ctas`). A CTA (or CTA pair) walks
+// units strided by the grid size, so unless the grid is a multiple of the
+// query tiles its query tile changes on every unit, and each change costs the
+// epilogue a flush of its staged candidates and a fresh set-up of the lanes'
+// per-query scale and threshold (about 90 instructions per warp). Where the
+// epilogue is the GEMM's bottleneck -- rows of at most 256 bytes, whose MMA is
+// short next to the epilogue of a 128 x 256 unit -- that is up to 17 % of a
+// unit, so the grid drops to the largest multiple of the query tiles when that
+// leaves at least 90 % of the CTAs (144 of 148 SMs at 8 query tiles). Longer
+// rows hide the set-up behind the MMA and keep every SM.
+static int32_t gemm_grid_ctas(int32_t ctas, int32_t wtiles, bool pair, int32_t kchunks) {
+  if (kchunks > 2 || wtiles <= 0) return ctas;
+  const int32_t walkers = pair ? ctas / 2 : ctas;
+  const int32_t fixed = walkers / wtiles * wtiles;
+  if (fixed == 0 || fixed == walkers || 10 * (int64_t)fixed < 9 * (int64_t)walkers) return ctas;
+  return pair ? 2 * fixed : fixed;
+}
+
 static void plan_ranges(int64_t n, int32_t M, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
   const int64_t room = std::max<int64_t>(4, cap / (4 * (int64_t)k));
   const bool fine = M > 64;
@@ -778,8 +796,10 @@ static int launch_topk_gemm(fi8_index* x, const GemmCorpus& corpus, const float*
     p.row_hi = ranges[i].row_hi;
     p.rtiles = (p.row_hi - p.row_lo + kGemmBN - 1) / kGemmBN;
     p.producer_waits = i == 0 ? 1 : 0;  // the first range follows the quantize kernel
-    const int64_t units = (int64_t)(pair ? p.qtiles / 2 : p.qtiles) * p.rtiles;
-    const int32_t ctas = x->gemm_ctas > 0 ? std::min(x->gemm_ctas, x->sm_count) : x->sm_count;
+    const int32_t wtiles = pair ? p.qtiles / 2 : p.qtiles;  // query tiles of the unit walk
+    const int64_t units = (int64_t)wtiles * p.rtiles;
+    const int32_t ctas = gemm_grid_ctas(x->gemm_ctas > 0 ? std::min(x->gemm_ctas, x->sm_count) : x->sm_count,
+                                        wtiles, pair, p.kchunks);
     // CTAs: one per SM, or pairs of them, no more than there are units
     const int32_t G = pair ? 2 * (int32_t)std::max<int64_t>(1, std::min<int64_t>({(int64_t)ctas / 2,
                                                                                    (int64_t)pair_clusters, units}))
