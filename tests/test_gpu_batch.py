@@ -103,13 +103,16 @@ def test_batch_at_the_top_k_limit(backend, M):
     ix.Close()
 
 
-@pytest.mark.parametrize("ctas", [1, 5, 7, 146])
+@pytest.mark.parametrize("ctas", [0, 1, 5, 7, 146])
 def test_gemm_grid_sizes(backend, ctas):
     """The answer does not depend on the GEMM's persistent grid (the multi-GPU
     path runs it on all SMs but two). With G CTAs, CTA c takes units c, c+G,
     ..., and a unit's query tile changes from one unit to the next unless G
     is a multiple of the tile count: here 3 tiles of a 300-query batch, the
-    last one holding 44 queries."""
+    last one holding 44 queries. Rows of 256 bytes take the launch's grid
+    rule: a cap of 146 (and the default, one CTA per SM) runs on the largest
+    multiple of 3 below it, so every CTA keeps one tile; caps of 5 and 7 are
+    too far from a multiple and keep the changing tiles."""
     r = synth.Recipe(synth.MIXTURE, 256, seed=ctas, ncl=30, sigma=0.3)
     n = 30_000
     bq, bs = r.codes(n)
