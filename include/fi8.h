@@ -176,16 +176,19 @@ int fi8_topk_batch_async_keep(fi8_index* idx, const float* d_q, int32_t M, int32
  * reference. */
 #define FI8_OPT_KERNEL_TIMING 2
 /* FI8_OPT_GEMM_CTAS: the batched GEMM's persistent grid uses at most this many
- * CTAs, one per SM (0, the default: every SM). No counterpart in the
- * reference. A multi-GPU caller that overlaps the NCCL all-gather of one batch
- * with the next batch's GEMM leaves a few SMs free for the collective's
- * kernel; results are identical. */
+ * CTAs, one per SM (0, the default: every SM). For rows of at most 256 bytes
+ * the launch may use fewer, down to the largest multiple of the batch's
+ * 128-query tiles when that keeps 90 % of the cap, so that each CTA stays on
+ * one query tile. No counterpart in the reference. A multi-GPU caller that
+ * overlaps the NCCL all-gather of one batch with the next batch's GEMM leaves
+ * a few SMs free for the collective's kernel; results are identical. */
 #define FI8_OPT_GEMM_CTAS 3
 /* FI8_OPT_GEMM_PAIR: 1 runs batches of more than 128 queries on pairs of
  * CTAs (tcgen05 cta_group::2: 256-query x 256-row tiles, each SM loading 2/3
  * of the operand bytes of a single-CTA tile); 0 (default) keeps one CTA per
- * tile, which measured faster on B200: the epilogue, not the operand feed,
- * bounds these batches, and a pair waits for the slower of two epilogues.
+ * tile, which measured faster on B200 (at the full C3 shape under the power
+ * cap, 154.5 against 194 ms of GEMM per batch of 4096): a pair waits for the
+ * slower of two epilogues, and it ran at a lower clock for the same power.
  * Results are identical. No counterpart in the reference. */
 #define FI8_OPT_GEMM_PAIR 4
 int fi8_index_set_option(fi8_index* idx, int option, int64_t value);
