@@ -28,6 +28,8 @@ def main() -> None:
     ap.add_argument("--over", type=int, default=100, help="binary mode: overquery (cand = k * over)")
     ap.add_argument("--tensor", type=int, default=0,
                     help="binary mode: prefilter batches of at least this many queries on the tensor cores")
+    ap.add_argument("--pair", type=int, default=0, help="1: batched GEMM on CTA pairs (FI8_OPT_GEMM_PAIR)")
+    ap.add_argument("--ctas", type=int, default=0, help="cap on the GEMM's CTAs (FI8_OPT_GEMM_CTAS; 0: every SM)")
     ap.add_argument("--trace", action="store_true",
                     help="also report per-kernel device time (torch.profiler / CUPTI) over the reps")
     a = ap.parse_args()
@@ -56,6 +58,8 @@ def main() -> None:
         r = synth.Recipe(synth.MIXTURE, a.dim, seed=20260, ncl=1000, sigma=0.3)
     bq, bs = r.codes(a.rows)
     ix = be.NewI8Index(bq, bs, a.rows, a.dim)
+    ix.set_gemm_pair(a.pair == 1)
+    ix.set_gemm_ctas(a.ctas)
     Q = torch.from_numpy(r.queries(a.batch)).cuda()
     keys = torch.zeros((a.batch, a.k), dtype=torch.int64, device="cuda")
     stream = torch.cuda.Stream()
