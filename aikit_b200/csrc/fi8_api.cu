@@ -673,22 +673,6 @@ static int32_t gemm_cap(int32_t M) {
   return std::min<int32_t>(cap, 65536);
 }
 
-// Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles. A range after
-// the first admits about k*F candidates per query; every range costs a GEMM
-// launch and a select.
-// The first range takes every row as a candidate: max(k, 4096) rows. Its
-// select is the most expensive one (a 4096-key union per query); a 16K-row
-// first range cost a row shard of 1.25M rows (C2 over 8 GPUs) 10 % more per
-// batch on B200, and 10M rows no less. Then two regimes:
-//  * batches of up to 64 queries stream the corpus at the HBM rate and the
-//    epilogue hides under the loads, so ranges are few: the growth factor is
-//    64 (16 while ranges are short);
-//  * larger batches are bound by the tensor pipe and the epilogue, where
-//    every candidate costs epilogue and select work, so ranges are finer: the
-//    growth factor is 8 (4 when k >= 512). On B200 this took a batch of 512
-//    at k = 1000 from 2.73 to 2.37 ms (4M rows) and a batch of 1024 at
-//    k = 1000 from 4.04 to 3.67 ms, with batch 4096 at k = 100 unchanged.
-// All factors stay within a quarter of the per-query buffer.
 // CTAs of a batched GEMM launch (at most `ctas`). A CTA (or CTA pair) walks
 // units strided by the grid size, so unless the grid is a multiple of the
 // query tiles its query tile changes on every unit, and each change costs the
@@ -707,10 +691,31 @@ static int32_t gemm_grid_ctas(int32_t ctas, int32_t wtiles, bool pair, int32_t k
   return pair ? 2 * fixed : fixed;
 }
 
+// Row ranges [0,s1), [s1, s1*F), ... rounded to 256-row tiles. A range after
+// the first admits about k*F candidates per query; every range costs a GEMM
+// launch and a select.
+// The first range takes every row as a candidate: max(k, 4096) rows. Its
+// select is the most expensive one (a 4096-key union per query); a 16K-row
+// first range cost a row shard of 1.25M rows (C2 over 8 GPUs) 10 % more per
+// batch on B200, and 10M rows no less. Then two regimes:
+//  * batches of up to 64 queries stream the corpus at the HBM rate and the
+//    epilogue hides under the loads, so ranges are few: the growth factor is
+//    64 (16 while ranges are short);
+//  * larger batches are bound by the tensor pipe and the epilogue, where
+//    every candidate costs epilogue and select work, so ranges are finer: the
+//    growth factor is 8 (2 when k >= 512). A range growing by F admits about
+//    k (F - 1) / ln F candidates per query per e-fold of rows, so at large k
+//    the finer growth saves more epilogue and select work than its extra
+//    launches cost. On B200 growth 4 (from 8) took a batch of 512 at k = 1000
+//    from 2.73 to 2.37 ms (4M rows) and a batch of 1024 at k = 1000 from 4.04
+//    to 3.67 ms, with batch 4096 at k = 100 unchanged; growth 2 then took the
+//    batch of 1024 at k = 1000 over 100M rows of d = 256 from 33.7-34.0 to
+//    32.0-32.4 ms and left the batch of 512 over 25M sign rows even.
+// All factors stay within a quarter of the per-query buffer.
 static void plan_ranges(int64_t n, int32_t M, int32_t k, int32_t cap, std::vector<GemmLevel>* out) {
   const int64_t room = std::max<int64_t>(4, cap / (4 * (int64_t)k));
   const bool fine = M > 64;
-  const int64_t F1 = std::min<int64_t>(fine ? (k >= 512 ? 4 : 8) : 16, room);
+  const int64_t F1 = std::min<int64_t>(fine ? (k >= 512 ? 2 : 8) : 16, room);
   const int64_t F2 = fine ? F1 : std::min<int64_t>(64, room);
   int64_t hi = std::max<int64_t>(k, 4096);
   hi = (hi + kGemmBN - 1) / kGemmBN * kGemmBN;

@@ -6,7 +6,7 @@ The plan's rules, restated here to pin them:
   * the first range takes max(k, 4096) rows (rounded up to 256-row tiles);
   * then each range ends at F times its start, rounded up to a 256-row tile;
     batches of up to 64 queries grow by 16 below 16K rows and 64 above, larger
-    batches by 8 (4 when k >= 512); every factor is capped by the per-query
+    batches by 8 (2 when k >= 512); every factor is capped by the per-query
     candidate buffer, room = cap / (4k) with cap = 8K..64K keys (256 MB of keys
     across the batch at most);
   * a short tail (under half the range before it) joins that range when the
@@ -42,7 +42,7 @@ def restated_plan(n, M, k):
     cap = min(pow2_ge(max(8192, min(65536, (1 << 25) // M))), 65536)
     room = max(4, cap // (4 * k))
     fine = M > 64
-    f1 = min((4 if k >= 512 else 8) if fine else 16, room)
+    f1 = min((2 if k >= 512 else 8) if fine else 16, room)
     f2 = f1 if fine else min(64, room)
     hi = -(-max(k, 4096) // 256) * 256
     lo, bounds = 0, [0]
@@ -61,8 +61,11 @@ def test_plans_of_the_profiled_launches():
     K = 1024
     # W8A8 batch 4096 at k = 100 over 1M rows: growth 8
     assert device_plan(1_000_000, 4096, 100) == [0, 4096, 32768, 262144, 1_000_000]
-    # the Hamming prefilter's batch 512 at cand = 1000 over 1M rows: growth 4
-    assert device_plan(1_000_000, 512, 1000) == [0, 4096, 16384, 65536, 262144, 1_000_000]
+    # the Hamming prefilter's batch 512 at cand = 1000 over 1M rows: growth 2
+    assert device_plan(1_000_000, 512, 1000) == [0, 4096, 8192, 16384, 32768, 65536, 131072, 262144, 524288,
+                                                  1_000_000]
+    # C5: batch 1024 at k = 1000 over 16M rows (the profiled shape)
+    assert device_plan(16_000_000, 1024, 1000) == [0] + [4096 << i for i in range(12)] + [16_000_000]
     # C2: batch 64 at k = 100 over 10M rows: growth 16, then 64
     assert device_plan(10_000_000, 64, 100) == [0, 4096, 65536, 4 * K * K, 10_000_000]
     # a row shard of C2 over 8 GPUs
@@ -91,7 +94,9 @@ def test_plan_properties(M, k):
         assert all(x < y for x, y in zip(b, b[1:]))
         assert all(x % 256 == 0 for x in b[1:-1])  # whole 256-row GEMM tiles
         assert b[1] == min(n, -(-max(k, 4096) // 256) * 256) or len(b) == 2
-        assert len(b) - 1 <= 12  # launches per batch stay few at any size
+        # launches per batch stay few at any size: growth 2 (k >= 512) reaches
+        # 2e9 rows in 20 ranges, the others in at most 12
+        assert len(b) - 1 <= (20 if k >= 512 and M > 64 else 12)
 
 
 def test_plan_rejects_bad_arguments():
