@@ -622,11 +622,15 @@ static int launch_topk_scan(fi8_index* x, const float* d_q, int32_t M, int32_t k
   int32_t G = grid_ctas(x, p);
   int32_t Mc = std::min(M, kScanMaxM);
   if (gate) {
-    // A gated launch costs its CTAs' start and exit even when closed, so the
-    // redo keeps each launch to about one wave: up to sm_count queries per
-    // launch, sm_count / queries CTAs each (at least one). When open it
-    // streams the corpus once per query all the same, on every SM.
-    Mc = std::min<int32_t>(M, std::max<int32_t>(kScanMaxM, x->sm_count));
+    // A closed gated launch costs its start plus a quick exit of each CTA, so
+    // the redo takes as many queries per launch as about 32 MB of per-query
+    // scratch allows (at least a wave's worth): one CTA per query, or
+    // sm_count / queries CTAs each when there are fewer queries than SMs.
+    // When open it streams the corpus once per query all the same. (One-wave
+    // launches cost a batch of 4096 queries 29 launches and 0.21 ms.)
+    const int64_t per_query = 2 * (int64_t)geo.kp * (int64_t)sizeof(uint64_t);  // lvl1 + lvl2 at G = 1
+    const int64_t fit = std::min<int64_t>(65535, std::max<int64_t>(x->sm_count, (32ll << 20) / per_query));
+    Mc = (int32_t)std::min<int64_t>(M, std::max<int64_t>(kScanMaxM, fit));
     G = std::max<int32_t>(1, std::min<int32_t>(G, x->sm_count / Mc));
   }
   int rc = ensure_topk_scratch(x, Mc, geo.kp, G, st);

@@ -798,9 +798,13 @@ __global__ void __launch_bounds__(256) sign_prep_kernel(const float* q, int M, i
 // the last range's select orders its keys (its output is the answer).
 // Threads and unrolled loads per CTA: a one-wave launch stages its union in
 // shared memory (one CTA per SM) and spreads it over 1024 threads; a larger
-// batch streams unions from L2 with several 512-thread CTAs per SM.
+// batch streams unions from L2 with eight 256-thread CTAs per SM (at least
+// 256 threads: one per radix bin). A union there is a few thousand keys, so
+// its passes are short and the launch's waves dominate: 256 threads x 4
+// loads halved the selects of a 4096-query batch against 512 x 8 (0.40 ms
+// against 0.79-0.83 per batch over 6.25M rows).
 constexpr int kSelThreadsStaged = 1024, kSelUnrollStaged = 4;
-constexpr int kSelThreads = 512, kSelUnroll = 8;
+constexpr int kSelThreads = 256, kSelUnroll = 4;
 constexpr int kRadixBins = 256;
 
 // Slot i of a query's union: its carried list, then this range's candidates.

@@ -154,14 +154,14 @@ def _against_query_order(r, n, d):
     return np.ascontiguousarray(bq[order]), np.ascontiguousarray(bs[order]), q
 
 
-@pytest.mark.parametrize("M", [2, 70])
+@pytest.mark.parametrize("M", [2, 70, 300])
 def test_async_overflow_is_exact(backend, M):
     """The device-resident form on the same corpus: the gated redo runs in
     stream order, so the keys are exact without a host round trip, the next
     sync reports no error, and ShardedTopK (the multi-GPU path, here one
-    rank) hands the exact keys on. Batches of 2 (a 64-query tile) and 70 (a
-    128-query tile); the redo's scan runs many queries per launch on few CTAs
-    each."""
+    rank) hands the exact keys on. Batches of 2 (a 64-query tile), 70 (a
+    128-query tile) and 300 (three tiles, and more queries than SMs: the
+    redo's one scan launch runs in several waves of one CTA per query)."""
     import torch
     from aikit_b200.ann import unpack_keys
     from aikit_b200.dist import ShardedTopK
@@ -190,7 +190,9 @@ def test_async_overflow_is_exact(backend, M):
     stream.synchronize()
     ix.set_kernel_timing(False)
     kt = ix.kernel_times()
-    chunk = max(64, backend.ctx.sm_count())  # queries per gated scan launch
+    # queries per gated scan launch: as many as ~32 MB of scratch allows
+    kp = 1 << (k - 1).bit_length()
+    chunk = min(65535, max(backend.ctx.sm_count(), (32 << 20) // (2 * kp * 8)))
     assert kt["redo_gated"]["launches"] == 1 + (M + chunk - 1) // chunk
     ix.Close()
 
