@@ -217,7 +217,8 @@ int fi8_index_kernel_log(fi8_index* idx, int32_t cap, int32_t* count, int32_t* k
 
 /* Number of kernels the index's last query call launched (scan: one per 64
  * queries; batched: quantize + a GEMM and a select per row range, then the
- * gated redo -- a latch and one scan per 64 queries, or the popcount
+ * gated redo -- a latch and one scan launch per up to 32 MB of its per-query
+ * scratch (one launch for a batch of 4096 at k = 100), or the popcount
  * prefilter's launches for a tensor-core shortlist -- which return at once
  * unless a candidate was dropped). */
 int fi8_index_last_launch_count(fi8_index* idx, int32_t* out);
