@@ -806,6 +806,8 @@ __global__ void __launch_bounds__(256) sign_prep_kernel(const float* q, int M, i
 constexpr int kSelThreadsStaged = 1024, kSelUnrollStaged = 4;
 constexpr int kSelThreads = 256, kSelUnroll = 4;
 constexpr int kRadixBins = 256;
+static_assert(kSelThreads >= kRadixBins && kSelThreadsStaged >= kRadixBins,
+              "the select clears its histogram with one thread per radix bin");
 
 // Slot i of a query's union: its carried list, then this range's candidates.
 __device__ __forceinline__ uint64_t union_key(const uint64_t* mine, int kp, const uint64_t* src, int n_all, int i) {
