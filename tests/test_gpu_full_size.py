@@ -1,4 +1,4 @@
-"""Parity at BASELINE.json's full sizes: the C3 headline and C5.
+"""Parity at BASELINE.json's full sizes: the C3 headline, C2 and C5.
 
 The other GPU tests check the device paths against the oracle at sizes the
 oracle finishes in a second or two. These run the configurations `bench.py`
@@ -11,7 +11,7 @@ run chunk by chunk as the corpus is generated. Selection decomposes, so the
 chunk answers merge exactly by queryBatchSharded's rule
 (ann/backend.go:262-277). The C3 test holds 51 GB on the device and takes
 about 25 s on a B200 (most of it generating the corpus); C5 holds 26 GB and
-takes about 6 s.
+takes about 6 s, C2 8 GB and a few seconds.
 """
 import os
 
@@ -80,4 +80,19 @@ def test_c5_full_size_batch_1024(backend):
     rows = [0, M - 1]
     ix, widx, wsc = _build_with_oracle(backend, r, n, d, Q[rows], k)
     _check_batch(ix, Q, k, widx, wsc, rows, "C5 full size, batch 1024")
+    ix.Close()
+
+
+def test_c2_full_size_batch_64_and_1(backend):
+    """C2: 10M rows of d = 768 (mixture of 1000 clusters, sigma 0.3), K = 100:
+    a batch of 64 on the HBM-bound GEMM path, and its first query alone on the
+    batch-1 scan, both against the oracle."""
+    n, d, k, M = 10_000_000, 768, 100, 64
+    r = synth.Recipe(synth.MIXTURE, d, seed=20260, ncl=1000, sigma=0.3)
+    Q = r.queries(M)
+    rows = [0, M - 1]
+    ix, widx, wsc = _build_with_oracle(backend, r, n, d, Q[rows], k)
+    _check_batch(ix, Q, k, widx, wsc, rows, "C2 full size, batch 64")
+    gidx, gsc = ix.topk_arrays(Q[:1], k)
+    assert_same(gidx.astype(np.int64), gsc, widx[:1], wsc[:1], "C2 full size, batch 1")
     ix.Close()
