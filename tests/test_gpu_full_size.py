@@ -1,4 +1,5 @@
-"""Parity at BASELINE.json's full sizes: the C3 headline, C2 and C5.
+"""Parity at BASELINE.json's full sizes: the C3 headline, C2, C5 and C4's
+per-GPU FlatBinaryI8 shard.
 
 The other GPU tests check the device paths against the oracle at sizes the
 oracle finishes in a second or two. These run the configurations `bench.py`
@@ -11,7 +12,8 @@ run chunk by chunk as the corpus is generated. Selection decomposes, so the
 chunk answers merge exactly by queryBatchSharded's rule
 (ann/backend.go:262-277). The C3 test holds 51 GB on the device and takes
 about 25 s on a B200 (most of it generating the corpus); C5 holds 26 GB and
-takes about 6 s, C2 8 GB and a few seconds.
+takes about 6 s, C2 8 GB and a few seconds, C4's shard about 55 GB (codes,
+int8 rows and the tensor prefilter's sign rows) and about 25 s.
 """
 import os
 
@@ -96,3 +98,49 @@ def test_c2_full_size_batch_64_and_1(backend):
     gidx, gsc = ix.topk_arrays(Q[:1], k)
     assert_same(gidx.astype(np.int64), gsc, widx[:1], wsc[:1], "C2 full size, batch 1")
     ix.Close()
+
+
+def test_c4_full_shard_batch_512_and_1(backend):
+    """C4's per-GPU shard: 25M rows of d = 1024 (unit recipe), K = 10,
+    overquery 100 (a 1000-row shortlist). A batch of 512 prefiltered on the
+    tensor cores and its first query alone on the popcount pass, both against
+    FlatBinaryI8.Query on the CPU. The oracle cuts each block's prefilterHist
+    shortlist together with the running one back to the cand nearest under
+    (distance, id), which is the global shortlist because the cut decomposes,
+    and reranks it at the end (flat_binary_i8.go:86-153)."""
+    n, d, k, over, M = 25_000_000, 1024, 10, 100, 512
+    cand = k * over
+    r = synth.Recipe(synth.UNIT, d, seed=20264)
+    ctr = r.center(CHUNK)  # the prefilter's centre: the mean of the first block
+    Q = r.queries(M)
+    rows = [0, M - 1]
+    qc = [oracle.pack_row(q, ctr) for q in Q[rows]]
+    keep = [None] * len(rows)  # per sampled query: (ids, codes, int8 rows, scales)
+    bix = backend.NewBinaryI8IndexEmpty(n, d, ctr, over)
+    for r0 in range(0, n, CHUNK):
+        m = min(CHUNK, n - r0)
+        bits, bq, bs = r.binary(m, ctr, row0=r0)
+        for j in range(len(rows)):
+            ids = oracle.prefilter_hist(qc[j], bits, d, cand)
+            part = (ids + r0, bits[ids], bq[ids], bs[ids])
+            if keep[j] is not None:
+                part = tuple(np.concatenate([a, b]) for a, b in zip(keep[j], part))
+                sel = oracle.prefilter_hist(qc[j], part[1], d, cand)  # ascending: ids stay in order
+                part = tuple(a[sel] for a in part)
+            keep[j] = part
+        bix.upload_rows(r0, bits, bq, bs)
+    bix.upload_finish()
+    widx = np.full((len(rows), k), -1, np.int64)
+    wsc = np.zeros((len(rows), k), np.float32)
+    for j, q in enumerate(Q[rows]):
+        gids, bits, bq, bs = keep[j]
+        # the shortlist is the whole candidate set: FlatI8's exact top-k over it
+        i, sc = oracle.flat_binary_i8_query(bits, ctr, bq, bs, cand, q, k)
+        widx[j, :len(i)] = gids[np.asarray(i, np.int64)]
+        wsc[j, :len(sc)] = np.asarray(sc, np.float32)
+    bix.set_tensor_prefilter(16)
+    gidx, gsc = bix.topk_arrays(Q, k)
+    assert_same(gidx[rows].astype(np.int64), gsc[rows], widx, wsc, "C4 shard, batch 512")
+    gidx, gsc = bix.topk_arrays(Q[:1], k)
+    assert_same(gidx.astype(np.int64), gsc, widx[:1], wsc[:1], "C4 shard, batch 1")
+    bix.Close()
