@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t lim = p.row_hi - row0;  // valid columns of this tile
+      const int lim = (int)min(p.row_hi - row0, (int64_t)kGemmBN);  // valid columns of this tile (32-bit compares)
       // W8A8: the largest row scale of each 16-column chunk (lane 8c holds
       // chunk c's after the group reduction) and the lanes whose two scales
       // are not finite and >= 0 (a chunk holding one gets no bound)
